@@ -1,0 +1,382 @@
+#!/usr/bin/env python
+"""Benchmark of the MMVQ hot path: the per-token quantized-GEMV chain of a decode model.
+
+A "step" is one token's pass over the chain: every distinct input quantised to Q8_1
+and every weight matrix multiplied once (the default workload, qwen3_8b: 253 GEMVs over
+4.51 GB of Q4_K/Q6_K weights plus 145 quantisations).  Weights are synthetic (seeded,
+drawn on the GPU in GGUF block layout with the workload's value distributions) and far
+larger than L2, so every step streams them from HBM.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl anvil|reference]
+
+One JSON line is printed by rank 0:
+  value        chain bytes / device time, whole job (GB/s): weights + Q8_1 reads + fp32
+               outputs, timed with CUDA events around K graph replays, max over ranks
+  e2e          the same metric through the public API with the step's fp32 inputs copied
+               host->device from pinned memory and the logits copied back, every step
+  roofline     the dominant kernel (Q4_K MMVQ): algorithmic bytes per launch / average
+               launch time measured here with CUDA events, against measured HBM copy bandwidth
+  cpu_baseline the CPU oracle (oracle/, all host threads) on a bounded sample of the same
+               workload (layer 0 of the chain), rank 0 at N=1 only
+With N > 1 (torchrun) each rank holds a row shard of every matrix and each GEMV's fp32
+output is all-gathered with NCCL (captured in the CUDA graph): strong scaling.
+--impl reference times the CPU oracle port on the same workload (rank 0 only).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _p in (ROOT / "kernel-anvil_b200", ROOT):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+METRIC = "Q4_K GEMV weight-stream GB/s (% of HBM peak); per-token GEMV-chain µs"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="qwen3_8b")
+    ap.add_argument("--impl", default="anvil", choices=["anvil", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def measured_peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi samples (200 ms) across the timed region: SM clocks and throttle reasons."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.out = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.out, stderr=subprocess.DEVNULL)
+        except FileNotFoundError:
+            self.proc = None
+        return self
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.out.flush()
+        rows = [ln.split(", ") for ln in Path(self.out.name).read_text().splitlines() if ln.strip()]
+        os.unlink(self.out.name)
+        sm, smax, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                smax = max(smax, float(r[2]))
+                for name, flag in zip(names, r[5:9]):
+                    if flag.strip().lower() == "active":
+                        reasons.add(name)
+            except (ValueError, IndexError):
+                continue
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------------------
+# CPU baseline / reference arm: the oracle on layer 0 of the workload
+# ---------------------------------------------------------------------------------------
+
+def cpu_sample(workload: str):
+    """Layer 0 (or the first 7 GEMVs) of the chain, generated on the host."""
+    from kernel_anvil.chains import get_chain
+    from kernel_anvil.quants import gemv_bytes, make_activation, make_weights
+
+    spec = get_chain(workload)
+    gemvs = [g for g in spec.gemvs if g.name.startswith("blk.0.")] or spec.gemvs[:7]
+    inputs = {}
+    for g in gemvs:
+        inputs.setdefault(g.input, g.K)
+    W = [make_weights(g.qt, g.nrows, g.K, seed=i) for i, g in enumerate(gemvs)]
+    x = {a: make_activation(k, seed=j) for j, (a, k) in enumerate(inputs.items())}
+    nbytes = sum(gemv_bytes(g.qt, g.nrows, g.K) for g in gemvs)
+    desc = f"{workload} layer 0: {len(gemvs)} GEMVs + {len(inputs)} quantisations, {nbytes/1e6:.1f} MB"
+    return gemvs, W, x, nbytes, desc
+
+
+def cpu_step(gemvs, W, x):
+    from oracle import oracle
+
+    xq = {a: oracle.quantize_q8_1(v) for a, v in x.items()}
+    for g, w in zip(gemvs, W):
+        oracle.mmvq(g.qt, w, xq[g.input], g.nrows, g.K)
+
+
+def cpu_baseline(workload: str, seconds: float) -> dict:
+    from oracle import oracle
+
+    gemvs, W, x, nbytes, desc = cpu_sample(workload)
+    cpu_step(gemvs, W, x)  # warm
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        cpu_step(gemvs, W, x)
+        reps += 1
+        dt = time.perf_counter() - t0
+        if dt >= seconds:
+            break
+    return {"value": round(nbytes * reps / dt / 1e9, 3), "unit": "GB/s", "cores": oracle.num_threads(),
+            "kind": "port", "sample": f"{desc}; {reps} passes in {dt:.1f} s"}
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import oracle
+
+    gemvs, W, x, nbytes, desc = cpu_sample(args.workload)
+    for _ in range(args.warmup):
+        cpu_step(gemvs, W, x)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_step(gemvs, W, x)
+    dt = time.perf_counter() - t0
+    value = nbytes * args.steps / dt / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "int8 dp4a / fp32", "data": "synthetic",
+        "config": {"workload": f"{args.workload} (CPU sample: layer 0)", "sample": desc},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": oracle.num_threads(),
+                         "kind": "port", "sample": desc},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------------------
+
+def time_graph(launch, stream, steps: int) -> float:
+    """Milliseconds per launch over `steps` launches, CUDA events on `stream`."""
+    import torch
+
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        launch()
+    e1.record(stream)
+    e1.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def dominant_kernel(dc, stream, steps: int, warmup: int) -> dict:
+    """Q4_K MMVQ launches of one chain step, replayed as their own PDL graph."""
+    import torch
+
+    from kernel_anvil.mmvq import Chain
+    from kernel_anvil.quants import gemv_bytes
+
+    ch = Chain()
+    nbytes, n = 0, 0
+    for gm, W, y, (r0, r1) in zip(dc.spec.gemvs, dc.weights, dc.outputs, dc.rows):
+        if gm.qt != "Q4_K":
+            continue
+        ch.add_mmvq(W, gm.qt, dc.xq[gm.input], y, nrows=r1 - r0, K=gm.K, ncols=dc.ncols)
+        nbytes += gemv_bytes(gm.qt, r1 - r0, gm.K, dc.ncols)
+        n += 1
+    with torch.cuda.stream(stream):
+        ch.instantiate(pdl=True)
+        for _ in range(warmup):
+            ch.launch()
+        ms = time_graph(ch.launch, stream, steps)
+    ch.close()
+    return {"launches_per_step": n, "bytes_per_launch": nbytes / n, "ms_per_launch": ms / n}
+
+
+def traffic_per_launch() -> float | None:
+    p = ROOT / "profiles" / "mmvq_q4k_qwen3_8b_traffic.json"
+    try:
+        return float(json.loads(p.read_text())["dram_bytes_per_launch"])
+    except Exception:
+        return None
+
+
+def run_anvil(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from kernel_anvil import mmvq as ops
+    from kernel_anvil.chains import DeviceChain, get_chain
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
+
+    spec = get_chain(args.workload)
+    dc = DeviceChain(spec, rank=rank, world=world, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    hbm_peak, peak_kind = measured_peaks()
+    total_bytes = spec.algorithmic_bytes()  # whole job: all shards together
+
+    graph = None
+    if world == 1:
+        with torch.cuda.stream(stream):
+            dc.instantiate(pdl=True)
+        launch = dc.launch
+        launches_per_step = dc.chain.n_mmvq + dc.chain.n_quantize
+    else:
+        from kernel_anvil.sharded import ShardedStep
+        step = ShardedStep(dc, dist)
+        with torch.cuda.stream(stream):
+            step.eager()  # warms NCCL before capture
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                step.eager()
+        launch = graph.replay
+        launches_per_step = dc.chain.n_mmvq + dc.chain.n_quantize
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # ---- device-timed chain -------------------------------------------------------------
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3)):
+            launch()
+    stream.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local).start()
+    with torch.cuda.stream(stream):
+        ms = time_graph(launch, stream, args.steps)
+    clk = clocks.stop()
+    torch.cuda.synchronize()
+    barrier()
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = total_bytes / (ms * 1e-3) / 1e9
+
+    # ---- end to end: host inputs in, logits out, every step --------------------------------
+    h_in = torch.empty(dc.x_all.numel(), dtype=torch.float32, pin_memory=True)
+    h_in.copy_(dc.x_all.cpu())
+    logits = dc.outputs[-1]
+    h_out = torch.empty(logits.numel(), dtype=torch.float32, pin_memory=True)
+
+    def e2e_step():
+        dc.x_all.copy_(h_in, non_blocking=True)
+        launch()
+        h_out.copy_(logits.view(-1), non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            e2e_step()
+    stream.synchronize()
+    barrier()
+    with torch.cuda.stream(stream):
+        ms_e2e = time_graph(e2e_step, stream, args.steps)
+    barrier()
+    if world > 1:
+        t = torch.tensor([ms_e2e], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_e2e = float(t.item())
+    e2e = {"value": round(total_bytes / (ms_e2e * 1e-3) / 1e9, 2), "unit": "GB/s",
+           "h2d_bytes_per_step": h_in.numel() * 4, "d2h_bytes_per_step": h_out.numel() * 4,
+           "ms_per_step": round(ms_e2e, 4)}
+
+    # ---- dominant kernel roofline -----------------------------------------------------------
+    dk = dominant_kernel(dc, stream, args.steps, args.warmup)
+    achieved = dk["bytes_per_launch"] / (dk["ms_per_launch"] * 1e-3) / 1e9
+    traffic = traffic_per_launch()
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
+                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                else "fallback 6.65 TB/s",
+                "kernel": "mmvq_kernel<Q4_K, ncols=1> (all Q4_K GEMVs of one step, PDL graph)",
+                "launches_per_step": dk["launches_per_step"],
+                "bytes_per_launch": round(dk["bytes_per_launch"]),
+                "us_per_launch": round(dk["ms_per_launch"] * 1e3, 3)}
+
+    status = ops.take_device_status()
+    if graph is not None:
+        del graph
+    dc.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "int8 dp4a / fp32", "data": "synthetic",
+        "config": {"workload": f"{args.workload} per-token GEMV chain",
+                   "gemvs_per_step": len(spec.gemvs), "quantizations_per_step": dc.chain.n_quantize,
+                   "bytes_per_step": total_bytes, "weight_bytes": spec.weight_bytes(),
+                   "us_per_token": round(ms * 1e3, 1), "pct_of_hbm_peak": round(100 * value / hbm_peak, 1),
+                   "pct_of_8TBps": round(100 * value / 8000.0, 1),
+                   "l2": "inputs larger than L2 (weights stream from HBM every step)",
+                   "parallelism": f"row-shard x{world} + NCCL all-gather" if world > 1 else "single GPU",
+                   "graph": "CUDA graph, programmatic dependent launch between kernels"},
+        "e2e": e2e, "roofline": roofline, "gpu_launches": launches_per_step * args.steps,
+        "device_status": status,
+    }
+    if clk is not None:
+        line["clocks"] = clk
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(args.workload, args.cpu_seconds)
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_anvil(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,196 @@
+/*
+ * anvil.h -- C ABI of libanvil.so, the B200 (sm_100a) MMVQ quantized GEMV library.
+ *
+ * libanvil.so replaces two things the reference (apollosenvy/kernel-anvil) drives:
+ *
+ *   1. llama.cpp's MMVQ device path: `quantize_q8_1` followed by
+ *      `mul_mat_vec_q<type, ncols_dst>` (reached from
+ *      `mul_mat_vec_q_switch_ncols_dst`, patched by patches/mmvq-smithy.patch:28-34;
+ *      the reference's own kernel ABI is the generated
+ *      `mmvq_<qt>_n<N>_k<K>_w<nw>_r<rpb>(weights, input_q8, output, stride_row)`,
+ *      kernel_anvil/hip_codegen.py:244-251, 408-415, launched with grid
+ *      (ceil(N/rpb)) and block (32, nwarps), kernel_anvil/autoforge.py:137-141).
+ *   2. The smithy runtime config loader, patches/smithy-config.h:30-331
+ *      (`smithy_get_bucket`, `smithy_set_model`, `smithy_load_configs`,
+ *      `smithy_try_load`, `smithy_lookup`).
+ *
+ * Conventions shared by every entry point:
+ *   - Return value: 0 (ANVIL_OK) on success, a negative anvil_status on failure.
+ *     `anvil_last_error()` returns a message for the calling thread's last failure.
+ *   - Device pointers are caller-owned.  Kernels write only their output buffers.
+ *     Nothing in the launch path allocates device memory.
+ *   - Every launch is asynchronous on the given stream (NULL = legacy default stream).
+ *   - Weight matrices are raw GGUF blocks, row-major: row r of a matrix with K columns
+ *     starts at byte r * (K / qk) * block_bytes.  Activation columns are contiguous:
+ *     column c of a K-long input starts at element c * K (fp32) or at byte
+ *     c * (K / 32) * 36 (Q8_1).  Output column c starts at element c * nrows.
+ *   - ggml type ids follow ggml.h (kernel_anvil/codegen.py:22-31):
+ *     Q8_0 = 8, Q4_K = 12, Q5_K = 13, Q6_K = 14.
+ *   - Thread-safe: the smithy table is guarded by a reader/writer lock; the launch
+ *     entry points keep no mutable shared state besides one-time function attributes.
+ */
+#ifndef ANVIL_H
+#define ANVIL_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same type as cudaStream_t / CUstream, declared without the CUDA headers. */
+typedef struct CUstream_st *anvil_stream_t;
+
+#define ANVIL_ABI_VERSION 1
+
+enum anvil_status {
+    ANVIL_OK = 0,
+    ANVIL_ERR_INVALID = -1,     /* bad argument: sizes, type, null pointer      */
+    ANVIL_ERR_UNSUPPORTED = -2, /* valid request this build does not implement   */
+    ANVIL_ERR_CUDA = -3,        /* a CUDA runtime call failed                    */
+    ANVIL_ERR_ALIGN = -4,       /* a pointer is not aligned as required          */
+    ANVIL_ERR_TIMEOUT = -5      /* a bounded device-side wait gave up            */
+};
+
+enum anvil_ggml_type {
+    ANVIL_TYPE_Q8_0 = 8,
+    ANVIL_TYPE_Q8_1 = 9,
+    ANVIL_TYPE_Q4_K = 12,
+    ANVIL_TYPE_Q5_K = 13,
+    ANVIL_TYPE_Q6_K = 14
+};
+
+/* Launch flags for anvil_mmvq_ex / anvil_quantize_q8_1_ex. */
+enum anvil_flags {
+    /* Launch with programmatic dependent launch.  The kernel starts streaming its
+     * weight tile before it waits for the preceding kernel in the stream, so the
+     * weights must not be written by that kernel (true for model weights).
+     * Activations and outputs are only touched after the wait. */
+    ANVIL_FLAG_PDL = 1u << 0
+};
+
+/* ---- library ------------------------------------------------------------ */
+
+int anvil_abi_version(void);
+const char *anvil_last_error(void);
+
+/* GGUF block geometry of a ggml type: values per block (qk) and bytes per block.
+ * Mirrors QUANT_TYPES qk/block_size, kernel_anvil/hip_codegen.py:75-102. */
+int anvil_type_geometry(int ggml_type, int *qk, int *block_bytes);
+
+/* Bytes of one weight row of K columns, or a negative status. */
+int64_t anvil_row_bytes(int ggml_type, int K);
+
+/* ---- Q8_1 activation quantiser ------------------------------------------ */
+
+/* Replaces llama.cpp `quantize_q8_1` (layout kernel_anvil/hip_codegen.py:392-396,
+ * 36-byte block kernel_anvil/hip_codegen.py:101-102).
+ * x: ncols columns of K fp32 values.  xq: ncols * (K/32) blocks of
+ * {half d, half s, int8 qs[32]}.  Per 32-value block: d = max|x| / 127 (fp32),
+ * qs = roundf(x / d) (0 when max|x| == 0), stored d = fp16(d), s = fp16(sum x)
+ * with the sum taken in xor-butterfly order (offsets 16, 8, 4, 2, 1).
+ * K % 32 == 0, x 4-byte aligned, xq 4-byte aligned. */
+int anvil_quantize_q8_1(const float *x, void *xq, int K, int ncols, anvil_stream_t stream);
+int anvil_quantize_q8_1_ex(const float *x, void *xq, int K, int ncols, unsigned flags,
+                           anvil_stream_t stream);
+
+/* ---- MMVQ quantized GEMV -------------------------------------------------- */
+
+/* y[c][r] = sum_k W[r][k] * xq[c][k] for r < nrows, c < ncols_dst.
+ * Replaces llama.cpp `mul_mat_vec_q<type, ncols_dst>` as launched by
+ * `mul_mat_vec_q_switch_ncols_dst` (docs/llama-cpp-kernel-analysis.md:16-24, 128-148)
+ * and the reference's generated kernels (kernel_anvil/hip_codegen.py:179-334).
+ * ncols_x is K (the weight row length); ncols_dst is 1..8 activation columns.
+ * nwarps (warps per CTA, 1..32) and rows_per_block (rows per CTA) keep their smithy
+ * meaning; 0 selects the smithy table entry for (type, nrows, ncols_x), else the
+ * built-in default.  rows_per_block is rounded down to 1, 2, 4 or 8 and reduced
+ * further when the tile would not fit in shared memory.
+ * Requirements: K % qk == 0; W 16-byte aligned; xq 4-byte aligned; y 4-byte aligned. */
+int anvil_mmvq(int ggml_type, const void *W, const void *xq, float *y, int nrows, int ncols_x,
+               int ncols_dst, int nwarps, int rows_per_block, anvil_stream_t stream);
+int anvil_mmvq_ex(int ggml_type, const void *W, const void *xq, float *y, int nrows,
+                  int ncols_x, int ncols_dst, int nwarps, int rows_per_block, unsigned flags,
+                  anvil_stream_t stream);
+
+/* Fused: quantize fp32 x to Q8_1 into the caller's xq scratch, then run anvil_mmvq.
+ * Same contract as calling anvil_quantize_q8_1 then anvil_mmvq on one stream. */
+int anvil_mmvq_f32(int ggml_type, const void *W, const float *x, void *xq, float *y, int nrows,
+                   int ncols_x, int ncols_dst, int nwarps, int rows_per_block,
+                   anvil_stream_t stream);
+
+/* Reads and clears the device status words of the current device: the OR of
+ * anvil_device_status flags set by kernels whose bounded waits gave up (0 = none),
+ * or a negative anvil_status.  Synchronous. */
+enum anvil_device_status { ANVIL_DEVICE_MBAR_TIMEOUT = 1 };
+int anvil_take_device_status(void);
+
+/* Parity probe: runs the production MMVQ kernel with its integer block sums written
+ * out instead of y.  sums[(c * nrows + r) * nsub + s] is the exact int32 dot of
+ * sub-block s of row r with column c, where a sub-block is 32 weights (one Q8_1
+ * block) for Q4_K, Q5_K and Q8_0, and 16 weights (one int8 scale group) for Q6_K,
+ * so nsub = K/32 or K/16.  For Q4_K/Q5_K the weight operand is the unsigned 4/5-bit
+ * quant (the min term is separate); for Q6_K it is q - 32; for Q8_0 the int8 quant. */
+int anvil_mmvq_block_sums(int ggml_type, const void *W, const void *xq, int32_t *sums,
+                          int nrows, int ncols_x, int ncols_dst, int nwarps, int rows_per_block,
+                          anvil_stream_t stream);
+
+/* Launch geometry that anvil_mmvq would use: resolved nwarps, rows_per_block,
+ * grid size and dynamic shared memory bytes. */
+int anvil_mmvq_plan(int ggml_type, int nrows, int ncols_x, int ncols_dst, int nwarps,
+                    int rows_per_block, int *out_nwarps, int *out_rpb, int *out_grid,
+                    int *out_smem_bytes);
+
+/* ---- GEMV chain executor (native CUDA-graph runtime) ---------------------- */
+
+/* A chain is an ordered list of quantize / MMVQ steps on fixed device buffers,
+ * captured once into a CUDA graph (with programmatic dependent launch between
+ * steps) and replayed per token.  It stands in for llama.cpp's per-token sequence
+ * of quantize_q8_1 + mul_mat_vec_q launches (docs/decode-pipeline-breakdown.md:20-21). */
+typedef struct anvil_chain anvil_chain;
+
+anvil_chain *anvil_chain_create(void);
+void anvil_chain_destroy(anvil_chain *chain);
+int anvil_chain_add_quantize(anvil_chain *chain, const float *x, void *xq, int K, int ncols);
+int anvil_chain_add_mmvq(anvil_chain *chain, int ggml_type, const void *W, const void *xq,
+                         float *y, int nrows, int ncols_x, int ncols_dst, int nwarps,
+                         int rows_per_block);
+/* use_pdl: launch every step after the first with ANVIL_FLAG_PDL. */
+int anvil_chain_instantiate(anvil_chain *chain, int use_pdl, anvil_stream_t stream);
+/* Replays the graph (or, before instantiation, launches the steps one by one). */
+int anvil_chain_launch(anvil_chain *chain, anvil_stream_t stream);
+int anvil_chain_num_steps(const anvil_chain *chain);
+
+/* ---- smithy runtime config (replaces patches/smithy-config.h) ------------ */
+
+/* patches/smithy-config.h:44-50: <=128 -> 0, <=1024 -> 1, <=4096 -> 2, <=16384 -> 3, else 4. */
+int anvil_smithy_bucket(int dim);
+
+/* patches/smithy-config.h:70-87: remember the model path (its stem selects
+ * ~/.cache/smithy/<stem>.json), clear the table and the load flags. */
+void anvil_smithy_set_model(const char *path);
+
+/* patches/smithy-config.h:89-266: parse one JSON file into the table.  Returns the
+ * number of cells loaded (> 0 means the table is now active), 0 when the file
+ * parsed but held no valid cell, or a negative status when unreadable / over 1 MiB. */
+int anvil_smithy_load(const char *path);
+
+/* patches/smithy-config.h:268-317: lazy load, first success wins:
+ * $SMITHY_CONFIG, then $HOME/.cache/smithy/<stem>.json (stem from
+ * anvil_smithy_set_model or $SMITHY_MODEL), then $HOME/.cache/smithy/default.json.
+ * Returns 1 when a table is active afterwards, else 0. */
+int anvil_smithy_try_load(void);
+
+/* patches/smithy-config.h:319-331: {nwarps, rows_per_block} for
+ * [type][bucket(nrows)][bucket(ncols)]; {0, 0} means "no override".
+ * Triggers the lazy load.  Returns 1 when an override was found, else 0. */
+int anvil_smithy_lookup(int ggml_type, int nrows, int ncols, int *nwarps, int *rows_per_block);
+
+/* Clears the table, the model path and the load flags (test helper). */
+void anvil_smithy_reset(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ANVIL_H */

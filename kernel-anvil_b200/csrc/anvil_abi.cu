@@ -1,0 +1,533 @@
+// anvil_abi.cu -- extern "C" entry points of libanvil.so (declared in include/anvil.h):
+// argument checks, launch planning, the Q8_1 quantiser kernel, programmatic dependent
+// launch, and the CUDA-graph chain executor.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "anvil.h"
+#include "mmvq.cuh"
+
+namespace anvil {
+
+// ---------------------------------------------------------------------------------
+// Q8_1 quantiser.  One warp per 32-value block, one lane per value, the semantics of
+// llama.cpp's CUDA quantize_q8_1: amax and sum by xor-butterfly warp reductions,
+// d = amax / 127, q = roundf(x / d) (0 when amax == 0), block = {half(d), half(sum), q}.
+// IEEE division (no fast-math), round-half-away-from-zero, fp16 round-to-nearest-even.
+// ---------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256)
+    quantize_q8_1_kernel(const float *__restrict__ x, uint8_t *__restrict__ xq, int nblocks) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (gw >= nblocks) return;  // uniform per warp
+    const float xi = x[size_t(gw) * 32 + lane];
+    const float amax = warp_max(fabsf(xi));
+    const float sum = warp_sum(xi);
+    const float d = __fdiv_rn(amax, 127.0f);
+    const int q = amax == 0.0f ? 0 : int(roundf(__fdiv_rn(xi, d)));
+    // Pack four quants per lane group and store words (blocks are 4-byte aligned).
+    const uint32_t b = uint32_t(q) & 0xFFu;
+    const uint32_t b1 = __shfl_down_sync(0xffffffffu, b, 1);
+    const uint32_t b2 = __shfl_down_sync(0xffffffffu, b, 2);
+    const uint32_t b3 = __shfl_down_sync(0xffffffffu, b, 3);
+    uint32_t *blk = reinterpret_cast<uint32_t *>(xq + size_t(gw) * kQ8_1Bytes);
+    if ((lane & 3) == 0) blk[1 + (lane >> 2)] = b | (b1 << 8) | (b2 << 16) | (b3 << 24);
+    if (lane == 0) {
+        const uint32_t hd = __half_as_ushort(__float2half_rn(d));
+        const uint32_t hs = __half_as_ushort(__float2half_rn(sum));
+        blk[0] = hd | (hs << 16);
+    }
+}
+
+static int take_quantize_status() {
+    int v = 0, z = 0;
+    if (cudaMemcpyFromSymbol(&v, g_anvil_device_status, sizeof(int)) != cudaSuccess) return -1;
+    if (cudaMemcpyToSymbol(g_anvil_device_status, &z, sizeof(int)) != cudaSuccess) return -1;
+    return v;
+}
+
+// ---------------------------------------------------------------------------------
+// Errors
+// ---------------------------------------------------------------------------------
+static thread_local std::string t_last_error;
+
+static int fail(int status, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    t_last_error = buf;
+    return status;
+}
+
+static int cuda_fail(cudaError_t e, const char *what) {
+    return fail(ANVIL_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+// ---------------------------------------------------------------------------------
+// Per-device state: SM count, one-time function attributes, occupancy cache.
+// ---------------------------------------------------------------------------------
+constexpr int kMaxDevices = 64;
+
+struct DeviceInfo {
+    std::atomic<int> sm_count{0};
+};
+static DeviceInfo g_dev[kMaxDevices];
+
+static std::mutex g_cache_mu;
+struct FnKey {
+    const void *fn;
+    int dev, threads, smem;
+    bool operator==(const FnKey &o) const {
+        return fn == o.fn && dev == o.dev && threads == o.threads && smem == o.smem;
+    }
+};
+struct FnKeyHash {
+    size_t operator()(const FnKey &k) const {
+        return std::hash<const void *>()(k.fn) ^ (size_t(k.dev) << 48) ^ (size_t(k.threads) << 32) ^
+               size_t(k.smem);
+    }
+};
+static std::unordered_map<FnKey, int, FnKeyHash> g_occ_cache;
+static std::unordered_map<uint64_t, bool> g_attr_set;  // (fn, dev) -> max smem attribute set
+
+static int current_device(int *dev) {
+    cudaError_t e = cudaGetDevice(dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (*dev < 0 || *dev >= kMaxDevices) return fail(ANVIL_ERR_UNSUPPORTED, "device %d", *dev);
+    return ANVIL_OK;
+}
+
+static int sm_count(int dev, int *out) {
+    int n = g_dev[dev].sm_count.load(std::memory_order_relaxed);
+    if (n == 0) {
+        cudaError_t e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(SM count)");
+        g_dev[dev].sm_count.store(n, std::memory_order_relaxed);
+    }
+    *out = n;
+    return ANVIL_OK;
+}
+
+// Lets `fn` use up to kMaxSmem of dynamic shared memory (once per device) and returns
+// how many CTAs of `threads` x `smem` fit on one SM.
+static int prepare_fn(const void *fn, int dev, int threads, int smem, int *occ) {
+    std::lock_guard<std::mutex> lk(g_cache_mu);
+    const uint64_t akey = reinterpret_cast<uint64_t>(fn) * 131u + uint64_t(dev);
+    if (!g_attr_set.count(akey)) {
+        cudaError_t e =
+            cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+        g_attr_set[akey] = true;
+    }
+    FnKey k{fn, dev, threads, smem};
+    auto it = g_occ_cache.find(k);
+    if (it != g_occ_cache.end()) {
+        *occ = it->second;
+        return ANVIL_OK;
+    }
+    int n = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, threads, smem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+    if (n < 1) return fail(ANVIL_ERR_UNSUPPORTED, "kernel does not fit on an SM (%d B smem)", smem);
+    g_occ_cache[k] = n;
+    *occ = n;
+    return ANVIL_OK;
+}
+
+// ---------------------------------------------------------------------------------
+// Geometry and launch planning
+// ---------------------------------------------------------------------------------
+static bool supported_type(int t) {
+    return t == kTypeQ4_K || t == kTypeQ5_K || t == kTypeQ6_K || t == kTypeQ8_0;
+}
+
+static MmvqKernelFn kernel_for(int t, int ncols, int rpb, bool sums) {
+    switch (t) {
+    case kTypeQ4_K: return mmvq_kernel_q4k(ncols, rpb, sums);
+    case kTypeQ5_K: return mmvq_kernel_q5k(ncols, rpb, sums);
+    case kTypeQ6_K: return mmvq_kernel_q6k(ncols, rpb, sums);
+    case kTypeQ8_0: return mmvq_kernel_q80(ncols, rpb, sums);
+    default: return nullptr;
+    }
+}
+
+// Built-in B200 default when neither the caller nor the smithy table chose.
+static void default_config(int t, int nrows, int K, int ncols, int *nw, int *rpb) {
+    (void)t;
+    (void)nrows;
+    (void)K;
+    (void)ncols;
+    *nw = 4;
+    *rpb = 2;
+}
+
+struct Plan {
+    MmvqKernelFn fn;
+    int nwarps, rpb, nstages, grid, smem;
+};
+
+static int round_rpb(int r) { return r >= 8 ? 8 : r >= 4 ? 4 : r >= 2 ? 2 : 1; }
+
+static int plan_mmvq(int t, int nrows, int K, int ncols, int nwarps, int rpb, bool sums,
+                     Plan *p) {
+    if (!supported_type(t)) return fail(ANVIL_ERR_UNSUPPORTED, "ggml type %d has no MMVQ kernel", t);
+    if (nrows <= 0 || K <= 0) return fail(ANVIL_ERR_INVALID, "nrows=%d ncols_x=%d", nrows, K);
+    const int qk = mmvq_type_qk(t);
+    if (K % qk != 0)
+        return fail(ANVIL_ERR_INVALID, "ncols_x=%d is not a multiple of the block size %d", K, qk);
+    if (ncols < 1 || ncols > kMaxCols)
+        return fail(ANVIL_ERR_INVALID, "ncols_dst=%d outside 1..%d", ncols, kMaxCols);
+    if (nwarps < 0 || rpb < 0)
+        return fail(ANVIL_ERR_INVALID, "nwarps=%d rows_per_block=%d", nwarps, rpb);
+    if (nwarps == 0 || rpb == 0) {
+        int lnw = 0, lrpb = 0;
+        if (anvil_smithy_lookup(t, nrows, K, &lnw, &lrpb) && lnw > 0 && lrpb > 0) {
+            if (nwarps == 0) nwarps = lnw;
+            if (rpb == 0) rpb = lrpb;
+        }
+        int dnw, drpb;
+        default_config(t, nrows, K, ncols, &dnw, &drpb);
+        if (nwarps == 0) nwarps = dnw;
+        if (rpb == 0) rpb = drpb;
+    }
+    nwarps = std::min(std::max(nwarps, 1), kMaxWarps);
+    rpb = round_rpb(rpb);
+    int dev;
+    if (int s = current_device(&dev)) return s;
+    int nsm;
+    if (int s = sm_count(dev, &nsm)) return s;
+    const int row_bytes = (K / qk) * mmvq_type_bytes(t);
+    // Stages: about 32 KB of weights in flight per CTA, 2..8 stages, within shared memory.
+    for (;;) {
+        const int tile = rpb * row_bytes;
+        int ns = std::min(8, std::max(2, (32768 + tile - 1) / tile));
+        MmvqSmem L = mmvq_smem_layout(t, K, ncols, rpb, nwarps, ns);
+        while (L.total > kMaxSmem && ns > 1) L = mmvq_smem_layout(t, K, ncols, rpb, nwarps, --ns);
+        if (L.total <= kMaxSmem) {
+            p->nstages = ns;
+            p->smem = L.total;
+            break;
+        }
+        if (rpb == 1)
+            return fail(ANVIL_ERR_UNSUPPORTED, "ncols_x=%d ncols_dst=%d does not fit in shared memory",
+                        K, ncols);
+        rpb >>= 1;
+    }
+    p->fn = kernel_for(t, ncols, rpb, sums);
+    if (!p->fn) return fail(ANVIL_ERR_UNSUPPORTED, "no kernel for ncols=%d rpb=%d", ncols, rpb);
+    p->nwarps = nwarps;
+    p->rpb = rpb;
+    int occ;
+    if (int s = prepare_fn(reinterpret_cast<const void *>(p->fn), dev, nwarps * 32, p->smem, &occ))
+        return s;
+    const long ntiles = (long(nrows) + rpb - 1) / rpb;
+    p->grid = int(std::min<long>(ntiles, long(occ) * nsm));
+    return ANVIL_OK;
+}
+
+static int launch_mmvq(const Plan &p, const void *W, const void *xq, float *y, int32_t *sums,
+                       int nrows, int K, unsigned flags, cudaStream_t stream) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.grid);
+    cfg.blockDim = dim3(p.nwarps * 32);
+    cfg.dynamicSmemBytes = p.smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    if (flags & ANVIL_FLAG_PDL) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    cudaError_t e = cudaLaunchKernelEx(&cfg, p.fn, static_cast<const uint8_t *>(W),
+                                       static_cast<const uint8_t *>(xq), y, sums, nrows, K,
+                                       p.nstages);
+    if (e != cudaSuccess) return cuda_fail(e, "mmvq launch");
+    return ANVIL_OK;
+}
+
+static int check_mmvq_ptrs(int t, const void *W, const void *xq, const void *out) {
+    if (!W || !xq || !out) return fail(ANVIL_ERR_INVALID, "null pointer argument");
+    (void)t;
+    if (reinterpret_cast<uintptr_t>(W) & 15)
+        return fail(ANVIL_ERR_ALIGN, "weights must be 16-byte aligned");
+    if ((reinterpret_cast<uintptr_t>(xq) | reinterpret_cast<uintptr_t>(out)) & 3)
+        return fail(ANVIL_ERR_ALIGN, "activation and output must be 4-byte aligned");
+    return ANVIL_OK;
+}
+
+static int launch_quantize(const float *x, void *xq, int K, int ncols, unsigned flags,
+                           cudaStream_t stream) {
+    if (!x || !xq) return fail(ANVIL_ERR_INVALID, "null pointer argument");
+    if (K <= 0 || K % 32 != 0) return fail(ANVIL_ERR_INVALID, "K=%d is not a positive multiple of 32", K);
+    if (ncols < 1) return fail(ANVIL_ERR_INVALID, "ncols=%d", ncols);
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(xq)) & 3)
+        return fail(ANVIL_ERR_ALIGN, "x and xq must be 4-byte aligned");
+    const long nblocks = long(K / 32) * ncols;
+    if (nblocks > (1L << 26)) return fail(ANVIL_ERR_INVALID, "input too large");
+    cudaLaunchConfig_t cfg = {};
+    cfg.blockDim = dim3(256);
+    cfg.gridDim = dim3(unsigned((nblocks + 7) / 8));
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    if (flags & ANVIL_FLAG_PDL) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    cudaError_t e = cudaLaunchKernelEx(&cfg, quantize_q8_1_kernel, x, static_cast<uint8_t *>(xq),
+                                       int(nblocks));
+    if (e != cudaSuccess) return cuda_fail(e, "quantize_q8_1 launch");
+    return ANVIL_OK;
+}
+
+}  // namespace anvil
+
+using namespace anvil;
+
+// ---------------------------------------------------------------------------------
+// Chain executor
+// ---------------------------------------------------------------------------------
+struct ChainStep {
+    bool quantize;
+    // quantize
+    const float *x;
+    void *xq;
+    int K, ncols;
+    // mmvq
+    int type;
+    const void *W;
+    const void *xqin;
+    float *y;
+    int nrows, ncols_x, ncols_dst, nwarps, rpb;
+    Plan plan;
+};
+
+struct anvil_chain {
+    std::vector<ChainStep> steps;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+};
+
+extern "C" {
+
+int anvil_abi_version(void) { return ANVIL_ABI_VERSION; }
+
+const char *anvil_last_error(void) { return t_last_error.c_str(); }
+
+int anvil_type_geometry(int ggml_type, int *qk, int *block_bytes) {
+    int q = 0, b = 0;
+    switch (ggml_type) {
+    case ANVIL_TYPE_Q8_0: q = 32; b = 34; break;
+    case ANVIL_TYPE_Q8_1: q = 32; b = 36; break;
+    case ANVIL_TYPE_Q4_K: q = 256; b = 144; break;
+    case ANVIL_TYPE_Q5_K: q = 256; b = 176; break;
+    case ANVIL_TYPE_Q6_K: q = 256; b = 210; break;
+    default: return fail(ANVIL_ERR_UNSUPPORTED, "ggml type %d has no block geometry here", ggml_type);
+    }
+    if (qk) *qk = q;
+    if (block_bytes) *block_bytes = b;
+    return ANVIL_OK;
+}
+
+int64_t anvil_row_bytes(int ggml_type, int K) {
+    int qk, bb;
+    if (int s = anvil_type_geometry(ggml_type, &qk, &bb)) return s;
+    if (K <= 0 || K % qk) return fail(ANVIL_ERR_INVALID, "K=%d is not a multiple of %d", K, qk);
+    return int64_t(K / qk) * bb;
+}
+
+int anvil_quantize_q8_1_ex(const float *x, void *xq, int K, int ncols, unsigned flags,
+                           anvil_stream_t stream) {
+    return launch_quantize(x, xq, K, ncols, flags, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int anvil_quantize_q8_1(const float *x, void *xq, int K, int ncols, anvil_stream_t stream) {
+    return anvil_quantize_q8_1_ex(x, xq, K, ncols, 0, stream);
+}
+
+int anvil_mmvq_plan(int ggml_type, int nrows, int ncols_x, int ncols_dst, int nwarps,
+                    int rows_per_block, int *out_nwarps, int *out_rpb, int *out_grid,
+                    int *out_smem_bytes) {
+    Plan p;
+    if (int s = plan_mmvq(ggml_type, nrows, ncols_x, ncols_dst, nwarps, rows_per_block, false, &p))
+        return s;
+    if (out_nwarps) *out_nwarps = p.nwarps;
+    if (out_rpb) *out_rpb = p.rpb;
+    if (out_grid) *out_grid = p.grid;
+    if (out_smem_bytes) *out_smem_bytes = p.smem;
+    return ANVIL_OK;
+}
+
+int anvil_mmvq_ex(int ggml_type, const void *W, const void *xq, float *y, int nrows,
+                  int ncols_x, int ncols_dst, int nwarps, int rows_per_block, unsigned flags,
+                  anvil_stream_t stream) {
+    if (int s = check_mmvq_ptrs(ggml_type, W, xq, y)) return s;
+    Plan p;
+    if (int s = plan_mmvq(ggml_type, nrows, ncols_x, ncols_dst, nwarps, rows_per_block, false, &p))
+        return s;
+    return launch_mmvq(p, W, xq, y, nullptr, nrows, ncols_x, flags,
+                       reinterpret_cast<cudaStream_t>(stream));
+}
+
+int anvil_mmvq(int ggml_type, const void *W, const void *xq, float *y, int nrows, int ncols_x,
+               int ncols_dst, int nwarps, int rows_per_block, anvil_stream_t stream) {
+    return anvil_mmvq_ex(ggml_type, W, xq, y, nrows, ncols_x, ncols_dst, nwarps, rows_per_block,
+                         0, stream);
+}
+
+int anvil_mmvq_f32(int ggml_type, const void *W, const float *x, void *xq, float *y, int nrows,
+                   int ncols_x, int ncols_dst, int nwarps, int rows_per_block,
+                   anvil_stream_t stream) {
+    if (int s = check_mmvq_ptrs(ggml_type, W, xq, y)) return s;
+    Plan p;
+    if (int s = plan_mmvq(ggml_type, nrows, ncols_x, ncols_dst, nwarps, rows_per_block, false, &p))
+        return s;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (int s = launch_quantize(x, xq, ncols_x, ncols_dst, 0, st)) return s;
+    // The GEMV's only producer is the quantiser above, which never writes W, so the
+    // weight stream may start before the quantiser finishes.
+    return launch_mmvq(p, W, xq, y, nullptr, nrows, ncols_x, ANVIL_FLAG_PDL, st);
+}
+
+int anvil_mmvq_block_sums(int ggml_type, const void *W, const void *xq, int32_t *sums,
+                          int nrows, int ncols_x, int ncols_dst, int nwarps, int rows_per_block,
+                          anvil_stream_t stream) {
+    if (int s = check_mmvq_ptrs(ggml_type, W, xq, sums)) return s;
+    Plan p;
+    if (int s = plan_mmvq(ggml_type, nrows, ncols_x, ncols_dst, nwarps, rows_per_block, true, &p))
+        return s;
+    return launch_mmvq(p, W, xq, nullptr, sums, nrows, ncols_x, 0,
+                       reinterpret_cast<cudaStream_t>(stream));
+}
+
+// Reads and clears the device status words (current device).  Returns the OR of all
+// flags (0 = no bounded wait gave up) or a negative status.
+int anvil_take_device_status(void) {
+    int v = 0;
+    int parts[5] = {take_quantize_status(), mmvq_kernel_q4k_take_status(),
+                    mmvq_kernel_q5k_take_status(), mmvq_kernel_q6k_take_status(),
+                    mmvq_kernel_q80_take_status()};
+    for (int x : parts) {
+        if (x < 0) return fail(ANVIL_ERR_CUDA, "reading device status failed");
+        v |= x;
+    }
+    return v;
+}
+
+// ---- chain ------------------------------------------------------------------------
+
+anvil_chain *anvil_chain_create(void) { return new (std::nothrow) anvil_chain(); }
+
+void anvil_chain_destroy(anvil_chain *c) {
+    if (!c) return;
+    if (c->exec) cudaGraphExecDestroy(c->exec);
+    if (c->graph) cudaGraphDestroy(c->graph);
+    delete c;
+}
+
+int anvil_chain_num_steps(const anvil_chain *c) { return c ? int(c->steps.size()) : 0; }
+
+int anvil_chain_add_quantize(anvil_chain *c, const float *x, void *xq, int K, int ncols) {
+    if (!c) return fail(ANVIL_ERR_INVALID, "null chain");
+    if (c->exec) return fail(ANVIL_ERR_INVALID, "chain already instantiated");
+    if (!x || !xq || K <= 0 || K % 32 || ncols < 1)
+        return fail(ANVIL_ERR_INVALID, "bad quantize step (K=%d ncols=%d)", K, ncols);
+    ChainStep s = {};
+    s.quantize = true;
+    s.x = x;
+    s.xq = xq;
+    s.K = K;
+    s.ncols = ncols;
+    c->steps.push_back(s);
+    return ANVIL_OK;
+}
+
+int anvil_chain_add_mmvq(anvil_chain *c, int ggml_type, const void *W, const void *xq, float *y,
+                         int nrows, int ncols_x, int ncols_dst, int nwarps, int rows_per_block) {
+    if (!c) return fail(ANVIL_ERR_INVALID, "null chain");
+    if (c->exec) return fail(ANVIL_ERR_INVALID, "chain already instantiated");
+    if (int s = check_mmvq_ptrs(ggml_type, W, xq, y)) return s;
+    ChainStep s = {};
+    s.quantize = false;
+    s.type = ggml_type;
+    s.W = W;
+    s.xqin = xq;
+    s.y = y;
+    s.nrows = nrows;
+    s.ncols_x = ncols_x;
+    s.ncols_dst = ncols_dst;
+    s.nwarps = nwarps;
+    s.rpb = rows_per_block;
+    if (int st = plan_mmvq(ggml_type, nrows, ncols_x, ncols_dst, nwarps, rows_per_block, false,
+                           &s.plan))
+        return st;
+    c->steps.push_back(s);
+    return ANVIL_OK;
+}
+
+static int run_steps(anvil_chain *c, bool use_pdl, cudaStream_t st) {
+    for (size_t i = 0; i < c->steps.size(); ++i) {
+        const ChainStep &s = c->steps[i];
+        const unsigned flags = (use_pdl && i > 0) ? ANVIL_FLAG_PDL : 0u;
+        int r = s.quantize ? launch_quantize(s.x, s.xq, s.K, s.ncols, flags, st)
+                           : launch_mmvq(s.plan, s.W, s.xqin, s.y, nullptr, s.nrows, s.ncols_x,
+                                         flags, st);
+        if (r) return r;
+    }
+    return ANVIL_OK;
+}
+
+int anvil_chain_instantiate(anvil_chain *c, int use_pdl, anvil_stream_t stream) {
+    if (!c) return fail(ANVIL_ERR_INVALID, "null chain");
+    if (c->exec) return fail(ANVIL_ERR_INVALID, "chain already instantiated");
+    if (c->steps.empty()) return fail(ANVIL_ERR_INVALID, "empty chain");
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (!st) return fail(ANVIL_ERR_INVALID, "graph capture needs a non-default stream");
+    cudaError_t e = cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamBeginCapture");
+    const int r = run_steps(c, use_pdl != 0, st);
+    cudaGraph_t g = nullptr;
+    e = cudaStreamEndCapture(st, &g);
+    if (r) {
+        if (g) cudaGraphDestroy(g);
+        return r;
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamEndCapture");
+    cudaGraphExec_t ex = nullptr;
+    e = cudaGraphInstantiate(&ex, g, 0);
+    if (e != cudaSuccess) {
+        cudaGraphDestroy(g);
+        return cuda_fail(e, "cudaGraphInstantiate");
+    }
+    c->graph = g;
+    c->exec = ex;
+    return ANVIL_OK;
+}
+
+int anvil_chain_launch(anvil_chain *c, anvil_stream_t stream) {
+    if (!c) return fail(ANVIL_ERR_INVALID, "null chain");
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (c->exec) {
+        cudaError_t e = cudaGraphLaunch(c->exec, st);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaGraphLaunch");
+        return ANVIL_OK;
+    }
+    return run_steps(c, false, st);
+}
+
+}  // extern "C"

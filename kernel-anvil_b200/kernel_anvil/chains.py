@@ -1,0 +1,198 @@
+"""Per-token GEMV chains of decode-shaped models, and their device-side builder.
+
+A chain is the sequence of quantized GEMVs one decode token runs (the MMVQ launches of
+llama.cpp's decode, docs/decode-pipeline-breakdown.md:20-21), each preceded by the Q8_1
+quantisation of its input when that input is new.  Attention, norms and activations are
+not part of the path: every distinct GEMV input is a fixed synthetic fp32 vector that
+is quantised inside the chain, so the chain carries exactly the quantize + MMVQ work.
+
+Shapes are (nrows N, ncols_x K) = (output features, input features).
+
+  qwen3_8b      36 layers: q 4096x4096, k/v 1024x4096, o 4096x4096, gate/up 12288x4096,
+                down 4096x12288; Q4_K except Q6_K on attn_v and ffn_down in even layers;
+                lm_head 151936x4096 Q4_K.  253 GEMVs, 145 quantisations per token.
+  qwen3_0_6b    28 layers, all Q8_0: q 2048x1024, k/v 1024x1024, o 1024x2048,
+                gate/up 3072x1024, down 1024x3072 (speculative-decoding draft).
+  llama3_70b    80 layers, all Q4_K: q/o 8192x8192, k/v 1024x8192, gate/up 28672x8192,
+                down 8192x28672.
+  qwen35_27b    tuned-shape set: Q4_K 5120x6144 x48, Q5_K 5120x10240 x48,
+                Q4_K 6144x5120 x64, Q4_K 5120x1024 x22 (shapes as given, N x K).
+"""
+from __future__ import annotations
+
+from collections import Counter
+from dataclasses import dataclass, field
+
+from kernel_anvil.quants import gemv_bytes, resolve_type
+
+
+@dataclass(frozen=True)
+class Gemv:
+    name: str
+    qt: str
+    nrows: int
+    K: int
+    input: str  # id of the activation vector it consumes
+
+
+@dataclass
+class ChainSpec:
+    name: str
+    gemvs: list[Gemv]
+    inputs: dict[str, int] = field(default_factory=dict)  # activation id -> K (in first-use order)
+
+    def unique_shapes(self) -> dict[tuple[str, int, int], int]:
+        """{(quant, N, K): count} over the chain's GEMVs."""
+        return dict(Counter((g.qt, g.nrows, g.K) for g in self.gemvs))
+
+    def algorithmic_bytes(self, ncols: int = 1) -> int:
+        return sum(gemv_bytes(g.qt, g.nrows, g.K, ncols) for g in self.gemvs)
+
+    def weight_bytes(self) -> int:
+        return sum(g.nrows * resolve_type(g.qt).row_bytes(g.K) for g in self.gemvs)
+
+
+def _layered(name: str, n_layers: int, per_layer, tail=()) -> ChainSpec:
+    spec = ChainSpec(name, [])
+    for layer in range(n_layers):
+        for gname, qt, n, k, inp in per_layer(layer):
+            act = f"{inp}.{layer}"
+            spec.inputs.setdefault(act, k)
+            spec.gemvs.append(Gemv(f"blk.{layer}.{gname}", qt, n, k, act))
+    for gname, qt, n, k, inp in tail:
+        spec.inputs.setdefault(inp, k)
+        spec.gemvs.append(Gemv(gname, qt, n, k, inp))
+    return spec
+
+
+def qwen3_8b() -> ChainSpec:
+    h, kv, inter = 4096, 1024, 12288
+
+    def layer(i):
+        mix = "Q6_K" if i % 2 == 0 else "Q4_K"
+        return [("attn_q", "Q4_K", h, h, "attn_in"), ("attn_k", "Q4_K", kv, h, "attn_in"),
+                ("attn_v", mix, kv, h, "attn_in"), ("attn_output", "Q4_K", h, h, "attn_out"),
+                ("ffn_gate", "Q4_K", inter, h, "ffn_in"), ("ffn_up", "Q4_K", inter, h, "ffn_in"),
+                ("ffn_down", mix, h, inter, "ffn_act")]
+
+    return _layered("qwen3_8b", 36, layer, tail=[("output", "Q4_K", 151936, h, "final")])
+
+
+def qwen3_0_6b() -> ChainSpec:
+    h, q, kv, inter = 1024, 2048, 1024, 3072
+
+    def layer(i):
+        return [("attn_q", "Q8_0", q, h, "attn_in"), ("attn_k", "Q8_0", kv, h, "attn_in"),
+                ("attn_v", "Q8_0", kv, h, "attn_in"), ("attn_output", "Q8_0", h, q, "attn_out"),
+                ("ffn_gate", "Q8_0", inter, h, "ffn_in"), ("ffn_up", "Q8_0", inter, h, "ffn_in"),
+                ("ffn_down", "Q8_0", h, inter, "ffn_act")]
+
+    return _layered("qwen3_0_6b", 28, layer)
+
+
+def llama3_70b() -> ChainSpec:
+    h, kv, inter = 8192, 1024, 28672
+
+    def layer(i):
+        return [("attn_q", "Q4_K", h, h, "attn_in"), ("attn_k", "Q4_K", kv, h, "attn_in"),
+                ("attn_v", "Q4_K", kv, h, "attn_in"), ("attn_output", "Q4_K", h, h, "attn_out"),
+                ("ffn_gate", "Q4_K", inter, h, "ffn_in"), ("ffn_up", "Q4_K", inter, h, "ffn_in"),
+                ("ffn_down", "Q4_K", h, inter, "ffn_act")]
+
+    return _layered("llama3_70b", 80, layer)
+
+
+def qwen35_27b() -> ChainSpec:
+    spec = ChainSpec("qwen35_27b", [])
+    for qt, n, k, count in (("Q4_K", 5120, 6144, 48), ("Q5_K", 5120, 10240, 48),
+                            ("Q4_K", 6144, 5120, 64), ("Q4_K", 5120, 1024, 22)):
+        for i in range(count):
+            act = f"in{k}.{i}"
+            spec.inputs[act] = k
+            spec.gemvs.append(Gemv(f"{qt}.{n}x{k}.{i}", qt, n, k, act))
+    return spec
+
+
+CHAINS = {"qwen3_8b": qwen3_8b, "qwen3_0_6b": qwen3_0_6b, "llama3_70b": llama3_70b,
+          "qwen35_27b": qwen35_27b}
+
+
+def get_chain(name: str) -> ChainSpec:
+    try:
+        return CHAINS[name]()
+    except KeyError:
+        raise ValueError(f"unknown chain {name!r}; have {sorted(CHAINS)}") from None
+
+
+def shard_rows(nrows: int, rank: int, world: int) -> tuple[int, int]:
+    """Row range [start, stop) of `rank` when nrows rows are split over `world` ranks.
+
+    Rows are independent in a GEMV and a GGUF block never spans two rows, so any split
+    on row boundaries is exact; ranks get contiguous, near-equal slices."""
+    base, extra = divmod(nrows, world)
+    start = rank * base + min(rank, extra)
+    return start, start + base + (1 if rank < extra else 0)
+
+
+class DeviceChain:
+    """Weights, activations and outputs of a ChainSpec on one GPU, plus its anvil Chain.
+
+    With world > 1 every matrix holds only this rank's row shard (shard_rows); outputs
+    are the local slices.  Weights are drawn on the device (quants.make_weights_device).
+    """
+
+    def __init__(self, spec: ChainSpec, ncols: int = 1, seed: int = 0, device="cuda",
+                 rank: int = 0, world: int = 1, nwarps: int = 0, rows_per_block: int = 0,
+                 configs: dict | None = None):
+        import torch
+
+        from kernel_anvil.mmvq import Chain, q8_1_bytes
+        from kernel_anvil.quants import make_weights_device
+
+        self.spec = spec
+        self.ncols = ncols
+        self.rank, self.world = rank, world
+        g = torch.Generator(device=device)
+        g.manual_seed(seed + 7919)
+        # All fp32 inputs live in one buffer so a step's inputs arrive with one copy.
+        total = sum(k * ncols for k in spec.inputs.values())
+        self.x_all = torch.randn(total, generator=g, device=device, dtype=torch.float32)
+        self.x, off = {}, 0
+        for a, k in spec.inputs.items():
+            self.x[a] = self.x_all[off:off + k * ncols].view(ncols, k)
+            off += k * ncols
+        self.xq = {a: torch.empty(q8_1_bytes(k, ncols), dtype=torch.uint8, device=device)
+                   for a, k in spec.inputs.items()}
+        self.weights, self.outputs, self.rows = [], [], []
+        self.chain = Chain()
+        quantized: set[str] = set()
+        for i, gm in enumerate(spec.gemvs):
+            r0, r1 = shard_rows(gm.nrows, rank, world)
+            n = r1 - r0
+            W = make_weights_device(gm.qt, n, gm.K, seed=seed * 100003 + i * 31 + rank, device=device)
+            y = torch.empty((ncols, n), dtype=torch.float32, device=device)
+            if gm.input not in quantized:
+                self.chain.add_quantize(self.x[gm.input], self.xq[gm.input])
+                quantized.add(gm.input)
+            nw, rpb = nwarps, rows_per_block
+            if configs and (gm.qt, gm.nrows, gm.K) in configs:
+                c = configs[(gm.qt, gm.nrows, gm.K)]
+                nw, rpb = c["nwarps"], c["rows_per_block"]
+            self.chain.add_mmvq(W, gm.qt, self.xq[gm.input], y, nrows=n, K=gm.K, ncols=ncols,
+                                nwarps=nw, rows_per_block=rpb)
+            self.weights.append(W)
+            self.outputs.append(y)
+            self.rows.append((r0, r1))
+
+    @property
+    def algorithmic_bytes(self) -> int:
+        return self.chain.algorithmic_bytes
+
+    def instantiate(self, pdl: bool = True) -> None:
+        self.chain.instantiate(pdl=pdl)
+
+    def launch(self) -> None:
+        self.chain.launch()
+
+    def close(self) -> None:
+        self.chain.close()

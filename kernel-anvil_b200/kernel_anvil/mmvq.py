@@ -1,0 +1,231 @@
+"""Torch-facing MMVQ ops over the libanvil C ABI (include/anvil.h).
+
+Tensors are passed as raw device pointers together with torch's current CUDA stream, so
+the ops compose with torch code and with CUDA graph capture.  All ops require CUDA
+tensors: there is no CPU path.
+
+Layouts (GGUF / llama.cpp conventions):
+  W   uint8 (nrows, row_bytes): row r holds K/qk consecutive blocks of the quant type.
+  x   fp32 (ncols, K): ncols activation columns.
+  xq  uint8 (ncols, K/32*36): Q8_1 blocks {half d, half s, int8 q[32]} per column.
+  y   fp32 (ncols, nrows).
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from kernel_anvil import _native
+from kernel_anvil._native import ANVIL_FLAG_PDL, AnvilError, check
+from kernel_anvil.quants import Q8_1_BLOCK_SIZE, QuantTypeInfo, resolve_type
+
+MAX_COLS = 8
+
+
+def _stream_ptr() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _require_cuda(name: str, t: torch.Tensor, dtype: torch.dtype) -> None:
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if not t.is_cuda:
+        raise AnvilError(_native.ANVIL_ERR_INVALID, f"{name} must be a CUDA tensor (no CPU path)")
+    if t.dtype != dtype:
+        raise AnvilError(_native.ANVIL_ERR_INVALID, f"{name} must be {dtype}, got {t.dtype}")
+    if not t.is_contiguous():
+        raise AnvilError(_native.ANVIL_ERR_INVALID, f"{name} must be contiguous")
+
+
+def q8_1_bytes(K: int, ncols: int = 1) -> int:
+    return ncols * (K // 32) * Q8_1_BLOCK_SIZE
+
+
+def quantize_q8_1(x: torch.Tensor, out: torch.Tensor | None = None, pdl: bool = False) -> torch.Tensor:
+    """Quantise fp32 activations (ncols, K) or (K,) to Q8_1 blocks (llama.cpp quantize_q8_1)."""
+    _require_cuda("x", x, torch.float32)
+    x2 = x.reshape(1, -1) if x.dim() == 1 else x
+    ncols, K = x2.shape
+    if out is None:
+        out = torch.empty((ncols, q8_1_bytes(K)), dtype=torch.uint8, device=x.device)
+    _require_cuda("out", out, torch.uint8)
+    if out.numel() < q8_1_bytes(K, ncols):
+        raise AnvilError(_native.ANVIL_ERR_INVALID, "out is too small")
+    check(_native.lib().anvil_quantize_q8_1_ex(x2.data_ptr(), out.data_ptr(), K, ncols,
+                                               ANVIL_FLAG_PDL if pdl else 0, _stream_ptr()))
+    return out
+
+
+def _shape_args(W: torch.Tensor, info: QuantTypeInfo, nrows, K):
+    if W.dim() == 2:
+        nrows = W.shape[0] if nrows is None else nrows
+        if K is None:
+            if W.shape[1] % info.block_size:
+                raise AnvilError(_native.ANVIL_ERR_INVALID, "row bytes not a multiple of the block size")
+            K = W.shape[1] // info.block_size * info.qk
+    if nrows is None or K is None:
+        raise AnvilError(_native.ANVIL_ERR_INVALID, "nrows and K are needed for a flat W")
+    if W.numel() < nrows * info.row_bytes(K):
+        raise AnvilError(_native.ANVIL_ERR_INVALID, "W is smaller than nrows x row_bytes")
+    return nrows, K
+
+
+def mmvq(W: torch.Tensor, qt, xq: torch.Tensor, nrows: int | None = None, K: int | None = None,
+         ncols: int | None = None, nwarps: int = 0, rows_per_block: int = 0,
+         out: torch.Tensor | None = None, pdl: bool = False) -> torch.Tensor:
+    """y = W @ dequant(xq) for ncols Q8_1 columns: the sm_100a MMVQ kernel.
+
+    nwarps / rows_per_block of 0 use the smithy table entry for (type, nrows, K) or the
+    built-in default.  ``pdl=True`` lets the kernel prefetch W before the previous kernel
+    in the stream finishes (W must not be produced by that kernel).
+    """
+    info = resolve_type(qt)
+    _require_cuda("W", W, torch.uint8)
+    _require_cuda("xq", xq, torch.uint8)
+    nrows, K = _shape_args(W, info, nrows, K)
+    if ncols is None:
+        ncols = xq.numel() // q8_1_bytes(K)
+    if not 1 <= ncols <= MAX_COLS:
+        raise AnvilError(_native.ANVIL_ERR_INVALID, f"ncols={ncols} outside 1..{MAX_COLS}")
+    if xq.numel() < q8_1_bytes(K, ncols):
+        raise AnvilError(_native.ANVIL_ERR_INVALID, "xq is too small")
+    if out is None:
+        out = torch.empty((ncols, nrows), dtype=torch.float32, device=W.device)
+    _require_cuda("out", out, torch.float32)
+    if out.numel() < ncols * nrows:
+        raise AnvilError(_native.ANVIL_ERR_INVALID, "out is too small")
+    check(_native.lib().anvil_mmvq_ex(info.ggml_type, W.data_ptr(), xq.data_ptr(), out.data_ptr(),
+                                      nrows, K, ncols, nwarps, rows_per_block,
+                                      ANVIL_FLAG_PDL if pdl else 0, _stream_ptr()))
+    return out
+
+
+def mmvq_f32(W: torch.Tensor, qt, x: torch.Tensor, nwarps: int = 0, rows_per_block: int = 0,
+             xq_scratch: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Quantise fp32 x (ncols, K) to Q8_1 and run MMVQ, as llama.cpp's MMVQ path does."""
+    info = resolve_type(qt)
+    _require_cuda("W", W, torch.uint8)
+    _require_cuda("x", x, torch.float32)
+    x2 = x.reshape(1, -1) if x.dim() == 1 else x
+    ncols, K = x2.shape
+    nrows, K = _shape_args(W, info, None, K)
+    if xq_scratch is None:
+        xq_scratch = torch.empty(q8_1_bytes(K, ncols), dtype=torch.uint8, device=W.device)
+    _require_cuda("xq_scratch", xq_scratch, torch.uint8)
+    if out is None:
+        out = torch.empty((ncols, nrows), dtype=torch.float32, device=W.device)
+    _require_cuda("out", out, torch.float32)
+    check(_native.lib().anvil_mmvq_f32(info.ggml_type, W.data_ptr(), x2.data_ptr(),
+                                       xq_scratch.data_ptr(), out.data_ptr(), nrows, K, ncols,
+                                       nwarps, rows_per_block, _stream_ptr()))
+    return out
+
+
+def block_sums(W: torch.Tensor, qt, xq: torch.Tensor, nrows: int | None = None, K: int | None = None,
+               ncols: int | None = None, nwarps: int = 0, rows_per_block: int = 0) -> torch.Tensor:
+    """The production kernel's exact int32 block dots, shape (ncols, nrows, nsub).
+
+    nsub = K/16 for Q6_K (one per int8 scale group), K/32 otherwise (one per Q8_1 block).
+    """
+    info = resolve_type(qt)
+    _require_cuda("W", W, torch.uint8)
+    _require_cuda("xq", xq, torch.uint8)
+    nrows, K = _shape_args(W, info, nrows, K)
+    if ncols is None:
+        ncols = xq.numel() // q8_1_bytes(K)
+    nsub = K // 16 if info.name == "Q6_K" else K // 32
+    out = torch.empty((ncols, nrows, nsub), dtype=torch.int32, device=W.device)
+    check(_native.lib().anvil_mmvq_block_sums(info.ggml_type, W.data_ptr(), xq.data_ptr(),
+                                              out.data_ptr(), nrows, K, ncols, nwarps,
+                                              rows_per_block, _stream_ptr()))
+    return out
+
+
+def plan(qt, nrows: int, K: int, ncols: int = 1, nwarps: int = 0, rows_per_block: int = 0) -> dict:
+    """Launch geometry the library would use: nwarps, rows_per_block, grid, smem bytes."""
+    info = resolve_type(qt)
+    v = [ctypes.c_int() for _ in range(4)]
+    check(_native.lib().anvil_mmvq_plan(info.ggml_type, nrows, K, ncols, nwarps, rows_per_block,
+                                        *[ctypes.byref(a) for a in v]))
+    return {"nwarps": v[0].value, "rows_per_block": v[1].value, "grid": v[2].value,
+            "smem_bytes": v[3].value}
+
+
+def take_device_status() -> int:
+    """OR of device status flags raised since the last call (1 = an mbarrier wait gave up)."""
+    return check(_native.lib().anvil_take_device_status())
+
+
+class Chain:
+    """An ordered list of quantize / MMVQ steps on fixed buffers, captured once into a CUDA
+    graph (native executor, include/anvil.h anvil_chain_*) and replayed per token.
+
+    The tensors passed to ``add_*`` must stay alive (and at the same address) for the
+    chain's lifetime; the chain keeps references to them.
+    """
+
+    def __init__(self):
+        self._lib = _native.lib()
+        self._h = self._lib.anvil_chain_create()
+        if not self._h:
+            raise AnvilError(_native.ANVIL_ERR_CUDA, "anvil_chain_create failed")
+        self._keep: list[torch.Tensor] = []
+        self.instantiated = False
+        self.weight_bytes = 0
+        self.algorithmic_bytes = 0
+        self.n_mmvq = 0
+        self.n_quantize = 0
+
+    def add_quantize(self, x: torch.Tensor, xq: torch.Tensor) -> None:
+        _require_cuda("x", x, torch.float32)
+        _require_cuda("xq", xq, torch.uint8)
+        x2 = x.reshape(1, -1) if x.dim() == 1 else x
+        ncols, K = x2.shape
+        if xq.numel() < q8_1_bytes(K, ncols):
+            raise AnvilError(_native.ANVIL_ERR_INVALID, "xq is too small")
+        check(self._lib.anvil_chain_add_quantize(self._h, x2.data_ptr(), xq.data_ptr(), K, ncols))
+        self._keep += [x, xq]
+        self.n_quantize += 1
+
+    def add_mmvq(self, W: torch.Tensor, qt, xq: torch.Tensor, y: torch.Tensor, nrows: int | None = None,
+                 K: int | None = None, ncols: int = 1, nwarps: int = 0, rows_per_block: int = 0) -> None:
+        info = resolve_type(qt)
+        _require_cuda("W", W, torch.uint8)
+        _require_cuda("xq", xq, torch.uint8)
+        _require_cuda("y", y, torch.float32)
+        nrows, K = _shape_args(W, info, nrows, K)
+        if xq.numel() < q8_1_bytes(K, ncols) or y.numel() < ncols * nrows:
+            raise AnvilError(_native.ANVIL_ERR_INVALID, "xq or y is too small")
+        check(self._lib.anvil_chain_add_mmvq(self._h, info.ggml_type, W.data_ptr(), xq.data_ptr(),
+                                             y.data_ptr(), nrows, K, ncols, nwarps, rows_per_block))
+        self._keep += [W, xq, y]
+        self.n_mmvq += 1
+        self.weight_bytes += nrows * info.row_bytes(K)
+        from kernel_anvil.quants import gemv_bytes
+        self.algorithmic_bytes += gemv_bytes(info, nrows, K, ncols)
+
+    def instantiate(self, pdl: bool = True, stream: torch.cuda.Stream | None = None) -> None:
+        s = stream if stream is not None else torch.cuda.current_stream()
+        check(self._lib.anvil_chain_instantiate(self._h, 1 if pdl else 0, s.cuda_stream))
+        self.instantiated = True
+
+    def launch(self, stream: torch.cuda.Stream | None = None) -> None:
+        s = stream if stream is not None else torch.cuda.current_stream()
+        check(self._lib.anvil_chain_launch(self._h, s.cuda_stream))
+
+    @property
+    def num_steps(self) -> int:
+        return self._lib.anvil_chain_num_steps(self._h)
+
+    def close(self) -> None:
+        if self._h:
+            self._lib.anvil_chain_destroy(self._h)
+            self._h = None
+            self._keep.clear()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

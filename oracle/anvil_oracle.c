@@ -1,0 +1,339 @@
+/*
+ * anvil_oracle.c -- CPU restatement of the MMVQ hot path, used ONLY as test
+ * infrastructure: the parity checker for tests/, __graft_entry__.smoke() and the
+ * cpu_baseline leg of bench.py.  Nothing in the product links or calls it.
+ *
+ * What it restates, and from where:
+ *   - GGUF block layouts and per-weight dequantisation of Q4_K, Q5_K, Q6_K and Q8_0:
+ *     gguf-py (the reference's declared dependency, kernel-anvil pyproject.toml:19,
+ *     gguf 0.19.0) gguf/quants.py:378-401 (Q8_0), 474-523 (Q4_K incl. get_scale_min),
+ *     525-549 (Q5_K), 552-572 (Q6_K).  Pinned in tests against gguf.quants.dequantize.
+ *   - Q8_1 activation quantisation: llama.cpp's CUDA quantize_q8_1 semantics (the
+ *     reference's runtime path: kernel_anvil/hip_codegen.py:392-396 layout, 101-102 size;
+ *     docs/decode-pipeline-breakdown.md:21): per 32 values d = max|x|/127,
+ *     q = roundf(x/d), stored {half(d), half(sum x)}; the sum is taken in the
+ *     xor-butterfly order of a 32-lane warp reduction.  gguf-py has no Q8_1; its Q8_0
+ *     quantiser (gguf/quants.py:381-392) is the closest pinned relative and tests
+ *     compare against it.
+ *   - Block dots: the MMVQ arithmetic of vec_dot_{q4_K,q5_K,q6_K,q8_0}_q8_1 as restated
+ *     in kernel_anvil/hip_codegen.py:430-491 (with qi = 32, the correct QI4_K of
+ *     kernel_anvil/hip_codegen.py:86) and docs/llama-cpp-kernel-analysis.md:200-224:
+ *     exact int32 sums per sub-block, then
+ *     y = sum_b d_b * sum_j d8_j * sc_j * sumi_j - dmin_b * sum_j d8_j * m_j * sumq_j,
+ *     evaluated here in double.
+ *
+ * Build: oracle/Makefile (gcc -O2 -fopenmp -ffp-contract=off, no fast-math: IEEE
+ * division and rounding must match the GPU bit for bit).
+ */
+#include <math.h>
+#include <stdint.h>
+#include <string.h>
+
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+enum { T_Q8_0 = 8, T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14 };
+
+/* ---- IEEE binary16 conversions (written from the format definition) ---------- */
+
+float oracle_half_to_float(uint16_t h) {
+    const uint32_t sign = (uint32_t)(h >> 15) << 31;
+    const uint32_t exp = (h >> 10) & 0x1F;
+    const uint32_t man = h & 0x3FF;
+    uint32_t bits;
+    if (exp == 0) {
+        if (man == 0) {
+            bits = sign;
+        } else { /* subnormal: value = man * 2^-24 */
+            float v = (float)man * 5.9604644775390625e-8f;
+            memcpy(&bits, &v, 4);
+            bits |= sign;
+        }
+    } else if (exp == 31) {
+        bits = sign | 0x7F800000u | (man << 13);
+    } else {
+        bits = sign | ((exp + 112) << 23) | (man << 13);
+    }
+    float f;
+    memcpy(&f, &bits, 4);
+    return f;
+}
+
+/* float -> binary16, round to nearest, ties to even. */
+uint16_t oracle_float_to_half(float f) {
+    uint32_t x;
+    memcpy(&x, &f, 4);
+    const uint16_t sign = (uint16_t)((x >> 16) & 0x8000);
+    const uint32_t ax = x & 0x7FFFFFFFu;
+    if (ax >= 0x7F800000u) { /* inf or nan */
+        return sign | 0x7C00 | (ax > 0x7F800000u ? 0x200 : 0);
+    }
+    const int e = (int)(ax >> 23) - 127; /* unbiased exponent */
+    if (e > 15) return sign | 0x7C00;    /* overflow to inf (>= 65536 before rounding) */
+    uint32_t mant = (ax & 0x7FFFFF) | 0x800000; /* 24-bit significand with hidden bit */
+    int shift;                                  /* right shift to the half ulp grid */
+    uint32_t hexp;
+    if (e >= -14) {
+        shift = 13;
+        hexp = (uint32_t)(e + 15);
+    } else {
+        if (ax == 0) return sign;
+        shift = 13 + (-14 - e); /* subnormal half */
+        hexp = 0;
+        if (shift > 24) return sign; /* below half the smallest subnormal */
+    }
+    const uint32_t q = mant >> shift;
+    const uint32_t rem = mant & ((1u << shift) - 1);
+    const uint32_t halfway = 1u << (shift - 1);
+    uint32_t r = q;
+    if (rem > halfway || (rem == halfway && (q & 1))) r += 1;
+    uint32_t out;
+    if (hexp == 0) {
+        out = r; /* may carry into the smallest normal: still the right encoding */
+    } else {
+        /* r has 11 bits (hidden bit at 10); a carry to bit 11 bumps the exponent */
+        if (r & 0x800) {
+            r >>= 1;
+            hexp += 1;
+        }
+        if (hexp >= 31) return sign | 0x7C00;
+        out = (hexp << 10) | (r & 0x3FF);
+    }
+    return sign | (uint16_t)out;
+}
+
+static inline uint16_t rd16(const uint8_t *p) { return (uint16_t)(p[0] | (p[1] << 8)); }
+
+/* ---- Q8_1 quantiser ---------------------------------------------------------- */
+
+void oracle_quantize_q8_1(const float *x, uint8_t *xq, int64_t K, int64_t ncols) {
+    const int64_t nb = K / 32 * ncols;
+#pragma omp parallel for schedule(static)
+    for (int64_t b = 0; b < nb; ++b) {
+        const float *v = x + b * 32;
+        float amax = 0.0f;
+        float s[32];
+        for (int l = 0; l < 32; ++l) {
+            const float a = fabsf(v[l]);
+            amax = a > amax ? a : amax;
+            s[l] = v[l];
+        }
+        for (int o = 16; o > 0; o >>= 1) { /* xor-butterfly: lane l adds lane l^o */
+            float t[32];
+            for (int l = 0; l < 32; ++l) t[l] = s[l] + s[l ^ o];
+            memcpy(s, t, sizeof(s));
+        }
+        const float d = amax / 127.0f;
+        uint8_t *blk = xq + b * 36;
+        for (int l = 0; l < 32; ++l) {
+            const int q = amax == 0.0f ? 0 : (int)roundf(v[l] / d);
+            blk[4 + l] = (uint8_t)(int8_t)q;
+        }
+        const uint16_t hd = oracle_float_to_half(d), hs = oracle_float_to_half(s[0]);
+        blk[0] = (uint8_t)hd;
+        blk[1] = (uint8_t)(hd >> 8);
+        blk[2] = (uint8_t)hs;
+        blk[3] = (uint8_t)(hs >> 8);
+    }
+}
+
+/* ---- K-quant scale unpacking (gguf/quants.py:478-501) ------------------------- */
+
+static void q4k_scale_min(const uint8_t *s, int j, int *sc, int *m) {
+    if (j < 4) {
+        *sc = s[j] & 63;
+        *m = s[j + 4] & 63;
+    } else {
+        *sc = (s[j + 4] & 0xF) | ((s[j - 4] >> 6) << 4);
+        *m = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+    }
+}
+
+/* Unsigned quant of weight e (0..31) of sub-block j (0..7). */
+static inline int q4k_quant(const uint8_t *blk, int j, int e) {
+    const uint8_t b = blk[16 + 32 * (j >> 1) + e];
+    return (j & 1) ? (b >> 4) : (b & 0xF);
+}
+static inline int q5k_quant(const uint8_t *blk, int j, int e) {
+    const uint8_t b = blk[48 + 32 * (j >> 1) + e];
+    const int lo = (j & 1) ? (b >> 4) : (b & 0xF);
+    const int hi = (blk[16 + e] >> j) & 1;
+    return lo | (hi << 4);
+}
+/* Signed quant (q - 32) of weight e (0..31) of 32-weight sub-block j (0..7) of a Q6_K
+ * block: j = 4h + 2s + t uses ql[64h + 32t + e] nibble s and qh[32h + e] bits 2(2s+t). */
+static inline int q6k_quant(const uint8_t *blk, int j, int e) {
+    const int h = j >> 2, s = (j >> 1) & 1, t = j & 1;
+    const uint8_t l = blk[64 * h + 32 * t + e];
+    const int lo = s ? (l >> 4) : (l & 0xF);
+    const int hi = (blk[128 + 32 * h + e] >> (2 * (j & 3))) & 3;
+    return (lo | (hi << 4)) - 32;
+}
+
+static int type_bytes(int t) {
+    return t == T_Q4_K ? 144 : t == T_Q5_K ? 176 : t == T_Q6_K ? 210 : t == T_Q8_0 ? 34 : 0;
+}
+static int type_qk(int t) { return t == T_Q8_0 ? 32 : 256; }
+
+/* ---- dequantisation (gguf-py float32 operation order) -------------------------- */
+
+int oracle_dequant(int type, const uint8_t *W, float *out, int64_t nrows, int64_t K) {
+    const int bytes = type_bytes(type), qk = type_qk(type);
+    if (!bytes || K % qk) return -1;
+    const int64_t nblk = nrows * (K / qk);
+#pragma omp parallel for schedule(static)
+    for (int64_t b = 0; b < nblk; ++b) {
+        const uint8_t *blk = W + b * bytes;
+        float *o = out + b * qk;
+        if (type == T_Q8_0) {
+            const float d = oracle_half_to_float(rd16(blk));
+            for (int e = 0; e < 32; ++e) o[e] = (float)(int8_t)blk[2 + e] * d;
+        } else if (type == T_Q6_K) {
+            const float d = oracle_half_to_float(rd16(blk + 208));
+            for (int j = 0; j < 8; ++j)
+                for (int e = 0; e < 32; ++e) {
+                    const float dl = d * (float)(int8_t)blk[192 + 2 * j + (e >> 4)];
+                    o[32 * j + e] = dl * (float)q6k_quant(blk, j, e);
+                }
+        } else {
+            const float d = oracle_half_to_float(rd16(blk));
+            const float dmin = oracle_half_to_float(rd16(blk + 2));
+            for (int j = 0; j < 8; ++j) {
+                int sc, m;
+                q4k_scale_min(blk + 4, j, &sc, &m);
+                const float dl = d * (float)sc, ml = dmin * (float)m;
+                for (int e = 0; e < 32; ++e) {
+                    const int q = type == T_Q4_K ? q4k_quant(blk, j, e) : q5k_quant(blk, j, e);
+                    o[32 * j + e] = dl * (float)q - ml;
+                }
+            }
+        }
+    }
+    return 0;
+}
+
+/* ---- integer block sums and y -------------------------------------------------- */
+
+/* Exact integer dots.  sums[(c*nrows + r)*nsub + s] with nsub = K/16 for Q6_K (one per
+ * int8 scale group) and K/32 otherwise (one per Q8_1 block).  Q4_K/Q5_K use the unsigned
+ * quant (the min term is separate), Q6_K uses q - 32, Q8_0 the int8 quant. */
+int oracle_block_sums(int type, const uint8_t *W, const uint8_t *xq, int32_t *sums,
+                      int64_t nrows, int64_t K, int64_t ncols) {
+    const int bytes = type_bytes(type), qk = type_qk(type);
+    if (!bytes || K % qk) return -1;
+    const int64_t nblk = K / qk, nkb = K / 32;
+    const int64_t nsub = type == T_Q6_K ? K / 16 : K / 32;
+#pragma omp parallel for collapse(2) schedule(static)
+    for (int64_t c = 0; c < ncols; ++c)
+        for (int64_t r = 0; r < nrows; ++r) {
+            const uint8_t *row = W + r * nblk * bytes;
+            const uint8_t *xc = xq + c * nkb * 36;
+            int32_t *out = sums + (c * nrows + r) * nsub;
+            for (int64_t b = 0; b < nblk; ++b) {
+                const uint8_t *blk = row + b * bytes;
+                if (type == T_Q8_0) {
+                    const int8_t *a = (const int8_t *)(xc + b * 36 + 4);
+                    int32_t s = 0;
+                    for (int e = 0; e < 32; ++e) s += (int32_t)(int8_t)blk[2 + e] * a[e];
+                    out[b] = s;
+                    continue;
+                }
+                for (int j = 0; j < 8; ++j) {
+                    const int8_t *a = (const int8_t *)(xc + (8 * b + j) * 36 + 4);
+                    if (type == T_Q6_K) {
+                        int32_t s0 = 0, s1 = 0;
+                        for (int e = 0; e < 16; ++e) s0 += q6k_quant(blk, j, e) * a[e];
+                        for (int e = 16; e < 32; ++e) s1 += q6k_quant(blk, j, e) * a[e];
+                        out[16 * b + 2 * j] = s0;
+                        out[16 * b + 2 * j + 1] = s1;
+                    } else {
+                        int32_t s = 0;
+                        for (int e = 0; e < 32; ++e)
+                            s += (type == T_Q4_K ? q4k_quant(blk, j, e) : q5k_quant(blk, j, e)) * a[e];
+                        out[8 * b + j] = s;
+                    }
+                }
+            }
+        }
+    return 0;
+}
+
+/* y[c*nrows + r] in double from the exact block sums (same formula as the kernels). */
+int oracle_mmvq(int type, const uint8_t *W, const uint8_t *xq, double *y, int64_t nrows,
+                int64_t K, int64_t ncols) {
+    const int bytes = type_bytes(type), qk = type_qk(type);
+    if (!bytes || K % qk) return -1;
+    const int64_t nblk = K / qk, nkb = K / 32;
+#pragma omp parallel for collapse(2) schedule(static)
+    for (int64_t c = 0; c < ncols; ++c)
+        for (int64_t r = 0; r < nrows; ++r) {
+            const uint8_t *row = W + r * nblk * bytes;
+            const uint8_t *xc = xq + c * nkb * 36;
+            double acc = 0.0;
+            for (int64_t b = 0; b < nblk; ++b) {
+                const uint8_t *blk = row + b * bytes;
+                if (type == T_Q8_0) {
+                    const uint8_t *ab = xc + b * 36;
+                    const int8_t *a = (const int8_t *)(ab + 4);
+                    int32_t s = 0;
+                    for (int e = 0; e < 32; ++e) s += (int32_t)(int8_t)blk[2 + e] * a[e];
+                    acc += (double)oracle_half_to_float(rd16(blk)) *
+                           (double)oracle_half_to_float(rd16(ab)) * (double)s;
+                    continue;
+                }
+                if (type == T_Q6_K) {
+                    const double d = oracle_half_to_float(rd16(blk + 208));
+                    double sb = 0.0;
+                    for (int j = 0; j < 8; ++j) {
+                        const uint8_t *ab = xc + (8 * b + j) * 36;
+                        const int8_t *a = (const int8_t *)(ab + 4);
+                        int32_t s0 = 0, s1 = 0;
+                        for (int e = 0; e < 16; ++e) s0 += q6k_quant(blk, j, e) * a[e];
+                        for (int e = 16; e < 32; ++e) s1 += q6k_quant(blk, j, e) * a[e];
+                        const int32_t sc0 = (int8_t)blk[192 + 2 * j], sc1 = (int8_t)blk[193 + 2 * j];
+                        sb += (double)oracle_half_to_float(rd16(ab)) *
+                              ((double)sc0 * (double)s0 + (double)sc1 * (double)s1);
+                    }
+                    acc += d * sb;
+                    continue;
+                }
+                const double d = oracle_half_to_float(rd16(blk));
+                const double dmin = oracle_half_to_float(rd16(blk + 2));
+                double sd = 0.0, sm = 0.0;
+                for (int j = 0; j < 8; ++j) {
+                    const uint8_t *ab = xc + (8 * b + j) * 36;
+                    const int8_t *a = (const int8_t *)(ab + 4);
+                    int32_t si = 0, sq = 0;
+                    for (int e = 0; e < 32; ++e) {
+                        si += (type == T_Q4_K ? q4k_quant(blk, j, e) : q5k_quant(blk, j, e)) * a[e];
+                        sq += a[e];
+                    }
+                    int sc, m;
+                    q4k_scale_min(blk + 4, j, &sc, &m);
+                    const double d8 = oracle_half_to_float(rd16(ab));
+                    sd += d8 * (double)sc * (double)si;
+                    sm += d8 * (double)m * (double)sq;
+                }
+                acc += d * sd - dmin * sm;
+            }
+            y[c * nrows + r] = acc;
+        }
+    return 0;
+}
+
+int oracle_num_threads(void) {
+#ifdef _OPENMP
+    return omp_get_max_threads();
+#else
+    return 1;
+#endif
+}
+
+void oracle_set_num_threads(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}

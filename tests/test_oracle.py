@@ -1,0 +1,141 @@
+"""The CPU oracle against the reference's pinned semantics (no GPU needed).
+
+Pins, in order of strength:
+  1. per-weight dequantisation == gguf-py gguf.quants.dequantize (the reference's declared
+     dependency), bit for bit, from committed fixtures and freshly generated blocks;
+  2. Q8_1 quantisation == gguf-py's Q8_0 rule (d = amax/127, round half away from zero)
+     up to the x/d vs x*(1/d) rounding difference, measured and bounded;
+  3. integer block sums and y are self-consistent with dequant(W) . dequant(Q8_1(x)).
+"""
+import numpy as np
+import pytest
+
+from kernel_anvil.quants import QUANT_TYPES, make_activation, make_weights
+from oracle import oracle
+
+TYPES = ["Q4_K", "Q5_K", "Q6_K", "Q8_0"]
+
+
+@pytest.mark.parametrize("qt", TYPES)
+def test_dequant_matches_gguf_fixture(golden_dir, qt):
+    f = np.load(golden_dir / f"dequant_{qt}.npz")
+    got = oracle.dequantize(qt, f["W"], int(f["nrows"]), int(f["K"]))
+    np.testing.assert_array_equal(got.view(np.uint32), f["dequant"].view(np.uint32))
+
+
+@pytest.mark.parametrize("qt", TYPES)
+@pytest.mark.parametrize("seed", [0, 3])
+def test_dequant_matches_gguf_live(qt, seed):
+    gguf = pytest.importorskip("gguf")
+    n, k = 16, 1024
+    W = make_weights(qt, n, k, seed=seed)
+    ref = gguf.quants.dequantize(W, getattr(gguf.GGMLQuantizationType, qt)).astype(np.float32)
+    got = oracle.dequantize(qt, W, n, k)
+    np.testing.assert_array_equal(got.view(np.uint32), ref.view(np.uint32))
+
+
+def test_half_conversion_matches_numpy():
+    rng = np.random.default_rng(0)
+    vals = np.concatenate([
+        rng.standard_normal(20000).astype(np.float32) * np.float32(10.0) ** rng.integers(-9, 5, 20000),
+        np.array([0.0, -0.0, 65504.0, 65519.99, 65520.0, 1e-8, 2.98e-8, 5.96e-8, 6.1e-5, 6.097e-5,
+                  np.inf, -np.inf, 1.0009765625, 1.00048828125, 1.00146484375], dtype=np.float32),
+    ])
+    with np.errstate(over="ignore"):
+        want = vals.astype(np.float16).view(np.uint16)
+    got = np.array([oracle.float_to_half_bits(float(v)) for v in vals], dtype=np.uint16)
+    np.testing.assert_array_equal(got, want)
+
+
+def test_q8_1_against_gguf_q8_0_rule(golden_dir):
+    f = np.load(golden_dir / "q8_0_gguf.npz")
+    x, q80 = f["x"], f["q8_0"]
+    xq = oracle.quantize_q8_1(x)
+    ncols, K = x.shape
+    b1 = xq.reshape(-1, 36)
+    b0 = q80.reshape(-1, 34)
+    # d: identical rule and rounding (fp32 amax/127 -> fp16)
+    np.testing.assert_array_equal(b1[:, 0:2], b0[:, 0:2])
+    # quants: x/d (llama.cpp CUDA) vs x*(1/d) (gguf-py) may differ by one ulp of rounding
+    diff = b1[:, 4:].view(np.int8).astype(int) - b0[:, 2:].view(np.int8).astype(int)
+    assert np.abs(diff).max() <= 1
+    assert np.count_nonzero(diff) <= 0.001 * diff.size
+    # the all-zero block (first block of column 1) quantises to d = 0, s = 0, q = 0
+    assert not b1[K // 32, :].any()
+
+
+def test_q8_1_sum_field_is_fp16_of_block_sum():
+    x = make_activation(4096, ncols=3, seed=9)
+    xq = oracle.quantize_q8_1(x).reshape(-1, 36)
+    s = xq[:, 2:4].copy().view(np.float16).astype(np.float64).ravel()
+    exact = x.reshape(-1, 32).astype(np.float64).sum(axis=1)
+    assert np.allclose(s, exact, rtol=2e-3, atol=1e-3)
+
+
+def test_q8_1_round_half_away_and_range():
+    # values that land exactly on .5 after division must round away from zero
+    x = np.zeros((1, 32), dtype=np.float32)
+    x[0, 0] = 127.0
+    x[0, 1] = 2.5
+    x[0, 2] = -2.5
+    x[0, 3] = -127.0
+    q = oracle.quantize_q8_1(x)[0, 4:].view(np.int8)
+    assert q[0] == 127 and q[3] == -127
+    assert q[1] == 3 and q[2] == -3
+
+
+@pytest.mark.parametrize("qt", TYPES)
+@pytest.mark.parametrize("ncols", [1, 3])
+def test_mmvq_equals_dequant_dot(qt, ncols):
+    n, k = 24, 1024
+    W = make_weights(qt, n, k, seed=2)
+    x = make_activation(k, ncols=ncols, seed=4)
+    xq = oracle.quantize_q8_1(x)
+    y = oracle.mmvq(qt, W, xq, n, k, ncols)
+    wd = oracle.dequantize(qt, W, n, k).astype(np.float64)
+    xd = oracle.dequantize_q8_1(xq, k).astype(np.float64)
+    ref = xd @ wd.T
+    assert oracle.max_rel_err(y, ref) < 1e-6  # fp32 rounding of the dequantised weights
+
+
+@pytest.mark.parametrize("qt", TYPES)
+def test_block_sums_reconstruct_y(qt):
+    """sum over sub-blocks of (scale terms x exact int sums) == oracle y."""
+    n, k = 6, 512
+    W = make_weights(qt, n, k, seed=5)
+    xq = oracle.quantize_q8_1(make_activation(k, seed=6))
+    sums = oracle.block_sums(qt, W, xq, n, k)[0].astype(np.float64)
+    xb = xq.reshape(-1, 36)
+    d8 = xb[:, 0:2].copy().view(np.float16).astype(np.float64).ravel()
+    qsum = xb[:, 4:].view(np.int8).astype(np.int64).sum(axis=1)
+    info = QUANT_TYPES[qt]
+    blocks = W.reshape(n, k // info.qk, info.block_size)
+    y = np.zeros(n)
+    for r in range(n):
+        for b in range(k // info.qk):
+            blk = blocks[r, b]
+            if qt == "Q8_0":
+                d = blk[0:2].copy().view(np.float16).astype(np.float64)[0]
+                y[r] += d * d8[b] * sums[r, b]
+            elif qt == "Q6_K":
+                d = blk[208:210].copy().view(np.float16).astype(np.float64)[0]
+                sc = blk[192:208].view(np.int8).astype(np.float64)
+                for g in range(16):
+                    y[r] += d * sc[g] * d8[8 * b + g // 2] * sums[r, 16 * b + g]
+            else:
+                d, dmin = blk[0:4].copy().view(np.float16).astype(np.float64)
+                s = blk[4:16].astype(int)
+                for j in range(8):
+                    if j < 4:
+                        sc, m = s[j] & 63, s[j + 4] & 63
+                    else:
+                        sc = (s[j + 4] & 0xF) | ((s[j - 4] >> 6) << 4)
+                        m = (s[j + 4] >> 4) | ((s[j] >> 6) << 4)
+                    kb = 8 * b + j
+                    y[r] += d * sc * d8[kb] * sums[r, kb] - dmin * m * d8[kb] * qsum[kb]
+    ref = oracle.mmvq(qt, W, xq, n, k)[0]
+    assert oracle.max_rel_err(y, ref) < 1e-12
+
+
+def test_oracle_threads_reported():
+    assert oracle.num_threads() >= 1
