@@ -164,14 +164,16 @@ static MmvqKernelFn kernel_for(int t, int ncols, int rpb, bool sums) {
     }
 }
 
-// Built-in B200 default when neither the caller nor the smithy table chose.
+// Built-in B200 default when neither the caller nor the smithy table chose: 4 warps, and
+// tiles of about 6 KB (rows_per_block = largest power of two with rpb * row_bytes <= 6 KB).
 static void default_config(int t, int nrows, int K, int ncols, int *nw, int *rpb) {
-    (void)t;
     (void)nrows;
-    (void)K;
     (void)ncols;
+    const int row_bytes = (K / mmvq_type_qk(t)) * mmvq_type_bytes(t);
+    int r = 1;
+    while (r < 8 && 2 * r * row_bytes <= 6144) r *= 2;
     *nw = 4;
-    *rpb = 2;
+    *rpb = r;
 }
 
 struct Plan {
@@ -210,10 +212,12 @@ static int plan_mmvq(int t, int nrows, int K, int ncols, int nwarps, int rpb, bo
     int nsm;
     if (int s = sm_count(dev, &nsm)) return s;
     const int row_bytes = (K / qk) * mmvq_type_bytes(t);
-    // Stages: about 32 KB of weights in flight per CTA, 2..8 stages, within shared memory.
+    // Each warp owns a ring of stages of rpb rows: aim for ~12 KB of weights per warp ring
+    // (2..8 stages); if the CTA does not fit in shared memory use fewer stages, then
+    // smaller tiles, then fewer warps.
     for (;;) {
         const int tile = rpb * row_bytes;
-        int ns = std::min(8, std::max(2, (32768 + tile - 1) / tile));
+        int ns = std::min(8, std::max(2, (12288 + tile - 1) / tile));
         MmvqSmem L = mmvq_smem_layout(t, K, ncols, rpb, nwarps, ns);
         while (L.total > kMaxSmem && ns > 1) L = mmvq_smem_layout(t, K, ncols, rpb, nwarps, --ns);
         if (L.total <= kMaxSmem) {
@@ -221,10 +225,14 @@ static int plan_mmvq(int t, int nrows, int K, int ncols, int nwarps, int rpb, bo
             p->smem = L.total;
             break;
         }
-        if (rpb == 1)
+        if (rpb > 1) {
+            rpb >>= 1;
+        } else if (nwarps > 1) {
+            nwarps >>= 1;
+        } else {
             return fail(ANVIL_ERR_UNSUPPORTED, "ncols_x=%d ncols_dst=%d does not fit in shared memory",
                         K, ncols);
-        rpb >>= 1;
+        }
     }
     p->fn = kernel_for(t, ncols, rpb, sums);
     if (!p->fn) return fail(ANVIL_ERR_UNSUPPORTED, "no kernel for ncols=%d rpb=%d", ncols, rpb);
@@ -233,8 +241,10 @@ static int plan_mmvq(int t, int nrows, int K, int ncols, int nwarps, int rpb, bo
     int occ;
     if (int s = prepare_fn(reinterpret_cast<const void *>(p->fn), dev, nwarps * 32, p->smem, &occ))
         return s;
+    // Persistent grid: every warp takes warp-tiles of rpb rows round-robin.
     const long ntiles = (long(nrows) + rpb - 1) / rpb;
-    p->grid = int(std::min<long>(ntiles, long(occ) * nsm));
+    const long ctas_needed = (ntiles + nwarps - 1) / nwarps;
+    p->grid = int(std::min<long>(ctas_needed, long(occ) * nsm));
     return ANVIL_OK;
 }
 

@@ -1,27 +1,28 @@
 // mmvq.cuh -- sm_100a MMVQ (quantized GEMV) kernel template.
 //
-// One CTA of 32*nwarps threads computes RPB consecutive output rows for NCOLS activation
-// columns, the launch geometry of llama.cpp's mul_mat_vec_q (grid ceil(N/rpb), block
-// (32, nwarps); docs/llama-cpp-kernel-analysis.md:107-123; kernel_anvil/hip_codegen.py:232)
-// so smithy's {nwarps, rows_per_block} keep their meaning.  What differs is how the
-// bytes move on a B200:
+// The reference's kernel is a CTA of (32, nwarps) threads computing rows_per_block rows,
+// with the warps splitting K and a shared-memory cross-warp reduction (grid ceil(N/rpb);
+// kernel_anvil/hip_codegen.py:228-333; docs/llama-cpp-kernel-analysis.md:107-148).  Here the
+// same two knobs keep their roles -- nwarps = warps per CTA, rows_per_block = rows per tile
+// -- but the bytes move the B200 way:
 //
-//   1. The RPB rows of W are one contiguous byte range.  One elected thread streams it
-//      into shared memory with a single bulk async copy (cp.async.bulk, the TMA engine's
-//      untiled form) completing on an mbarrier.  This is issued BEFORE the programmatic
-//      dependent launch wait, so inside a chain the weight stream of GEMV i+1 starts
-//      while GEMV i drains.  No register is spent holding weights in flight.
-//   2. After the wait, the Q8_1 activation (NCOLS * K/32 blocks) is staged to shared
-//      memory in a split layout: quant words in a 16-byte-chunk XOR swizzle (keeps the
-//      per-unit 16-byte reads bank-conflict free), fp32 scales, and int half-block sums
-//      of the quants (the Q4_K/Q5_K min term and the Q6_K -32 offset use them).
-//   3. Threads walk the row's "units" (64 weights of a K-quant super-block, or one Q8_0
-//      block) with stride 32*nwarps, exactly like the reference loop
-//      `for kbx = tid/(qi/vdr); kbx < blocks_per_row; kbx += blocks_per_iter`
-//      (kernel_anvil/hip_codegen.py:266-285), decode the unit once per row and do
-//      __dp4a int8 dots against every column.
-//   4. Partial sums are reduced with warp shuffles, then across warps in shared memory
-//      (kernel_anvil/hip_codegen.py:287-333), and lane 0 of the reduction writes y.
+//   1. Persistent CTAs (the host sizes the grid to what is resident).  Each warp is an
+//      autonomous consumer owning a ring of `nstages` tiles of RPB rows; tiles are dealt
+//      round-robin over all warps of the grid.  A tile is one contiguous byte range of W,
+//      streamed into shared memory by one bulk async copy (cp.async.bulk, the TMA
+//      engine's untiled form) issued by lane 0 and completing on the stage's mbarrier.
+//      The first copies go out BEFORE the programmatic-dependent-launch wait, so inside a
+//      chain the weight stream of GEMV i+1 starts while GEMV i drains.  No register is
+//      tied up by bytes in flight and no CTA-wide barrier sits in the tile loop.
+//   2. After the wait the Q8_1 activation (NCOLS * K/32 blocks) is staged once per CTA:
+//      quant words in a 16-byte-chunk XOR swizzle (bank-conflict-free per-unit reads),
+//      fp32 scales, and int half-block sums of the quants (the Q4_K/Q5_K min term and the
+//      Q6_K -32 offset use them).
+//   3. Lanes walk the row's "units" (64 weights of a K-quant super-block, or one Q8_0
+//      block) with stride 32, as the reference loop walks kbx with stride blocks_per_iter
+//      (kernel_anvil/hip_codegen.py:266-285); each unit is decoded once per row and dotted
+//      with __dp4a against every column.
+//   4. Each row's partial sums are reduced with warp shuffles and lane 0 writes y.
 //
 // With SUMS=true the same kernel writes its exact int32 block dots instead of y (the
 // parity probe behind anvil_mmvq_block_sums).
@@ -45,26 +46,32 @@ __host__ __device__ inline int mmvq_type_bytes(int qt) {
 }
 __host__ __device__ inline int mmvq_type_qk(int qt) { return qt == kTypeQ8_0 ? 32 : 256; }
 
+// Bytes of one column's swizzled activation quants: 2 chunks of 16 B per Q8_1 block,
+// padded to whole 8-chunk groups so the XOR swizzle never leaves the column.
+__host__ __device__ inline int act_col_bytes(int nkb) { return ((2 * nkb + 7) & ~7) * 16; }
+
 // Dynamic shared memory layout; identical on host (launch size) and device.
-// [nstages mbarriers][nstages weight stages][act quants][act scales][act sums][reduction]
+// [nwarps x nstages mbarriers][nwarps x nstages weight stages][act quants][act scales][act sums]
 __host__ __device__ inline MmvqSmem mmvq_smem_layout(int qt, int K, int ncols, int rpb,
                                                      int nwarps, int nstages) {
     const int row_bytes = (K / mmvq_type_qk(qt)) * mmvq_type_bytes(qt);
     const int nkb = K / 32;
     MmvqSmem L;
     L.bar = 0;
-    L.w = (8 * nstages + 15) & ~15;
+    L.w = (8 * nwarps * nstages + 15) & ~15;
     // +32 per stage: up to 15 bytes of head misalignment plus one word of funnel over-read.
     L.stage = ((rpb * row_bytes + 32) + 15) & ~15;
-    L.aq = L.w + nstages * L.stage;
-    L.ad = L.aq + ncols * nkb * 32;
+    L.aq = L.w + nwarps * nstages * L.stage;
+    L.ad = L.aq + ncols * act_col_bytes(nkb);
     L.as = (L.ad + ncols * nkb * 4 + 15) & ~15;
     L.red = L.as + ncols * nkb * 8;
-    L.total = L.red + nwarps * rpb * ncols * 4;
+    L.total = L.red;
     return L;
 }
 
-// Swizzled position of 16-byte activation chunk `ci` (two chunks per Q8_1 block).
+// Swizzled position of 16-byte activation chunk `ci` (two chunks per Q8_1 block).  The XOR
+// only flips bits 0-1 inside each aligned group of 8 chunks (the column is padded to whole
+// groups), so chunks 4u..4u+3 read by consecutive threads land in distinct bank quads.
 __device__ __forceinline__ int act_chunk(int ci) { return (ci & ~7) | ((ci & 7) ^ ((ci >> 3) & 3)); }
 
 struct ActUnit {          // one column's activation operands for one unit
@@ -295,32 +302,37 @@ __global__ void __launch_bounds__(kMaxWarps * 32)
     extern __shared__ __align__(16) uint8_t smem[];
     const int T = blockDim.x;
     const int tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
     const int nwarps = T >> 5;
     const int nkb = K >> 5;
+    const int acb = act_col_bytes(nkb);
     const int nblk = K / TR::qk;
     const int row_bytes = nblk * TR::bytes;
     const MmvqSmem L = mmvq_smem_layout(QT, K, NCOLS, RPB, nwarps, nstages);
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bar);
     uint8_t *aq = smem + L.aq;
     float *ad = reinterpret_cast<float *>(smem + L.ad);
     int2 *as = reinterpret_cast<int2 *>(smem + L.as);
-    float *red = reinterpret_cast<float *>(smem + L.red);
 
+    // Every warp is an independent consumer with its own ring of `nstages` row tiles.
+    // Warp-tiles of RPB rows are dealt round-robin over all warps of the grid.
     const int ntiles = (nrows + RPB - 1) / RPB;
-    const int my_tiles = blockIdx.x < ntiles ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    const int gwarp = blockIdx.x * nwarps + warp;
+    const int wstride = gridDim.x * nwarps;
+    const int my_tiles = gwarp < ntiles ? (ntiles - 1 - gwarp) / wstride + 1 : 0;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bar) + warp * nstages;
+    uint8_t *ring = smem + L.w + warp * nstages * L.stage;
 
-    // Issues the bulk copy of tile `tile` into stage `st` (elected thread only).  The
-    // 16-byte aligned interior of the row range goes through the copy engine; a range
-    // that does not start or end on 16 bytes leaves at most 15 + 15 bytes for the
-    // consumers to fetch with plain loads (fixup_tile).
+    // Bulk copy of tile `tile` into stage `st` (lane 0 only).  The 16-byte aligned
+    // interior of the row range goes through the copy engine; a range that does not start
+    // or end on 16 bytes leaves at most 15 + 15 bytes for plain loads (below).
     auto issue = [&](int tile, int st) {
         const uint8_t *src = W + size_t(tile) * RPB * size_t(row_bytes);
         const int rows = min(RPB, nrows - tile * RPB);
         const uintptr_t s = reinterpret_cast<uintptr_t>(src);
         const uintptr_t e = s + size_t(rows) * row_bytes;
         const uintptr_t s_al = (s + 15) & ~uintptr_t(15), e_al = e & ~uintptr_t(15);
-        uint8_t *dst = smem + L.w + st * L.stage + int(s & 15);
-        // Generic-proxy reads/writes of this stage happen before the copy engine rewrites it.
+        uint8_t *dst = ring + st * L.stage + int(s & 15);
+        // Generic-proxy reads of this stage happen before the copy engine rewrites it.
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         if (e_al > s_al) {
             mbar_arrive_expect_tx(&full[st], uint32_t(e_al - s_al));
@@ -332,10 +344,10 @@ __global__ void __launch_bounds__(kMaxWarps * 32)
     };
 
     // ---- 1. start streaming weights before waiting on the producer of xq -----------
-    if (tid == 0) {
+    if (lane == 0) {
         for (int st = 0; st < nstages; ++st) mbar_init(&full[st], 1);
         mbar_fence_init();
-        for (int k = 0; k < my_tiles && k < nstages; ++k) issue(blockIdx.x + k * gridDim.x, k);
+        for (int k = 0; k < my_tiles && k < nstages; ++k) issue(gwarp + k * wstride, k);
     }
     pdl_launch_dependents();
     pdl_wait();
@@ -352,7 +364,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32)
             } else {
                 const int c = blk / nkb, kb = blk - c * nkb;
                 const int ci = 2 * kb + ((w - 1) >> 2);
-                *reinterpret_cast<uint32_t *>(aq + c * nkb * 32 + act_chunk(ci) * 16 +
+                *reinterpret_cast<uint32_t *>(aq + c * acb + act_chunk(ci) * 16 +
                                               ((w - 1) & 3) * 4) = v;
             }
         }
@@ -362,7 +374,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32)
         const int blk = i >> 1, half = i & 1;
         const int c = blk / nkb, kb = blk - c * nkb;
         const uint4 q =
-            *reinterpret_cast<const uint4 *>(aq + c * nkb * 32 + act_chunk(2 * kb + half) * 16);
+            *reinterpret_cast<const uint4 *>(aq + c * acb + act_chunk(2 * kb + half) * 16);
         int sq = 0;
         sq = __dp4a(int(q.x), 0x01010101, sq);
         sq = __dp4a(int(q.y), 0x01010101, sq);
@@ -372,50 +384,48 @@ __global__ void __launch_bounds__(kMaxWarps * 32)
     }
     __syncthreads();
 
-    // ---- 3. thread -> (row lane, unit) mapping, fixed for all tiles ------------------
-    // U units per row.  With T >= U, G = T / U row lanes each own one unit column and
-    // every G-th row of a tile; with T < U a thread strides over units and owns all rows.
+    // ---- 3. lane -> (row group, unit) mapping, fixed for all tiles -------------------
+    // U units per row.  LPR lanes share a row (32, or the power of two >= U when a row
+    // has fewer than 32 units); the warp's 32/LPR lane groups take alternate rows.
     const int U = nblk * TR::units;
-    const int G = T >= U ? T / U : 1;
-    const int u_first = T >= U ? tid % U : tid;
-    const int u_step = T >= U ? U : T;
-    const int rlane = T >= U ? tid / U : 0;
+    int LPR = 32;
+    while (LPR > 1 && (LPR >> 1) >= U) LPR >>= 1;
+    const int RG = 32 / LPR;
+    const int ul = lane & (LPR - 1);
+    const int grp = lane / LPR;
     unsigned rowmask = 0;
-    if (rlane < G) {
 #pragma unroll
-        for (int i = 0; i < RPB; ++i)
-            if (i % G == rlane) rowmask |= 1u << i;
-    }
-    const int warp = tid >> 5, lane = tid & 31;
+    for (int i = 0; i < RPB; ++i)
+        if (i % RG == grp) rowmask |= 1u << i;
 
     for (int k = 0; k < my_tiles; ++k) {
-        const int tile = blockIdx.x + k * gridDim.x;
+        const int tile = gwarp + k * wstride;
         const int st = k % nstages;
         const int r0 = tile * RPB;
         const int rows = min(RPB, nrows - r0);
         const uint8_t *src = W + size_t(r0) * size_t(row_bytes);
         const uintptr_t s = reinterpret_cast<uintptr_t>(src);
         const uintptr_t e = s + size_t(rows) * row_bytes;
-        uint8_t *wrow0 = smem + L.w + st * L.stage + int(s & 15);
+        uint8_t *wrow0 = ring + st * L.stage + int(s & 15);
 
-        bool have_w = mbar_wait_bounded(&full[st], (k / nstages) & 1, kWaitLimitNs);
+        const bool have_w = mbar_wait_bounded(&full[st], (k / nstages) & 1, kWaitLimitNs);
         if (!have_w) {
             // The copy did not land in time: one more bounded wait so that it is not still
-            // writing this stage when the CTA moves on, then the tile is skipped.
+            // writing this stage when the warp moves on; the tile is then skipped.
             (void)mbar_wait_bounded(&full[st], (k / nstages) & 1, kWaitLimitNs);
         }
-        if ((s | e) & 15) {  // unaligned ends (uniform across the CTA)
+        if ((s | e) & 15) {  // unaligned ends: plain loads of at most 30 bytes
             const uintptr_t s_al = (s + 15) & ~uintptr_t(15), e_al = e & ~uintptr_t(15);
             if (e_al > s_al) {
                 const int nh = int(s_al - s), nt = int(e - e_al);
-                for (int i = tid; i < nh + nt; i += T) {
+                for (int i = lane; i < nh + nt; i += 32) {
                     const size_t off = i < nh ? size_t(i) : size_t(e_al - s) + size_t(i - nh);
                     wrow0[off] = src[off];
                 }
             } else {
-                for (int i = tid; i < int(e - s); i += T) wrow0[i] = src[i];
+                for (int i = lane; i < int(e - s); i += 32) wrow0[i] = src[i];
             }
-            __syncthreads();
+            __syncwarp();
         }
 
         float acc[RPB][NCOLS];
@@ -424,8 +434,8 @@ __global__ void __launch_bounds__(kMaxWarps * 32)
 #pragma unroll
             for (int c = 0; c < NCOLS; ++c) acc[i][c] = 0.f;
 
-        if (have_w && rowmask) {
-            for (int u = u_first; u < U; u += u_step) {
+        if (have_w) {
+            for (int u = ul; u < U; u += LPR) {
                 const int b = u / TR::units, ub = u - b * TR::units;
                 int kb0, kb1;
                 unit_blocks<QT>(b, ub, kb0, kb1);
@@ -442,8 +452,8 @@ __global__ void __launch_bounds__(kMaxWarps * 32)
                             if constexpr (NCOLS == 1) {
                                 a = a1;
                             } else {
-                                a = load_act<QT>(aq + c * nkb * 32, ad + c * nkb, as + c * nkb,
-                                                 kb0, kb1);
+                                a = load_act<QT>(aq + c * acb, ad + c * nkb, as + c * nkb, kb0,
+                                                 kb1);
                             }
                             int isum[4];
                             acc[i][c] += dot_unit<QT>(w, a, isum);
@@ -458,27 +468,18 @@ __global__ void __launch_bounds__(kMaxWarps * 32)
             }
         }
 
-        // ---- 4. reduction and store ---------------------------------------------------
+        // ---- 4. warp reduction and store (rows a lane group does not own add zeros) ---
 #pragma unroll
         for (int i = 0; i < RPB; ++i)
 #pragma unroll
             for (int c = 0; c < NCOLS; ++c) {
                 const float v = warp_sum(acc[i][c]);
-                if (lane == 0) red[(warp * RPB + i) * NCOLS + c] = v;
-            }
-        __syncthreads();
-        if constexpr (!SUMS) {
-            for (int o = tid; o < RPB * NCOLS; o += T) {
-                const int i = o / NCOLS, c = o - i * NCOLS;
-                if (i < rows) {
-                    float v = 0.f;
-                    for (int w = 0; w < nwarps; ++w) v += red[(w * RPB + i) * NCOLS + c];
-                    y[size_t(c) * nrows + r0 + i] = v;
+                if constexpr (!SUMS) {
+                    if (lane == 0 && i < rows) y[size_t(c) * nrows + r0 + i] = v;
                 }
             }
-        }
-        __syncthreads();  // stage `st` and `red` are free again
-        if (tid == 0 && k + nstages < my_tiles) issue(blockIdx.x + (k + nstages) * gridDim.x, st);
+        __syncwarp();  // every lane is done with stage `st`
+        if (lane == 0 && k + nstages < my_tiles) issue(tile + nstages * wstride, st);
     }
 }
 
