@@ -113,11 +113,19 @@ int anvil_mmvq_ex(int ggml_type, const void *W, const void *xq, float *y, int nr
                   int ncols_x, int ncols_dst, int nwarps, int rows_per_block, unsigned flags,
                   anvil_stream_t stream);
 
-/* Fused: quantize fp32 x to Q8_1 into the caller's xq scratch, then run anvil_mmvq.
- * Same contract as calling anvil_quantize_q8_1 then anvil_mmvq on one stream. */
+/* GEMV from fp32 activations: y = W . dequant(Q8_1(x)), bit-identical to calling
+ * anvil_quantize_q8_1 then anvil_mmvq.  When x is 16-byte aligned and its K * ncols
+ * fp32 values fit in shared memory next to the weight ring, one kernel quantises x in
+ * its prologue (every CTA, in shared memory) and xq is not touched; otherwise the two
+ * launches run and xq receives the Q8_1 blocks.  xq is scratch of
+ * ncols * (K/32) * 36 bytes whose contents are unspecified afterwards.
+ * anvil_mmvq_f32_ex takes anvil_flags (ANVIL_FLAG_PDL). */
 int anvil_mmvq_f32(int ggml_type, const void *W, const float *x, void *xq, float *y, int nrows,
                    int ncols_x, int ncols_dst, int nwarps, int rows_per_block,
                    anvil_stream_t stream);
+int anvil_mmvq_f32_ex(int ggml_type, const void *W, const float *x, void *xq, float *y,
+                      int nrows, int ncols_x, int ncols_dst, int nwarps, int rows_per_block,
+                      unsigned flags, anvil_stream_t stream);
 
 /* Reads and clears the device status words of the current device: the OR of
  * anvil_device_status flags set by kernels whose bounded waits gave up (0 = none),
@@ -155,6 +163,10 @@ int anvil_chain_add_quantize(anvil_chain *chain, const float *x, void *xq, int K
 int anvil_chain_add_mmvq(anvil_chain *chain, int ggml_type, const void *W, const void *xq,
                          float *y, int nrows, int ncols_x, int ncols_dst, int nwarps,
                          int rows_per_block);
+/* A GEMV step reading fp32 x (anvil_mmvq_f32 semantics: fused quantisation when it fits). */
+int anvil_chain_add_mmvq_f32(anvil_chain *chain, int ggml_type, const void *W, const float *x,
+                             void *xq, float *y, int nrows, int ncols_x, int ncols_dst,
+                             int nwarps, int rows_per_block);
 /* use_pdl: launch every step after the first with ANVIL_FLAG_PDL. */
 int anvil_chain_instantiate(anvil_chain *chain, int use_pdl, anvil_stream_t stream);
 /* Replays the graph (or, before instantiation, launches the steps one by one). */

@@ -154,12 +154,12 @@ static bool supported_type(int t) {
     return t == kTypeQ4_K || t == kTypeQ5_K || t == kTypeQ6_K || t == kTypeQ8_0;
 }
 
-static MmvqKernelFn kernel_for(int t, int ncols, int rpb, bool sums) {
+static MmvqKernelFn kernel_for(int t, int ncols, int rpb, int mode) {
     switch (t) {
-    case kTypeQ4_K: return mmvq_kernel_q4k(ncols, rpb, sums);
-    case kTypeQ5_K: return mmvq_kernel_q5k(ncols, rpb, sums);
-    case kTypeQ6_K: return mmvq_kernel_q6k(ncols, rpb, sums);
-    case kTypeQ8_0: return mmvq_kernel_q80(ncols, rpb, sums);
+    case kTypeQ4_K: return mmvq_kernel_q4k(ncols, rpb, mode);
+    case kTypeQ5_K: return mmvq_kernel_q5k(ncols, rpb, mode);
+    case kTypeQ6_K: return mmvq_kernel_q6k(ncols, rpb, mode);
+    case kTypeQ8_0: return mmvq_kernel_q80(ncols, rpb, mode);
     default: return nullptr;
     }
 }
@@ -178,12 +178,12 @@ static void default_config(int t, int nrows, int K, int ncols, int *nw, int *rpb
 
 struct Plan {
     MmvqKernelFn fn;
-    int nwarps, rpb, nstages, grid, smem;
+    int mode, nwarps, rpb, nstages, grid, smem;
 };
 
 static int round_rpb(int r) { return r >= 8 ? 8 : r >= 4 ? 4 : r >= 2 ? 2 : 1; }
 
-static int plan_mmvq(int t, int nrows, int K, int ncols, int nwarps, int rpb, bool sums,
+static int plan_mmvq(int t, int nrows, int K, int ncols, int nwarps, int rpb, int mode,
                      Plan *p) {
     if (!supported_type(t)) return fail(ANVIL_ERR_UNSUPPORTED, "ggml type %d has no MMVQ kernel", t);
     if (nrows <= 0 || K <= 0) return fail(ANVIL_ERR_INVALID, "nrows=%d ncols_x=%d", nrows, K);
@@ -218,8 +218,9 @@ static int plan_mmvq(int t, int nrows, int K, int ncols, int nwarps, int rpb, bo
     for (;;) {
         const int tile = rpb * row_bytes;
         int ns = std::min(8, std::max(2, (12288 + tile - 1) / tile));
-        MmvqSmem L = mmvq_smem_layout(t, K, ncols, rpb, nwarps, ns);
-        while (L.total > kMaxSmem && ns > 1) L = mmvq_smem_layout(t, K, ncols, rpb, nwarps, --ns);
+        MmvqSmem L = mmvq_smem_layout(t, K, ncols, rpb, nwarps, ns, mode);
+        while (L.total > kMaxSmem && ns > 1)
+            L = mmvq_smem_layout(t, K, ncols, rpb, nwarps, --ns, mode);
         if (L.total <= kMaxSmem) {
             p->nstages = ns;
             p->smem = L.total;
@@ -234,7 +235,8 @@ static int plan_mmvq(int t, int nrows, int K, int ncols, int nwarps, int rpb, bo
                         K, ncols);
         }
     }
-    p->fn = kernel_for(t, ncols, rpb, sums);
+    p->fn = kernel_for(t, ncols, rpb, mode);
+    p->mode = mode;
     if (!p->fn) return fail(ANVIL_ERR_UNSUPPORTED, "no kernel for ncols=%d rpb=%d", ncols, rpb);
     p->nwarps = nwarps;
     p->rpb = rpb;
@@ -248,7 +250,7 @@ static int plan_mmvq(int t, int nrows, int K, int ncols, int nwarps, int rpb, bo
     return ANVIL_OK;
 }
 
-static int launch_mmvq(const Plan &p, const void *W, const void *xq, float *y, int32_t *sums,
+static int launch_mmvq(const Plan &p, const void *W, const void *x, float *y, int32_t *sums,
                        int nrows, int K, unsigned flags, cudaStream_t stream) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(p.grid);
@@ -262,9 +264,15 @@ static int launch_mmvq(const Plan &p, const void *W, const void *xq, float *y, i
         cfg.attrs = attr;
         cfg.numAttrs = 1;
     }
-    cudaError_t e = cudaLaunchKernelEx(&cfg, p.fn, static_cast<const uint8_t *>(W),
-                                       static_cast<const uint8_t *>(xq), y, sums, nrows, K,
-                                       p.nstages);
+    MmvqArgs a;
+    a.W = static_cast<const uint8_t *>(W);
+    a.x = x;
+    a.y = y;
+    a.sums = sums;
+    a.nrows = nrows;
+    a.K = K;
+    a.nstages = p.nstages;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, p.fn, a);
     if (e != cudaSuccess) return cuda_fail(e, "mmvq launch");
     return ANVIL_OK;
 }
@@ -314,6 +322,7 @@ using namespace anvil;
 // ---------------------------------------------------------------------------------
 struct ChainStep {
     bool quantize;
+    bool fused;  // mmvq step reading fp32 x (fused quantisation, or quantise + mmvq)
     // quantize
     const float *x;
     void *xq;
@@ -374,7 +383,7 @@ int anvil_mmvq_plan(int ggml_type, int nrows, int ncols_x, int ncols_dst, int nw
                     int rows_per_block, int *out_nwarps, int *out_rpb, int *out_grid,
                     int *out_smem_bytes) {
     Plan p;
-    if (int s = plan_mmvq(ggml_type, nrows, ncols_x, ncols_dst, nwarps, rows_per_block, false, &p))
+    if (int s = plan_mmvq(ggml_type, nrows, ncols_x, ncols_dst, nwarps, rows_per_block, kModeQ81, &p))
         return s;
     if (out_nwarps) *out_nwarps = p.nwarps;
     if (out_rpb) *out_rpb = p.rpb;
@@ -388,7 +397,7 @@ int anvil_mmvq_ex(int ggml_type, const void *W, const void *xq, float *y, int nr
                   anvil_stream_t stream) {
     if (int s = check_mmvq_ptrs(ggml_type, W, xq, y)) return s;
     Plan p;
-    if (int s = plan_mmvq(ggml_type, nrows, ncols_x, ncols_dst, nwarps, rows_per_block, false, &p))
+    if (int s = plan_mmvq(ggml_type, nrows, ncols_x, ncols_dst, nwarps, rows_per_block, kModeQ81, &p))
         return s;
     return launch_mmvq(p, W, xq, y, nullptr, nrows, ncols_x, flags,
                        reinterpret_cast<cudaStream_t>(stream));
@@ -400,18 +409,40 @@ int anvil_mmvq(int ggml_type, const void *W, const void *xq, float *y, int nrows
                          0, stream);
 }
 
+// Plans the fused fp32 path; returns false (with no error) when it cannot be used.
+static bool plan_fused(int t, const float *x, int nrows, int K, int ncols, int nwarps, int rpb,
+                       Plan *p) {
+    if (reinterpret_cast<uintptr_t>(x) & 15) return false;
+    const std::string saved = t_last_error;
+    if (plan_mmvq(t, nrows, K, ncols, nwarps, rpb, kModeF32, p) != ANVIL_OK) {
+        t_last_error = saved;
+        return false;
+    }
+    return true;
+}
+
+int anvil_mmvq_f32_ex(int ggml_type, const void *W, const float *x, void *xq, float *y, int nrows,
+                      int ncols_x, int ncols_dst, int nwarps, int rows_per_block, unsigned flags,
+                      anvil_stream_t stream) {
+    if (int s = check_mmvq_ptrs(ggml_type, W, xq, y)) return s;
+    if (!x) return fail(ANVIL_ERR_INVALID, "null pointer argument");
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    Plan p;
+    if (plan_fused(ggml_type, x, nrows, ncols_x, ncols_dst, nwarps, rows_per_block, &p))
+        return launch_mmvq(p, W, x, y, nullptr, nrows, ncols_x, flags, st);
+    // Two launches: quantise into the caller's scratch, then the Q8_1 GEMV.  The GEMV's
+    // only producer is that quantiser, which never writes W, so it may prefetch early.
+    if (int s = plan_mmvq(ggml_type, nrows, ncols_x, ncols_dst, nwarps, rows_per_block, kModeQ81, &p))
+        return s;
+    if (int s = launch_quantize(x, xq, ncols_x, ncols_dst, flags, st)) return s;
+    return launch_mmvq(p, W, xq, y, nullptr, nrows, ncols_x, ANVIL_FLAG_PDL, st);
+}
+
 int anvil_mmvq_f32(int ggml_type, const void *W, const float *x, void *xq, float *y, int nrows,
                    int ncols_x, int ncols_dst, int nwarps, int rows_per_block,
                    anvil_stream_t stream) {
-    if (int s = check_mmvq_ptrs(ggml_type, W, xq, y)) return s;
-    Plan p;
-    if (int s = plan_mmvq(ggml_type, nrows, ncols_x, ncols_dst, nwarps, rows_per_block, false, &p))
-        return s;
-    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    if (int s = launch_quantize(x, xq, ncols_x, ncols_dst, 0, st)) return s;
-    // The GEMV's only producer is the quantiser above, which never writes W, so the
-    // weight stream may start before the quantiser finishes.
-    return launch_mmvq(p, W, xq, y, nullptr, nrows, ncols_x, ANVIL_FLAG_PDL, st);
+    return anvil_mmvq_f32_ex(ggml_type, W, x, xq, y, nrows, ncols_x, ncols_dst, nwarps,
+                             rows_per_block, 0, stream);
 }
 
 int anvil_mmvq_block_sums(int ggml_type, const void *W, const void *xq, int32_t *sums,
@@ -419,7 +450,7 @@ int anvil_mmvq_block_sums(int ggml_type, const void *W, const void *xq, int32_t 
                           anvil_stream_t stream) {
     if (int s = check_mmvq_ptrs(ggml_type, W, xq, sums)) return s;
     Plan p;
-    if (int s = plan_mmvq(ggml_type, nrows, ncols_x, ncols_dst, nwarps, rows_per_block, true, &p))
+    if (int s = plan_mmvq(ggml_type, nrows, ncols_x, ncols_dst, nwarps, rows_per_block, kModeSums, &p))
         return s;
     return launch_mmvq(p, W, xq, nullptr, sums, nrows, ncols_x, 0,
                        reinterpret_cast<cudaStream_t>(stream));
@@ -483,9 +514,40 @@ int anvil_chain_add_mmvq(anvil_chain *c, int ggml_type, const void *W, const voi
     s.ncols_dst = ncols_dst;
     s.nwarps = nwarps;
     s.rpb = rows_per_block;
-    if (int st = plan_mmvq(ggml_type, nrows, ncols_x, ncols_dst, nwarps, rows_per_block, false,
+    if (int st = plan_mmvq(ggml_type, nrows, ncols_x, ncols_dst, nwarps, rows_per_block, kModeQ81,
                            &s.plan))
         return st;
+    c->steps.push_back(s);
+    return ANVIL_OK;
+}
+
+int anvil_chain_add_mmvq_f32(anvil_chain *c, int ggml_type, const void *W, const float *x,
+                             void *xq, float *y, int nrows, int ncols_x, int ncols_dst, int nwarps,
+                             int rows_per_block) {
+    if (!c) return fail(ANVIL_ERR_INVALID, "null chain");
+    if (c->exec) return fail(ANVIL_ERR_INVALID, "chain already instantiated");
+    if (int s = check_mmvq_ptrs(ggml_type, W, xq, y)) return s;
+    if (!x) return fail(ANVIL_ERR_INVALID, "null pointer argument");
+    ChainStep s = {};
+    s.fused = true;
+    s.type = ggml_type;
+    s.W = W;
+    s.x = x;
+    s.xq = xq;
+    s.xqin = xq;
+    s.y = y;
+    s.nrows = nrows;
+    s.ncols_x = ncols_x;
+    s.K = ncols_x;
+    s.ncols = ncols_dst;
+    s.ncols_dst = ncols_dst;
+    s.nwarps = nwarps;
+    s.rpb = rows_per_block;
+    if (!plan_fused(ggml_type, x, nrows, ncols_x, ncols_dst, nwarps, rows_per_block, &s.plan)) {
+        if (int st = plan_mmvq(ggml_type, nrows, ncols_x, ncols_dst, nwarps, rows_per_block,
+                               kModeQ81, &s.plan))
+            return st;
+    }
     c->steps.push_back(s);
     return ANVIL_OK;
 }
@@ -494,9 +556,18 @@ static int run_steps(anvil_chain *c, bool use_pdl, cudaStream_t st) {
     for (size_t i = 0; i < c->steps.size(); ++i) {
         const ChainStep &s = c->steps[i];
         const unsigned flags = (use_pdl && i > 0) ? ANVIL_FLAG_PDL : 0u;
-        int r = s.quantize ? launch_quantize(s.x, s.xq, s.K, s.ncols, flags, st)
-                           : launch_mmvq(s.plan, s.W, s.xqin, s.y, nullptr, s.nrows, s.ncols_x,
-                                         flags, st);
+        int r;
+        if (s.quantize) {
+            r = launch_quantize(s.x, s.xq, s.K, s.ncols, flags, st);
+        } else if (s.fused && s.plan.mode == kModeF32) {
+            r = launch_mmvq(s.plan, s.W, s.x, s.y, nullptr, s.nrows, s.ncols_x, flags, st);
+        } else if (s.fused) {
+            r = launch_quantize(s.x, s.xq, s.K, s.ncols, flags, st);
+            if (!r) r = launch_mmvq(s.plan, s.W, s.xq, s.y, nullptr, s.nrows, s.ncols_x,
+                                    use_pdl ? ANVIL_FLAG_PDL : 0u, st);
+        } else {
+            r = launch_mmvq(s.plan, s.W, s.xqin, s.y, nullptr, s.nrows, s.ncols_x, flags, st);
+        }
         if (r) return r;
     }
     return ANVIL_OK;

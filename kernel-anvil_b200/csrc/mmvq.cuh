@@ -14,18 +14,23 @@
 //      The first copies go out BEFORE the programmatic-dependent-launch wait, so inside a
 //      chain the weight stream of GEMV i+1 starts while GEMV i drains.  No register is
 //      tied up by bytes in flight and no CTA-wide barrier sits in the tile loop.
-//   2. After the wait the Q8_1 activation (NCOLS * K/32 blocks) is staged once per CTA:
-//      quant words in a 16-byte-chunk XOR swizzle (bank-conflict-free per-unit reads),
-//      fp32 scales, and int half-block sums of the quants (the Q4_K/Q5_K min term and the
-//      Q6_K -32 offset use them).
-//   3. Lanes walk the row's "units" (64 weights of a K-quant super-block, or one Q8_0
-//      block) with stride 32, as the reference loop walks kbx with stride blocks_per_iter
-//      (kernel_anvil/hip_codegen.py:266-285); each unit is decoded once per row and dotted
-//      with __dp4a against every column.
-//   4. Each row's partial sums are reduced with warp shuffles and lane 0 writes y.
+//   2. After the wait the activation is staged once per CTA: either Q8_1 blocks from
+//      global memory, or fp32 values brought in by one bulk copy and quantised to Q8_1 in
+//      shared memory with the quantiser's exact arithmetic (the fused prologue that
+//      removes the separate quantize_q8_1 launch).  Quants are stored in 16-byte chunks
+//      with an XOR swizzle matched to the read pattern, plus fp32 scales d8, d8 * sum(q)
+//      and int half-block sums of q.
+//   3. Each lane owns whole weight blocks of its rows (lanes split a row's blocks the way
+//      the reference loop splits kbx, kernel_anvil/hip_codegen.py:266-285).  Per block the
+//      header is read once and the units (64-weight pairs of sub-blocks, or the single
+//      Q8_0 block) are walked in a compile-time sequence, so the 6-bit scale unpacking is
+//      a fixed bit extraction.  Dots are __dp4a; Q4_K high nibbles go through the
+//      unsigned x signed form on the unshifted byte (x16, removed exactly by a shift).
+//   4. Row sums are reduced with warp shuffles across the lanes sharing the row.
 //
-// With SUMS=true the same kernel writes its exact int32 block dots instead of y (the
-// parity probe behind anvil_mmvq_block_sums).
+// Modes: kModeQ81 (Q8_1 input), kModeF32 (fp32 input, fused quantisation), kModeSums
+// (Q8_1 input; the exact int32 block dots are written instead of y: the parity probe
+// behind anvil_mmvq_block_sums).
 #pragma once
 
 #include "anvil_common.cuh"
@@ -37,8 +42,20 @@ constexpr int kMaxCols = 8;        // MMVQ_MAX_BATCH_SIZE
 constexpr int kMaxSmem = 227 * 1024;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s bound on any mbarrier wait
 
+constexpr int kModeQ81 = 0;
+constexpr int kModeF32 = 1;
+constexpr int kModeSums = 2;
+
+struct MmvqArgs {
+    const uint8_t *W;   // weights, raw GGUF blocks, row-major
+    const void *x;      // Q8_1 blocks (kModeQ81 / kModeSums) or fp32 values (kModeF32)
+    float *y;           // ncols x nrows outputs
+    int32_t *sums;      // kModeSums output
+    int nrows, K, nstages;
+};
+
 struct MmvqSmem {
-    int bar, w, stage, aq, ad, as, red, total;
+    int bar, w, stage, xbuf, aq, ad, ads, as, total;
 };
 
 __host__ __device__ inline int mmvq_type_bytes(int qt) {
@@ -47,86 +64,44 @@ __host__ __device__ inline int mmvq_type_bytes(int qt) {
 __host__ __device__ inline int mmvq_type_qk(int qt) { return qt == kTypeQ8_0 ? 32 : 256; }
 
 // Bytes of one column's swizzled activation quants: 2 chunks of 16 B per Q8_1 block,
-// padded to whole 8-chunk groups so the XOR swizzle never leaves the column.
-__host__ __device__ inline int act_col_bytes(int nkb) { return ((2 * nkb + 7) & ~7) * 16; }
+// padded to whole 16-chunk groups so the XOR swizzle never leaves the column.
+__host__ __device__ inline int act_col_bytes(int nkb) { return ((2 * nkb + 15) & ~15) * 16; }
 
 // Dynamic shared memory layout; identical on host (launch size) and device.
-// [nwarps x nstages mbarriers][nwarps x nstages weight stages][act quants][act scales][act sums]
+// [mbarriers][nwarps x nstages weight stages][fp32 x (fused mode)][act quants][d8][d8*sum q][sums]
 __host__ __device__ inline MmvqSmem mmvq_smem_layout(int qt, int K, int ncols, int rpb,
-                                                     int nwarps, int nstages) {
+                                                     int nwarps, int nstages, int mode) {
     const int row_bytes = (K / mmvq_type_qk(qt)) * mmvq_type_bytes(qt);
     const int nkb = K / 32;
     MmvqSmem L;
     L.bar = 0;
-    L.w = (8 * nwarps * nstages + 15) & ~15;
+    L.w = (8 * (nwarps * nstages + 1) + 15) & ~15;
     // +32 per stage: up to 15 bytes of head misalignment plus one word of funnel over-read.
     L.stage = ((rpb * row_bytes + 32) + 15) & ~15;
-    L.aq = L.w + nwarps * nstages * L.stage;
+    L.xbuf = L.w + nwarps * nstages * L.stage;
+    L.aq = L.xbuf + (mode == kModeF32 ? ncols * K * 4 : 0);
     L.ad = L.aq + ncols * act_col_bytes(nkb);
-    L.as = (L.ad + ncols * nkb * 4 + 15) & ~15;
-    L.red = L.as + ncols * nkb * 8;
-    L.total = L.red;
+    L.ads = L.ad + ncols * nkb * 4;
+    L.as = (L.ads + ncols * nkb * 4 + 15) & ~15;
+    L.total = L.as + ncols * nkb * 8;
     return L;
 }
 
-// Swizzled position of 16-byte activation chunk `ci` (two chunks per Q8_1 block).  The XOR
-// only flips bits 0-1 inside each aligned group of 8 chunks (the column is padded to whole
-// groups), so chunks 4u..4u+3 read by consecutive threads land in distinct bank quads.
-__device__ __forceinline__ int act_chunk(int ci) { return (ci & ~7) | ((ci & 7) ^ ((ci >> 3) & 3)); }
-
-struct ActUnit {          // one column's activation operands for one unit
-    uint32_t a0[8], a1[8];  // quant words of Q8_1 blocks kb0 and kb1 (a1 unused for Q8_0)
-    float d0, d1;           // their fp16 scales, widened
-    int s0lo, s0hi, s1lo, s1hi;  // sums of the first / last 16 quants of each block
-};
-
-struct WUnit {            // one row's decoded weight operands for one unit
-    uint32_t q0[8], q1[8];  // weight bytes matching a0 / a1 (unsigned 0..63 or int8 for Q8_0)
-    int sc[4];              // K4/K5: sc0, sc1, m0, m1.  Q6_K: scale of groups 0..3
-    float d, dmin;
-};
-
-// Q8_1 blocks consumed by unit `ub` of super-block `b`.
+// Swizzled position of 16-byte activation chunk `ci` (chunks 2kb, 2kb+1 hold Q8_1 block kb).
+// K-quants: a quarter warp reads the same chunk of 8 consecutive super-blocks (chunk
+// stride 16), so the chunk's slot in its 128-byte line is XORed with bits 4-6 of ci.
+// Q8_0: a quarter warp reads chunk 2b+h of 8 consecutive blocks (stride 2), so the odd
+// line of each pair of lines is shifted by one slot.
 template <int QT>
-__device__ __forceinline__ void unit_blocks(int b, int ub, int &kb0, int &kb1) {
+__device__ __forceinline__ int act_chunk(int ci) {
     if constexpr (QT == kTypeQ8_0) {
-        kb0 = b;
-        kb1 = b;
-    } else if constexpr (QT == kTypeQ6_K) {
-        // unit (h, t): sub-blocks 4h+t (low nibble, qh shift 2t) and 4h+2+t (high nibble).
-        const int h = ub >> 1, t = ub & 1;
-        kb0 = 8 * b + 4 * h + t;
-        kb1 = kb0 + 2;
+        return ci ^ ((ci >> 3) & 1);
     } else {
-        // unit p: sub-blocks 2p (low nibble) and 2p+1 (high nibble).
-        kb0 = 8 * b + 2 * ub;
-        kb1 = kb0 + 1;
+        return ci ^ ((ci >> 4) & 7);
     }
 }
 
-__device__ __forceinline__ void load_act_block(const uint8_t *aq, const float *ad,
-                                               const int2 *as, int kb, uint32_t (&q)[8],
-                                               float &d, int &slo, int &shi) {
-    const uint4 c0 = *reinterpret_cast<const uint4 *>(aq + act_chunk(2 * kb) * 16);
-    const uint4 c1 = *reinterpret_cast<const uint4 *>(aq + act_chunk(2 * kb + 1) * 16);
-    q[0] = c0.x; q[1] = c0.y; q[2] = c0.z; q[3] = c0.w;
-    q[4] = c1.x; q[5] = c1.y; q[6] = c1.z; q[7] = c1.w;
-    d = ad[kb];
-    const int2 s = as[kb];
-    slo = s.x;
-    shi = s.y;
-}
-
-template <int QT>
-__device__ __forceinline__ ActUnit load_act(const uint8_t *aq, const float *ad, const int2 *as,
-                                            int kb0, int kb1) {
-    ActUnit a;
-    load_act_block(aq, ad, as, kb0, a.a0, a.d0, a.s0lo, a.s0hi);
-    if constexpr (QT != kTypeQ8_0) {
-        load_act_block(aq, ad, as, kb1, a.a1, a.d1, a.s1lo, a.s1hi);
-    }
-    return a;
-}
+// ---- small device helpers ------------------------------------------------------------
 
 // 32 bytes starting at a 2-byte aligned shared-memory address, as 8 little-endian words:
 // nine aligned word loads and a funnel shift by the address's byte offset.
@@ -143,138 +118,227 @@ __device__ __forceinline__ void lds32_a2(const uint8_t *p, uint32_t (&w)[8]) {
     }
 }
 
-__device__ __forceinline__ uint32_t lds16_a2(const uint8_t *p) {
+__device__ __forceinline__ uint32_t lds16(const uint8_t *p) {
     return *reinterpret_cast<const uint16_t *>(p);
 }
 
-// Six-bit scale/min pair of sub-blocks 2p and 2p+1 from the packed scales[12]
-// (gguf-py quants.py:478-501, the Q4_K.get_scale_min unpacking): for j < 4
-// sc = s[j] & 63, m = s[j+4] & 63; for j >= 4 sc = (s[j+4] & 15) | (s[j-4] >> 6) << 4,
-// m = (s[j+4] >> 4) | (s[j] >> 6) << 4.  Both bytes of a pair come out together.
-__device__ __forceinline__ void unpack_scale_pair(uint32_t s0, uint32_t s1, uint32_t s2, int p,
-                                                  int (&sc)[4]) {
-    const uint32_t sh = (p & 1) * 16;
-    const uint32_t b0 = (s0 >> sh) & 0xFFFFu, b1 = (s1 >> sh) & 0xFFFFu, b2 = (s2 >> sh) & 0xFFFFu;
-    uint32_t scp, mp;
-    if (p < 2) {
-        scp = b0 & 0x3F3Fu;
-        mp = b1 & 0x3F3Fu;
-    } else {
-        scp = (b2 & 0x0F0Fu) | ((b0 >> 2) & 0x3030u);
-        mp = ((b2 >> 4) & 0x0F0Fu) | ((b1 >> 2) & 0x3030u);
+__device__ __forceinline__ void lds32_a16(const uint8_t *p, uint32_t (&w)[8]) {
+    const uint4 a = *reinterpret_cast<const uint4 *>(p);
+    const uint4 b = *reinterpret_cast<const uint4 *>(p + 16);
+    w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w;
+    w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
+}
+
+// Unsigned bytes of `a` dotted with signed bytes of `b`, plus c (PTX dp4a.u32.s32).
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// One Q8_1 activation block as seen by a dot: 32 quants, d8, d8 * sum(q), half sums.
+struct ActBlk {
+    uint32_t q[8];
+    float d, ds;
+    int slo, shi;
+};
+
+struct ActView {  // one column's staged activation
+    const uint8_t *aq;
+    const float *ad, *ads;
+    const int2 *as;
+};
+
+template <int QT>
+__device__ __forceinline__ void load_act(const ActView &v, int kb, ActBlk &a) {
+    const uint4 c0 = *reinterpret_cast<const uint4 *>(v.aq + act_chunk<QT>(2 * kb) * 16);
+    const uint4 c1 = *reinterpret_cast<const uint4 *>(v.aq + act_chunk<QT>(2 * kb + 1) * 16);
+    a.q[0] = c0.x; a.q[1] = c0.y; a.q[2] = c0.z; a.q[3] = c0.w;
+    a.q[4] = c1.x; a.q[5] = c1.y; a.q[6] = c1.z; a.q[7] = c1.w;
+    a.d = v.ad[kb];
+    a.ds = 0.f;
+    a.slo = a.shi = 0;
+    if constexpr (QT == kTypeQ4_K || QT == kTypeQ5_K) a.ds = v.ads[kb];
+    if constexpr (QT == kTypeQ6_K) {
+        const int2 s = v.as[kb];
+        a.slo = s.x;
+        a.shi = s.y;
     }
-    sc[0] = scp & 0xFF;
-    sc[1] = scp >> 8;
-    sc[2] = mp & 0xFF;
-    sc[3] = mp >> 8;
+}
+
+// ---- per-type block decode and dot ------------------------------------------------------
+//
+// A lane handling (row, block) first reads the block header (BlkHdr), then for each unit U
+// (compile time) decodes the unit's weight bytes and dots them with the unit's activation
+// blocks.  Units: Q4_K/Q5_K U = sub-block pair (2U, 2U+1); Q6_K U = (h, t) = (U>>1, U&1),
+// sub-blocks 4h+t and 4h+2+t; Q8_0 one unit, the block itself.
+
+struct BlkHdr {
+    float d, dmin;
+    uint32_t s0, s1, s2;  // K4/K5 packed scales[12]
+};
+
+template <int QT> struct Units { static constexpr int n = 4; };
+template <> struct Units<kTypeQ8_0> { static constexpr int n = 1; };
+
+// Q8_1 blocks consumed by unit U of super-block b.
+template <int QT, int U>
+__device__ __forceinline__ void unit_kb(int b, int &kb0, int &kb1) {
+    if constexpr (QT == kTypeQ8_0) {
+        kb0 = b;
+        kb1 = b;
+    } else if constexpr (QT == kTypeQ6_K) {
+        kb0 = 8 * b + 4 * (U >> 1) + (U & 1);
+        kb1 = kb0 + 2;
+    } else {
+        kb0 = 8 * b + 2 * U;
+        kb1 = kb0 + 1;
+    }
 }
 
 template <int QT>
-__device__ __forceinline__ WUnit decode_unit(const uint8_t *blk, int ub) {
-    WUnit w;
+__device__ __forceinline__ BlkHdr load_hdr(const uint8_t *blk) {
+    BlkHdr h;
+    h.dmin = 0.f;
+    h.s0 = h.s1 = h.s2 = 0;
     if constexpr (QT == kTypeQ4_K || QT == kTypeQ5_K) {
-        const uint4 h = *reinterpret_cast<const uint4 *>(blk);
-        const int qs_off = (QT == kTypeQ4_K ? 16 : 48) + 32 * ub;
-        const uint4 qa = *reinterpret_cast<const uint4 *>(blk + qs_off);
-        const uint4 qb = *reinterpret_cast<const uint4 *>(blk + qs_off + 16);
-        const uint32_t v[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-        if constexpr (QT == kTypeQ4_K) {
+        const uint4 v = *reinterpret_cast<const uint4 *>(blk);
+        h.d = h2f(v.x);
+        h.dmin = h2f(v.x >> 16);
+        h.s0 = v.y;
+        h.s1 = v.z;
+        h.s2 = v.w;
+    } else if constexpr (QT == kTypeQ6_K) {
+        h.d = h2f(lds16(blk + 208));
+    } else {
+        h.d = h2f(lds16(blk));
+    }
+    return h;
+}
+
+// Six-bit scale and min of sub-blocks 2U and 2U+1 (gguf-py quants.py:478-501,
+// Q4_K.get_scale_min): for j < 4 sc = s[j] & 63, m = s[j+4] & 63; for j >= 4
+// sc = (s[j+4] & 15) | (s[j-4] >> 6) << 4, m = (s[j+4] >> 4) | (s[j] >> 6) << 4.
+template <int U>
+__device__ __forceinline__ void scale_min_pair(const BlkHdr &h, int &sc0, int &sc1, int &m0,
+                                               int &m1) {
+    constexpr int sh = (U & 1) * 16;  // bytes 2U%4 and 2U%4+1 of each word
+    if constexpr (U < 2) {
+        const uint32_t scp = (h.s0 >> sh) & 0x3F3Fu, mp = (h.s1 >> sh) & 0x3F3Fu;
+        sc0 = scp & 0xFF;
+        sc1 = scp >> 8;
+        m0 = mp & 0xFF;
+        m1 = mp >> 8;
+    } else {
+        const uint32_t b0 = h.s0 >> sh, b1 = h.s1 >> sh, b2 = h.s2 >> sh;
+        const uint32_t scp = (b2 & 0x0F0Fu) | ((b0 >> 2) & 0x3030u);
+        const uint32_t mp = ((b2 >> 4) & 0x0F0Fu) | ((b1 >> 2) & 0x3030u);
+        sc0 = scp & 0xFF;
+        sc1 = (scp >> 8) & 0xFF;
+        m0 = mp & 0xFF;
+        m1 = (mp >> 8) & 0xFF;
+    }
+}
+
+// Decoded weight bytes of one unit of one row (q0 pairs with Q8_1 block kb0, q1 with kb1).
+struct WBytes {
+    uint32_t q0[8], q1[8];
+};
+
+template <int QT, int U>
+__device__ __forceinline__ void load_unit(const uint8_t *blk, WBytes &w) {
+    if constexpr (QT == kTypeQ4_K) {
+        uint32_t v[8];
+        lds32_a16(blk + 16 + 32 * U, v);
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                w.q0[k] = v[k] & 0x0F0F0F0Fu;
-                w.q1[k] = (v[k] >> 4) & 0x0F0F0F0Fu;
-            }
-        } else {
-            // fifth bit of weight e of sub-block j is bit j of qh[e] (gguf-py quants.py:540-547)
-            const uint4 ha = *reinterpret_cast<const uint4 *>(blk + 16);
-            const uint4 hb = *reinterpret_cast<const uint4 *>(blk + 32);
-            const uint32_t qh[8] = {ha.x, ha.y, ha.z, ha.w, hb.x, hb.y, hb.z, hb.w};
-            const int j0 = 2 * ub;
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                w.q0[k] = (v[k] & 0x0F0F0F0Fu) | (((qh[k] >> j0) & 0x01010101u) << 4);
-                w.q1[k] = ((v[k] >> 4) & 0x0F0F0F0Fu) | (((qh[k] >> (j0 + 1)) & 0x01010101u) << 4);
-            }
+        for (int k = 0; k < 8; ++k) {
+            w.q0[k] = v[k] & 0x0F0F0F0Fu;
+            w.q1[k] = v[k] & 0xF0F0F0F0u;  // high nibbles in place (x16)
         }
-        unpack_scale_pair(h.y, h.z, h.w, ub, w.sc);
-        w.d = h2f(h.x);
-        w.dmin = h2f(h.x >> 16);
+    } else if constexpr (QT == kTypeQ5_K) {
+        uint32_t v[8], qh[8];
+        lds32_a16(blk + 48 + 32 * U, v);
+        lds32_a16(blk + 16, qh);  // fifth bit of weight e of sub-block j = bit j of qh[e]
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            w.q0[k] = (v[k] & 0x0F0F0F0Fu) | (((qh[k] >> (2 * U)) & 0x01010101u) << 4);
+            w.q1[k] = ((v[k] >> 4) & 0x0F0F0F0Fu) | (((qh[k] >> (2 * U + 1)) & 0x01010101u) << 4);
+        }
     } else if constexpr (QT == kTypeQ6_K) {
         // unit (h, t): ql bytes [64h+32t, +32) hold sub-block 4h+t (low nibbles) and
         // 4h+2+t (high nibbles); qh bytes [32h, +32) hold their top two bits at shifts
         // 2t and 4+2t (gguf-py quants.py:563-569).
-        const int h = ub >> 1, t = ub & 1;
+        constexpr int h = U >> 1, t = U & 1;
         uint32_t ql[8], qh[8];
         lds32_a2(blk + 64 * h + 32 * t, ql);
         lds32_a2(blk + 128 + 32 * h, qh);
-        const int s0 = 2 * t, s1 = 4 + 2 * t;
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
-            w.q0[k] = (ql[k] & 0x0F0F0F0Fu) | (((qh[k] >> s0) & 0x03030303u) << 4);
-            w.q1[k] = ((ql[k] >> 4) & 0x0F0F0F0Fu) | (((qh[k] >> s1) & 0x03030303u) << 4);
+            w.q0[k] = (ql[k] & 0x0F0F0F0Fu) | (((qh[k] >> (2 * t)) & 0x03030303u) << 4);
+            w.q1[k] = ((ql[k] >> 4) & 0x0F0F0F0Fu) | ((qh[k] >> (2 * t)) & 0x30303030u);
         }
-        const int j0 = 4 * h + t, j1 = j0 + 2;
-        const uint32_t sc0 = lds16_a2(blk + 192 + 2 * j0);
-        const uint32_t sc1 = lds16_a2(blk + 192 + 2 * j1);
-        w.sc[0] = int(int8_t(sc0 & 0xFF));
-        w.sc[1] = int(int8_t(sc0 >> 8));
-        w.sc[2] = int(int8_t(sc1 & 0xFF));
-        w.sc[3] = int(int8_t(sc1 >> 8));
-        w.d = h2f(lds16_a2(blk + 208));
-        w.dmin = 0.f;
     } else {  // Q8_0
         lds32_a2(blk + 2, w.q0);
-        w.d = h2f(lds16_a2(blk));
-        w.dmin = 0.f;
     }
-    return w;
 }
 
-// Float contribution of one decoded weight unit against one column; the exact int32
-// block dots go to `isum` (K4/K5/Q8_0: isum[0..1] per 32; Q6_K: isum[0..3] per 16).
-template <int QT>
-__device__ __forceinline__ float dot_unit(const WUnit &w, const ActUnit &a, int (&isum)[4]) {
+// Float contribution of one unit against one column; exact int32 block dots to `isum`
+// (K4/K5/Q8_0: isum[0..1], one per 32; Q6_K: isum[0..3], one per 16).
+template <int QT, int U>
+__device__ __forceinline__ float dot_unit(const uint8_t *blk, const BlkHdr &h, const WBytes &w,
+                                          const ActBlk &a0, const ActBlk &a1, int (&isum)[4]) {
     if constexpr (QT == kTypeQ4_K || QT == kTypeQ5_K) {
         int i0 = 0, i1 = 0;
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
-            i0 = __dp4a(int(w.q0[k]), int(a.a0[k]), i0);
-            i1 = __dp4a(int(w.q1[k]), int(a.a1[k]), i1);
+            i0 = __dp4a(int(w.q0[k]), int(a0.q[k]), i0);
+            if constexpr (QT == kTypeQ4_K) {
+                i1 = dp4a_us(w.q1[k], a1.q[k], i1);
+            } else {
+                i1 = __dp4a(int(w.q1[k]), int(a1.q[k]), i1);
+            }
         }
+        if constexpr (QT == kTypeQ4_K) i1 >>= 4;  // exact: the sum is 16 x the nibble dot
         isum[0] = i0;
         isum[1] = i1;
-        // llama.cpp vec_dot_q4_K_q8_1_impl_vmmq structure (docs/llama-cpp-kernel-analysis.md:200-224):
-        // d * sum_j d8_j * (sumi_j * sc_j) - dmin * sum_j d8_j * (sumq_j * m_j)
-        const float fd = a.d0 * float(i0 * w.sc[0]) + a.d1 * float(i1 * w.sc[1]);
-        const float fm = a.d0 * float((a.s0lo + a.s0hi) * w.sc[2]) +
-                         a.d1 * float((a.s1lo + a.s1hi) * w.sc[3]);
-        return w.d * fd - w.dmin * fm;
+        int sc0, sc1, m0, m1;
+        scale_min_pair<U>(h, sc0, sc1, m0, m1);
+        // d * sum_j d8_j * (sumi_j * sc_j) - dmin * sum_j m_j * (d8_j * sumq_j)
+        // (vec_dot_q4_K_q8_1 structure, docs/llama-cpp-kernel-analysis.md:200-224)
+        const float fd = a0.d * float(i0 * sc0) + a1.d * float(i1 * sc1);
+        const float fm = a0.ds * float(m0) + a1.ds * float(m1);
+        return h.d * fd - h.dmin * fm;
     } else if constexpr (QT == kTypeQ6_K) {
+        constexpr int h6 = U >> 1, t = U & 1;
         int p00 = 0, p01 = 0, p10 = 0, p11 = 0;
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-            p00 = __dp4a(int(w.q0[k]), int(a.a0[k]), p00);
-            p01 = __dp4a(int(w.q0[k + 4]), int(a.a0[k + 4]), p01);
-            p10 = __dp4a(int(w.q1[k]), int(a.a1[k]), p10);
-            p11 = __dp4a(int(w.q1[k + 4]), int(a.a1[k + 4]), p11);
+            p00 = __dp4a(int(w.q0[k]), int(a0.q[k]), p00);
+            p01 = __dp4a(int(w.q0[k + 4]), int(a0.q[k + 4]), p01);
+            p10 = __dp4a(int(w.q1[k]), int(a1.q[k]), p10);
+            p11 = __dp4a(int(w.q1[k + 4]), int(a1.q[k + 4]), p11);
         }
-        // q - 32 applied through the activation sums: sum (q-32) a = sum q a - 32 sum a.
-        p00 -= 32 * a.s0lo;
-        p01 -= 32 * a.s0hi;
-        p10 -= 32 * a.s1lo;
-        p11 -= 32 * a.s1hi;
+        // q - 32 through the activation sums: sum (q-32) a = sum q a - 32 sum a.
+        p00 -= 32 * a0.slo;
+        p01 -= 32 * a0.shi;
+        p10 -= 32 * a1.slo;
+        p11 -= 32 * a1.shi;
         isum[0] = p00;
         isum[1] = p01;
         isum[2] = p10;
         isum[3] = p11;
-        return w.d * (a.d0 * float(p00 * w.sc[0] + p01 * w.sc[1]) +
-                      a.d1 * float(p10 * w.sc[2] + p11 * w.sc[3]));
+        constexpr int j0 = 4 * h6 + t, j1 = j0 + 2;
+        const uint32_t sc0 = lds16(blk + 192 + 2 * j0);
+        const uint32_t sc1 = lds16(blk + 192 + 2 * j1);
+        const int s00 = int(int8_t(sc0 & 0xFF)), s01 = int(int8_t(sc0 >> 8));
+        const int s10 = int(int8_t(sc1 & 0xFF)), s11 = int(int8_t(sc1 >> 8));
+        return h.d * (a0.d * float(p00 * s00 + p01 * s01) + a1.d * float(p10 * s10 + p11 * s11));
     } else {
         int i0 = 0;
 #pragma unroll
-        for (int k = 0; k < 8; ++k) i0 = __dp4a(int(w.q0[k]), int(a.a0[k]), i0);
+        for (int k = 0; k < 8; ++k) i0 = __dp4a(int(w.q0[k]), int(a0.q[k]), i0);
         isum[0] = i0;
-        return w.d * (a.d0 * float(i0));
+        return h.d * (a0.d * float(i0));
     }
 }
 
@@ -293,33 +357,129 @@ __device__ __forceinline__ void store_sums(int32_t *srow, int kb0, int kb1, cons
     }
 }
 
-template <int QT, int NCOLS, int RPB, bool SUMS>
-__global__ void __launch_bounds__(kMaxWarps * 32)
-    mmvq_kernel(const uint8_t *__restrict__ W, const uint8_t *__restrict__ xq,
-                float *__restrict__ y, int32_t *__restrict__ sums, int nrows, int K,
-                int nstages) {
+// Lanes per row (power of two) that keeps the most lanes busy: LB lanes split a row's
+// nblk blocks, 32/LB lane groups take alternate rows of a tile of rpb rows.
+__device__ __forceinline__ int choose_lanes_per_row(int nblk, int rpb) {
+    int best = 32;
+    float best_u = -1.f;
+    for (int lb = 32; lb >= 1; lb >>= 1) {
+        const int rg = 32 / lb;
+        const int per_lane = (nblk + lb - 1) / lb;
+        const float u = float(nblk) / float(lb * per_lane) * fminf(1.f, float(rpb) / float(rg));
+        if (u > best_u + 1e-6f) {
+            best_u = u;
+            best = lb;
+        }
+    }
+    return best;
+}
+
+// Per-tile context shared by the unit steps of one block.
+template <int RPB, int NCOLS>
+struct TileCtx {
+    const uint8_t *wrow0;
+    int row_bytes, nrows, r0, K, nkb, acb;
+    unsigned live;  // rows of the tile this lane computes
+    const uint8_t *aq;
+    const float *ad, *ads;
+    const int2 *as;
+    int32_t *sums;
+};
+
+// One compile-time unit U of block b for every live row and column.
+template <int QT, int NCOLS, int RPB, int MODE, int U>
+__device__ __forceinline__ void unit_step(const TileCtx<RPB, NCOLS> &t, int b,
+                                          const BlkHdr (&hdr)[RPB], float (&acc)[RPB][NCOLS]) {
+    using TR = QTraits<QT>;
+    int kb0, kb1;
+    unit_kb<QT, U>(b, kb0, kb1);
+    ActBlk a0, a1;
+    if constexpr (NCOLS == 1) {
+        const ActView v{t.aq, t.ad, t.ads, t.as};
+        load_act<QT>(v, kb0, a0);
+        if constexpr (QT != kTypeQ8_0) load_act<QT>(v, kb1, a1);
+    }
+#pragma unroll
+    for (int i = 0; i < RPB; ++i) {
+        if ((t.live >> i) & 1u) {
+            const uint8_t *blk = t.wrow0 + i * t.row_bytes + b * TR::bytes;
+            WBytes wb;
+            load_unit<QT, U>(blk, wb);
+#pragma unroll
+            for (int c = 0; c < NCOLS; ++c) {
+                if constexpr (NCOLS > 1) {
+                    const ActView v{t.aq + c * t.acb, t.ad + c * t.nkb, t.ads + c * t.nkb,
+                                    t.as + c * t.nkb};
+                    load_act<QT>(v, kb0, a0);
+                    if constexpr (QT != kTypeQ8_0) load_act<QT>(v, kb1, a1);
+                }
+                int isum[4];
+                acc[i][c] += dot_unit<QT, U>(blk, hdr[i], wb, a0, QT == kTypeQ8_0 ? a0 : a1, isum);
+                if constexpr (MODE == kModeSums) {
+                    const int nsub = QT == kTypeQ6_K ? t.K / 16 : t.K / 32;
+                    store_sums<QT>(t.sums + (size_t(c) * t.nrows + t.r0 + i) * nsub, kb0, kb1, isum);
+                }
+            }
+        }
+    }
+}
+
+// ---- the Q8_1 quantisation of one 32-value block by one warp ------------------------------
+// Semantics of llama.cpp's CUDA quantize_q8_1: amax and sum by xor-butterfly warp
+// reductions, d = amax / 127, q = roundf(x / d) (0 when amax == 0); IEEE division.
+struct Q81Lane {
+    int q;       // this lane's quant
+    float d;     // fp32 scale (stored as fp16)
+    float sum;   // block sum of x (stored as fp16)
+};
+
+__device__ __forceinline__ Q81Lane quantize_lane(float xi) {
+    Q81Lane r;
+    const float amax = warp_max(fabsf(xi));
+    r.sum = warp_sum(xi);
+    r.d = __fdiv_rn(amax, 127.0f);
+    r.q = amax == 0.0f ? 0 : int(roundf(__fdiv_rn(xi, r.d)));
+    return r;
+}
+
+// Packs lane quants into words: lanes 4w..4w+3 -> word w, returned on lane 4w.
+__device__ __forceinline__ uint32_t pack_quants(int q) {
+    const uint32_t b = uint32_t(q) & 0xFFu;
+    const uint32_t b1 = __shfl_down_sync(0xffffffffu, b, 1);
+    const uint32_t b2 = __shfl_down_sync(0xffffffffu, b, 2);
+    const uint32_t b3 = __shfl_down_sync(0xffffffffu, b, 3);
+    return b | (b1 << 8) | (b2 << 16) | (b3 << 24);
+}
+
+// ---- the kernel --------------------------------------------------------------------------
+
+template <int QT, int NCOLS, int RPB, int MODE>
+__global__ void __launch_bounds__(kMaxWarps * 32, 1) mmvq_kernel(const MmvqArgs args) {
     using TR = QTraits<QT>;
     extern __shared__ __align__(16) uint8_t smem[];
     const int T = blockDim.x;
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
     const int nwarps = T >> 5;
+    const int K = args.K, nrows = args.nrows, nstages = args.nstages;
     const int nkb = K >> 5;
     const int acb = act_col_bytes(nkb);
     const int nblk = K / TR::qk;
     const int row_bytes = nblk * TR::bytes;
-    const MmvqSmem L = mmvq_smem_layout(QT, K, NCOLS, RPB, nwarps, nstages);
+    const MmvqSmem L = mmvq_smem_layout(QT, K, NCOLS, RPB, nwarps, nstages, MODE);
     uint8_t *aq = smem + L.aq;
     float *ad = reinterpret_cast<float *>(smem + L.ad);
+    float *ads = reinterpret_cast<float *>(smem + L.ads);
     int2 *as = reinterpret_cast<int2 *>(smem + L.as);
+    const uint8_t *W = args.W;
 
-    // Every warp is an independent consumer with its own ring of `nstages` row tiles.
     // Warp-tiles of RPB rows are dealt round-robin over all warps of the grid.
     const int ntiles = (nrows + RPB - 1) / RPB;
     const int gwarp = blockIdx.x * nwarps + warp;
     const int wstride = gridDim.x * nwarps;
     const int my_tiles = gwarp < ntiles ? (ntiles - 1 - gwarp) / wstride + 1 : 0;
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bar) + warp * nstages;
+    uint64_t *xbar = reinterpret_cast<uint64_t *>(smem + L.bar) + nwarps * nstages;
     uint8_t *ring = smem + L.w + warp * nstages * L.stage;
 
     // Bulk copy of tile `tile` into stage `st` (lane 0 only).  The 16-byte aligned
@@ -343,56 +503,91 @@ __global__ void __launch_bounds__(kMaxWarps * 32)
         }
     };
 
-    // ---- 1. start streaming weights before waiting on the producer of xq -----------
+    // ---- 1. start streaming weights before waiting on the producer of x ------------
     if (lane == 0) {
         for (int st = 0; st < nstages; ++st) mbar_init(&full[st], 1);
+        if (MODE == kModeF32 && warp == 0) mbar_init(xbar, 1);
         mbar_fence_init();
         for (int k = 0; k < my_tiles && k < nstages; ++k) issue(gwarp + k * wstride, k);
     }
     pdl_launch_dependents();
     pdl_wait();
 
-    // ---- 2. stage the Q8_1 activation once per CTA -----------------------------------
-    {
-        const uint32_t *xw = reinterpret_cast<const uint32_t *>(xq);
+    // ---- 2. stage the activation once per CTA ------------------------------------------
+    if constexpr (MODE == kModeF32) {
+        // fp32 x arrives by one bulk copy, then each warp quantises whole Q8_1 blocks.
+        const float *xb = reinterpret_cast<const float *>(smem + L.xbuf);
+        const uint32_t xbytes = uint32_t(NCOLS) * uint32_t(K) * 4u;
+        __syncthreads();  // xbar initialised
+        if (tid == 0) {
+            mbar_arrive_expect_tx(xbar, xbytes);
+            bulk_copy_g2s(smem + L.xbuf, args.x, xbytes, xbar);
+        }
+        if (!mbar_wait_bounded(xbar, 0, kWaitLimitNs)) (void)mbar_wait_bounded(xbar, 0, kWaitLimitNs);
+        for (int blk = warp; blk < NCOLS * nkb; blk += nwarps) {
+            const Q81Lane r = quantize_lane(xb[blk * 32 + lane]);
+            const uint32_t word = pack_quants(r.q);
+            const int c = blk / nkb, kb = blk - c * nkb;
+            if ((lane & 3) == 0) {
+                const int w = lane >> 2;  // word 0..7 of the block
+                *reinterpret_cast<uint32_t *>(aq + c * acb + act_chunk<QT>(2 * kb + (w >> 2)) * 16 +
+                                              (w & 3) * 4) = word;
+            }
+            if (lane == 0) ad[blk] = __half2float(__float2half_rn(r.d));
+        }
+    } else {
+        // Q8_1 blocks: 9 words each ({d, s} then 8 quant words); loads batched 8 deep.
+        const uint32_t *xw = reinterpret_cast<const uint32_t *>(args.x);
         const int nw = NCOLS * nkb * 9;
-        for (int i = tid; i < nw; i += T) {
-            const int blk = i / 9, w = i - blk * 9;  // blk = c * nkb + kb
-            const uint32_t v = __ldg(xw + i);
-            if (w == 0) {
-                ad[blk] = h2f(v);
-            } else {
-                const int c = blk / nkb, kb = blk - c * nkb;
-                const int ci = 2 * kb + ((w - 1) >> 2);
-                *reinterpret_cast<uint32_t *>(aq + c * acb + act_chunk(ci) * 16 +
-                                              ((w - 1) & 3) * 4) = v;
+        for (int base = 0; base < nw; base += 8 * T) {
+            uint32_t v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int i = base + j * T + tid;
+                v[j] = i < nw ? __ldg(xw + i) : 0u;
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int i = base + j * T + tid;
+                if (i < nw) {
+                    const int blk = i / 9, w = i - blk * 9;  // blk = c * nkb + kb
+                    if (w == 0) {
+                        ad[blk] = h2f(v[j]);
+                    } else {
+                        const int c = blk / nkb, kb = blk - c * nkb;
+                        *reinterpret_cast<uint32_t *>(aq + c * acb +
+                                                      act_chunk<QT>(2 * kb + ((w - 1) >> 2)) * 16 +
+                                                      ((w - 1) & 3) * 4) = v[j];
+                    }
+                }
             }
         }
     }
     __syncthreads();
-    for (int i = tid; i < NCOLS * nkb * 2; i += T) {
-        const int blk = i >> 1, half = i & 1;
-        const int c = blk / nkb, kb = blk - c * nkb;
-        const uint4 q =
-            *reinterpret_cast<const uint4 *>(aq + c * acb + act_chunk(2 * kb + half) * 16);
-        int sq = 0;
-        sq = __dp4a(int(q.x), 0x01010101, sq);
-        sq = __dp4a(int(q.y), 0x01010101, sq);
-        sq = __dp4a(int(q.z), 0x01010101, sq);
-        sq = __dp4a(int(q.w), 0x01010101, sq);
-        reinterpret_cast<int *>(as)[i] = sq;
+    for (int i = tid; i < NCOLS * nkb; i += T) {
+        const int c = i / nkb, kb = i - c * nkb;
+        const uint8_t *base = aq + c * acb;
+        const uint4 q0 = *reinterpret_cast<const uint4 *>(base + act_chunk<QT>(2 * kb) * 16);
+        const uint4 q1 = *reinterpret_cast<const uint4 *>(base + act_chunk<QT>(2 * kb + 1) * 16);
+        int lo = 0, hi = 0;
+        lo = __dp4a(int(q0.x), 0x01010101, lo);
+        lo = __dp4a(int(q0.y), 0x01010101, lo);
+        lo = __dp4a(int(q0.z), 0x01010101, lo);
+        lo = __dp4a(int(q0.w), 0x01010101, lo);
+        hi = __dp4a(int(q1.x), 0x01010101, hi);
+        hi = __dp4a(int(q1.y), 0x01010101, hi);
+        hi = __dp4a(int(q1.z), 0x01010101, hi);
+        hi = __dp4a(int(q1.w), 0x01010101, hi);
+        as[i] = make_int2(lo, hi);
+        ads[i] = ad[i] * float(lo + hi);
     }
     __syncthreads();
 
-    // ---- 3. lane -> (row group, unit) mapping, fixed for all tiles -------------------
-    // U units per row.  LPR lanes share a row (32, or the power of two >= U when a row
-    // has fewer than 32 units); the warp's 32/LPR lane groups take alternate rows.
-    const int U = nblk * TR::units;
-    int LPR = 32;
-    while (LPR > 1 && (LPR >> 1) >= U) LPR >>= 1;
-    const int RG = 32 / LPR;
-    const int ul = lane & (LPR - 1);
-    const int grp = lane / LPR;
+    // ---- 3. lane -> (row group, blocks) mapping, fixed for all tiles -------------------
+    const int LB = choose_lanes_per_row(nblk, RPB);
+    const int RG = 32 / LB;
+    const int bl = lane & (LB - 1);
+    const int grp = lane / LB;
     unsigned rowmask = 0;
 #pragma unroll
     for (int i = 0; i < RPB; ++i)
@@ -407,12 +602,14 @@ __global__ void __launch_bounds__(kMaxWarps * 32)
         const uintptr_t s = reinterpret_cast<uintptr_t>(src);
         const uintptr_t e = s + size_t(rows) * row_bytes;
         uint8_t *wrow0 = ring + st * L.stage + int(s & 15);
+        unsigned live = rowmask & ((1u << rows) - 1u);
 
         const bool have_w = mbar_wait_bounded(&full[st], (k / nstages) & 1, kWaitLimitNs);
         if (!have_w) {
             // The copy did not land in time: one more bounded wait so that it is not still
             // writing this stage when the warp moves on; the tile is then skipped.
             (void)mbar_wait_bounded(&full[st], (k / nstages) & 1, kWaitLimitNs);
+            live = 0;
         }
         if ((s | e) & 15) {  // unaligned ends: plain loads of at most 30 bytes
             const uintptr_t s_al = (s + 15) & ~uintptr_t(15), e_al = e & ~uintptr_t(15);
@@ -434,62 +631,46 @@ __global__ void __launch_bounds__(kMaxWarps * 32)
 #pragma unroll
             for (int c = 0; c < NCOLS; ++c) acc[i][c] = 0.f;
 
-        if (have_w) {
-            for (int u = ul; u < U; u += LPR) {
-                const int b = u / TR::units, ub = u - b * TR::units;
-                int kb0, kb1;
-                unit_blocks<QT>(b, ub, kb0, kb1);
-                ActUnit a1;
-                if constexpr (NCOLS == 1) a1 = load_act<QT>(aq, ad, as, kb0, kb1);
+        if (live) {
+            const TileCtx<RPB, NCOLS> ctx{wrow0, row_bytes, nrows, r0, K, nkb, acb, live,
+                                          aq, ad, ads, as, args.sums};
+            for (int b = bl; b < nblk; b += LB) {
+                BlkHdr hdr[RPB];
 #pragma unroll
-                for (int i = 0; i < RPB; ++i) {
-                    if (((rowmask >> i) & 1u) && i < rows) {
-                        const WUnit w =
-                            decode_unit<QT>(wrow0 + i * row_bytes + b * TR::bytes, ub);
-#pragma unroll
-                        for (int c = 0; c < NCOLS; ++c) {
-                            ActUnit a;
-                            if constexpr (NCOLS == 1) {
-                                a = a1;
-                            } else {
-                                a = load_act<QT>(aq + c * acb, ad + c * nkb, as + c * nkb, kb0,
-                                                 kb1);
-                            }
-                            int isum[4];
-                            acc[i][c] += dot_unit<QT>(w, a, isum);
-                            if constexpr (SUMS) {
-                                const int nsub = QT == kTypeQ6_K ? K / 16 : K / 32;
-                                store_sums<QT>(sums + (size_t(c) * nrows + r0 + i) * nsub, kb0,
-                                               kb1, isum);
-                            }
-                        }
-                    }
+                for (int i = 0; i < RPB; ++i)
+                    if ((live >> i) & 1u) hdr[i] = load_hdr<QT>(wrow0 + i * row_bytes + b * TR::bytes);
+                unit_step<QT, NCOLS, RPB, MODE, 0>(ctx, b, hdr, acc);
+                if constexpr (Units<QT>::n == 4) {
+                    unit_step<QT, NCOLS, RPB, MODE, 1>(ctx, b, hdr, acc);
+                    unit_step<QT, NCOLS, RPB, MODE, 2>(ctx, b, hdr, acc);
+                    unit_step<QT, NCOLS, RPB, MODE, 3>(ctx, b, hdr, acc);
                 }
             }
         }
 
-        // ---- 4. warp reduction and store (rows a lane group does not own add zeros) ---
+        // ---- 4. reduction over the LB lanes sharing a row, then store ------------------
+        if constexpr (MODE != kModeSums) {
 #pragma unroll
-        for (int i = 0; i < RPB; ++i)
+            for (int i = 0; i < RPB; ++i)
 #pragma unroll
-            for (int c = 0; c < NCOLS; ++c) {
-                const float v = warp_sum(acc[i][c]);
-                if constexpr (!SUMS) {
-                    if (lane == 0 && i < rows) y[size_t(c) * nrows + r0 + i] = v;
+                for (int c = 0; c < NCOLS; ++c) {
+                    float v = acc[i][c];
+                    for (int o = LB >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                    if (bl == 0 && ((rowmask >> i) & 1u) && i < rows)
+                        args.y[size_t(c) * nrows + r0 + i] = v;
                 }
-            }
+        }
         __syncwarp();  // every lane is done with stage `st`
         if (lane == 0 && k + nstages < my_tiles) issue(tile + nstages * wstride, st);
     }
 }
 
 // Host-side kernel table access, one instantiation file per type.
-using MmvqKernelFn = void (*)(const uint8_t *, const uint8_t *, float *, int32_t *, int, int,
-                              int);
-MmvqKernelFn mmvq_kernel_q4k(int ncols, int rpb, bool sums);
-MmvqKernelFn mmvq_kernel_q5k(int ncols, int rpb, bool sums);
-MmvqKernelFn mmvq_kernel_q6k(int ncols, int rpb, bool sums);
-MmvqKernelFn mmvq_kernel_q80(int ncols, int rpb, bool sums);
+using MmvqKernelFn = void (*)(MmvqArgs);
+MmvqKernelFn mmvq_kernel_q4k(int ncols, int rpb, int mode);
+MmvqKernelFn mmvq_kernel_q5k(int ncols, int rpb, int mode);
+MmvqKernelFn mmvq_kernel_q6k(int ncols, int rpb, int mode);
+MmvqKernelFn mmvq_kernel_q80(int ncols, int rpb, int mode);
 // Reads and clears the device status word of that type's translation unit (current device).
 int mmvq_kernel_q4k_take_status();
 int mmvq_kernel_q5k_take_status();
@@ -498,29 +679,38 @@ int mmvq_kernel_q80_take_status();
 
 }  // namespace anvil
 
-// Builds the [ncols 1..8] x [rpb 1,2,4,8] x [sums] table for one type.
+// Builds the [ncols 1..8] x [rpb 1,2,4,8] x [mode] table for one type.
 #define ANVIL_MMVQ_TABLE(FN, QT)                                                          \
     namespace anvil {                                                                     \
-    template <int NC>                                                                     \
-    static MmvqKernelFn FN##_pick(int rpb, bool sums) {                                   \
-        switch (rpb) {                                                                    \
-        case 1: return sums ? mmvq_kernel<QT, NC, 1, true> : mmvq_kernel<QT, NC, 1, false>; \
-        case 2: return sums ? mmvq_kernel<QT, NC, 2, true> : mmvq_kernel<QT, NC, 2, false>; \
-        case 4: return sums ? mmvq_kernel<QT, NC, 4, true> : mmvq_kernel<QT, NC, 4, false>; \
-        case 8: return sums ? mmvq_kernel<QT, NC, 8, true> : mmvq_kernel<QT, NC, 8, false>; \
+    template <int NC, int R>                                                              \
+    static MmvqKernelFn FN##_mode(int mode) {                                             \
+        switch (mode) {                                                                   \
+        case kModeQ81: return mmvq_kernel<QT, NC, R, kModeQ81>;                           \
+        case kModeF32: return mmvq_kernel<QT, NC, R, kModeF32>;                           \
+        case kModeSums: return mmvq_kernel<QT, NC, R, kModeSums>;                         \
         default: return nullptr;                                                          \
         }                                                                                 \
     }                                                                                     \
-    MmvqKernelFn FN(int ncols, int rpb, bool sums) {                                      \
+    template <int NC>                                                                     \
+    static MmvqKernelFn FN##_pick(int rpb, int mode) {                                    \
+        switch (rpb) {                                                                    \
+        case 1: return FN##_mode<NC, 1>(mode);                                            \
+        case 2: return FN##_mode<NC, 2>(mode);                                            \
+        case 4: return FN##_mode<NC, 4>(mode);                                            \
+        case 8: return FN##_mode<NC, 8>(mode);                                            \
+        default: return nullptr;                                                          \
+        }                                                                                 \
+    }                                                                                     \
+    MmvqKernelFn FN(int ncols, int rpb, int mode) {                                       \
         switch (ncols) {                                                                  \
-        case 1: return FN##_pick<1>(rpb, sums);                                           \
-        case 2: return FN##_pick<2>(rpb, sums);                                           \
-        case 3: return FN##_pick<3>(rpb, sums);                                           \
-        case 4: return FN##_pick<4>(rpb, sums);                                           \
-        case 5: return FN##_pick<5>(rpb, sums);                                           \
-        case 6: return FN##_pick<6>(rpb, sums);                                           \
-        case 7: return FN##_pick<7>(rpb, sums);                                           \
-        case 8: return FN##_pick<8>(rpb, sums);                                           \
+        case 1: return FN##_pick<1>(rpb, mode);                                           \
+        case 2: return FN##_pick<2>(rpb, mode);                                           \
+        case 3: return FN##_pick<3>(rpb, mode);                                           \
+        case 4: return FN##_pick<4>(rpb, mode);                                           \
+        case 5: return FN##_pick<5>(rpb, mode);                                           \
+        case 6: return FN##_pick<6>(rpb, mode);                                           \
+        case 7: return FN##_pick<7>(rpb, mode);                                           \
+        case 8: return FN##_pick<8>(rpb, mode);                                           \
         default: return nullptr;                                                          \
         }                                                                                 \
     }                                                                                     \

@@ -134,6 +134,8 @@ SIGNATURES = {
                               c_uint, c_void_p]),
     "anvil_mmvq_f32": (c_int, [c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
                                c_int, c_int, c_void_p]),
+    "anvil_mmvq_f32_ex": (c_int, [c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
+                                  c_int, c_int, c_uint, c_void_p]),
     "anvil_take_device_status": (c_int, []),
     "anvil_mmvq_block_sums": (c_int, [c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
                                       c_int, c_void_p]),
@@ -143,6 +145,8 @@ SIGNATURES = {
     "anvil_chain_add_quantize": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int]),
     "anvil_chain_add_mmvq": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int, c_int,
                                      c_int, c_int, c_int]),
+    "anvil_chain_add_mmvq_f32": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p,
+                                         c_int, c_int, c_int, c_int, c_int]),
     "anvil_chain_instantiate": (c_int, [c_void_p, c_int, c_void_p]),
     "anvil_chain_launch": (c_int, [c_void_p, c_void_p]),
     "anvil_chain_num_steps": (c_int, [c_void_p]),

@@ -143,7 +143,7 @@ class DeviceChain:
 
     def __init__(self, spec: ChainSpec, ncols: int = 1, seed: int = 0, device="cuda",
                  rank: int = 0, world: int = 1, nwarps: int = 0, rows_per_block: int = 0,
-                 configs: dict | None = None):
+                 configs: dict | None = None, fused: bool = True):
         import torch
 
         from kernel_anvil.mmvq import Chain, q8_1_bytes
@@ -171,15 +171,20 @@ class DeviceChain:
             n = r1 - r0
             W = make_weights_device(gm.qt, n, gm.K, seed=seed * 100003 + i * 31 + rank, device=device)
             y = torch.empty((ncols, n), dtype=torch.float32, device=device)
-            if gm.input not in quantized:
-                self.chain.add_quantize(self.x[gm.input], self.xq[gm.input])
-                quantized.add(gm.input)
             nw, rpb = nwarps, rows_per_block
             if configs and (gm.qt, gm.nrows, gm.K) in configs:
                 c = configs[(gm.qt, gm.nrows, gm.K)]
                 nw, rpb = c["nwarps"], c["rows_per_block"]
-            self.chain.add_mmvq(W, gm.qt, self.xq[gm.input], y, nrows=n, K=gm.K, ncols=ncols,
-                                nwarps=nw, rows_per_block=rpb)
+            if fused:
+                # each GEMV quantises its fp32 input in its own prologue
+                self.chain.add_mmvq_f32(W, gm.qt, self.x[gm.input], self.xq[gm.input], y, nrows=n,
+                                        K=gm.K, ncols=ncols, nwarps=nw, rows_per_block=rpb)
+            else:
+                if gm.input not in quantized:
+                    self.chain.add_quantize(self.x[gm.input], self.xq[gm.input])
+                    quantized.add(gm.input)
+                self.chain.add_mmvq(W, gm.qt, self.xq[gm.input], y, nrows=n, K=gm.K, ncols=ncols,
+                                    nwarps=nw, rows_per_block=rpb)
             self.weights.append(W)
             self.outputs.append(y)
             self.rows.append((r0, r1))

@@ -22,10 +22,13 @@ import sys
 def cmd_bench_gemv(args) -> None:
     from kernel_anvil.verify import bench_gemv
 
-    res = bench_gemv(args.quant, args.n, args.k, ncols=args.ncols, nwarps=args.nwarps,
-                     rows_per_block=args.rpb, warmup=args.warmup, runs=args.runs,
-                     rotate_bytes=int(args.rotate_mb * 1e6), pdl=args.pdl)
-    print(json.dumps(res))
+    for n in _int_list(args.n):
+        for k in _int_list(args.k):
+            for pdl in ([False, True] if args.pdl == "both" else [args.pdl == "on"]):
+                res = bench_gemv(args.quant, n, k, ncols=args.ncols, nwarps=args.nwarps,
+                                 rows_per_block=args.rpb, warmup=args.warmup, runs=args.runs,
+                                 rotate_bytes=int(args.rotate_mb * 1e6), pdl=pdl)
+                print(json.dumps(res), flush=True)
 
 
 def _int_list(text: str) -> list[int]:
@@ -69,8 +72,8 @@ def build_parser() -> argparse.ArgumentParser:
 
     p = sub.add_parser("bench-gemv", help="Time one quantized GEMV shape (L2-defeating buffer rotation)")
     p.add_argument("--quant", default="Q4_K")
-    p.add_argument("--n", type=int, default=4096, help="rows (output features)")
-    p.add_argument("--k", type=int, default=4096, help="columns (input features)")
+    p.add_argument("--n", default="4096", help="rows (output features); comma list allowed")
+    p.add_argument("--k", default="4096", help="columns (input features); comma list allowed")
     p.add_argument("--ncols", type=int, default=1)
     p.add_argument("--nwarps", type=int, default=0)
     p.add_argument("--rpb", type=int, default=0)
@@ -78,7 +81,8 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--runs", type=int, default=100)
     p.add_argument("--rotate-mb", type=float, default=512.0,
                    help="distinct weight copies cycled through (> L2 so each launch reads HBM)")
-    p.add_argument("--pdl", action="store_true", help="launch with programmatic dependent launch")
+    p.add_argument("--pdl", choices=["off", "on", "both"], default="off",
+                   help="launch with programmatic dependent launch (consecutive launches overlap)")
     p.set_defaults(fn=cmd_bench_gemv)
 
     p = sub.add_parser("autoforge", help="Sweep the real MMVQ kernels per shape and write smithy JSON")

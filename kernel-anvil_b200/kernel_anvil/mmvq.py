@@ -102,8 +102,12 @@ def mmvq(W: torch.Tensor, qt, xq: torch.Tensor, nrows: int | None = None, K: int
 
 
 def mmvq_f32(W: torch.Tensor, qt, x: torch.Tensor, nwarps: int = 0, rows_per_block: int = 0,
-             xq_scratch: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
-    """Quantise fp32 x (ncols, K) to Q8_1 and run MMVQ, as llama.cpp's MMVQ path does."""
+             xq_scratch: torch.Tensor | None = None, out: torch.Tensor | None = None,
+             pdl: bool = False) -> torch.Tensor:
+    """y = W @ dequant(Q8_1(x)) from fp32 x (ncols, K), as llama.cpp's MMVQ path computes it.
+
+    One kernel quantises x in its prologue when it fits (else quantise + MMVQ); the result
+    is bit-identical to quantize_q8_1 followed by mmvq."""
     info = resolve_type(qt)
     _require_cuda("W", W, torch.uint8)
     _require_cuda("x", x, torch.float32)
@@ -116,9 +120,10 @@ def mmvq_f32(W: torch.Tensor, qt, x: torch.Tensor, nwarps: int = 0, rows_per_blo
     if out is None:
         out = torch.empty((ncols, nrows), dtype=torch.float32, device=W.device)
     _require_cuda("out", out, torch.float32)
-    check(_native.lib().anvil_mmvq_f32(info.ggml_type, W.data_ptr(), x2.data_ptr(),
-                                       xq_scratch.data_ptr(), out.data_ptr(), nrows, K, ncols,
-                                       nwarps, rows_per_block, _stream_ptr()))
+    check(_native.lib().anvil_mmvq_f32_ex(info.ggml_type, W.data_ptr(), x2.data_ptr(),
+                                          xq_scratch.data_ptr(), out.data_ptr(), nrows, K, ncols,
+                                          nwarps, rows_per_block, ANVIL_FLAG_PDL if pdl else 0,
+                                          _stream_ptr()))
     return out
 
 
@@ -200,6 +205,27 @@ class Chain:
         check(self._lib.anvil_chain_add_mmvq(self._h, info.ggml_type, W.data_ptr(), xq.data_ptr(),
                                              y.data_ptr(), nrows, K, ncols, nwarps, rows_per_block))
         self._keep += [W, xq, y]
+        self.n_mmvq += 1
+        self.weight_bytes += nrows * info.row_bytes(K)
+        from kernel_anvil.quants import gemv_bytes
+        self.algorithmic_bytes += gemv_bytes(info, nrows, K, ncols)
+
+    def add_mmvq_f32(self, W: torch.Tensor, qt, x: torch.Tensor, xq_scratch: torch.Tensor,
+                     y: torch.Tensor, nrows: int | None = None, K: int | None = None, ncols: int = 1,
+                     nwarps: int = 0, rows_per_block: int = 0) -> None:
+        """GEMV step from fp32 x (quantisation fused into the GEMV when it fits)."""
+        info = resolve_type(qt)
+        _require_cuda("W", W, torch.uint8)
+        _require_cuda("x", x, torch.float32)
+        _require_cuda("xq_scratch", xq_scratch, torch.uint8)
+        _require_cuda("y", y, torch.float32)
+        nrows, K = _shape_args(W, info, nrows, K)
+        if x.numel() < K * ncols or xq_scratch.numel() < q8_1_bytes(K, ncols) or y.numel() < ncols * nrows:
+            raise AnvilError(_native.ANVIL_ERR_INVALID, "x, xq_scratch or y is too small")
+        check(self._lib.anvil_chain_add_mmvq_f32(self._h, info.ggml_type, W.data_ptr(), x.data_ptr(),
+                                                 xq_scratch.data_ptr(), y.data_ptr(), nrows, K, ncols,
+                                                 nwarps, rows_per_block))
+        self._keep += [W, x, xq_scratch, y]
         self.n_mmvq += 1
         self.weight_bytes += nrows * info.row_bytes(K)
         from kernel_anvil.quants import gemv_bytes
