@@ -52,6 +52,10 @@ def parse_args():
     ap.add_argument("--impl", default="anvil", choices=["anvil", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--quantize", choices=["fused", "separate"], default="separate",
+                    help="quantise each GEMV input in its own kernel or inside the GEMV (fused)")
+    ap.add_argument("--coresident", type=int, default=1,
+                    help="GEMV kernels sized to share each SM (2: the next GEMV prefetches during this one)")
     return ap.parse_args()
 
 
@@ -253,7 +257,8 @@ def run_anvil(args) -> None:
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
 
     spec = get_chain(args.workload)
-    dc = DeviceChain(spec, rank=rank, world=world, device=dev)
+    dc = DeviceChain(spec, rank=rank, world=world, device=dev, fused=args.quantize == "fused",
+                     coresident=args.coresident)
     stream = torch.cuda.Stream(device=dev)
     hbm_peak, peak_kind = measured_peaks()
     total_bytes = spec.algorithmic_bytes()  # whole job: all shards together
@@ -359,7 +364,8 @@ def run_anvil(args) -> None:
                    "pct_of_8TBps": round(100 * value / 8000.0, 1),
                    "l2": "inputs larger than L2 (weights stream from HBM every step)",
                    "parallelism": f"row-shard x{world} + NCCL all-gather" if world > 1 else "single GPU",
-                   "graph": "CUDA graph, programmatic dependent launch between kernels"},
+                   "graph": "CUDA graph, programmatic dependent launch between kernels",
+                   "quantize": args.quantize, "coresident_kernels_per_sm": args.coresident},
         "e2e": e2e, "roofline": roofline, "gpu_launches": launches_per_step * args.steps,
         "device_status": status,
     }

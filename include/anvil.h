@@ -167,6 +167,11 @@ int anvil_chain_add_mmvq(anvil_chain *chain, int ggml_type, const void *W, const
 int anvil_chain_add_mmvq_f32(anvil_chain *chain, int ggml_type, const void *W, const float *x,
                              void *xq, float *y, int nrows, int ncols_x, int ncols_dst,
                              int nwarps, int rows_per_block);
+/* Sizes every GEMV grid so that `kernels_per_sm` consecutive GEMVs (1..4) fit on each SM
+ * together: with programmatic dependent launch the next GEMV's CTAs are then resident
+ * while the current one runs and stream their first weight tiles early.  Default 1 (each
+ * GEMV takes every resident slot).  Call before instantiation. */
+int anvil_chain_set_coresident(anvil_chain *chain, int kernels_per_sm);
 /* use_pdl: launch every step after the first with ANVIL_FLAG_PDL. */
 int anvil_chain_instantiate(anvil_chain *chain, int use_pdl, anvil_stream_t stream);
 /* Replays the graph (or, before instantiation, launches the steps one by one). */

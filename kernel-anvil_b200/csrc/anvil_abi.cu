@@ -179,7 +179,17 @@ static void default_config(int t, int nrows, int K, int ncols, int *nw, int *rpb
 struct Plan {
     MmvqKernelFn fn;
     int mode, nwarps, rpb, nstages, grid, smem;
+    int occ, nsm;
+    long ctas_needed;
 };
+
+// Grid of a plan when `share` kernels are meant to be resident on each SM at once (a chain
+// under programmatic dependent launch: the next GEMV's CTAs fit beside the current one's
+// and stream their first weight tiles while it runs).
+static int grid_for(const Plan &p, int share) {
+    const long per_sm = share > 1 ? std::max(1, p.occ / share) : p.occ;
+    return int(std::min<long>(p.ctas_needed, per_sm * p.nsm));
+}
 
 static int round_rpb(int r) { return r >= 8 ? 8 : r >= 4 ? 4 : r >= 2 ? 2 : 1; }
 
@@ -245,15 +255,17 @@ static int plan_mmvq(int t, int nrows, int K, int ncols, int nwarps, int rpb, in
         return s;
     // Persistent grid: every warp takes warp-tiles of rpb rows round-robin.
     const long ntiles = (long(nrows) + rpb - 1) / rpb;
-    const long ctas_needed = (ntiles + nwarps - 1) / nwarps;
-    p->grid = int(std::min<long>(ctas_needed, long(occ) * nsm));
+    p->ctas_needed = (ntiles + nwarps - 1) / nwarps;
+    p->occ = occ;
+    p->nsm = nsm;
+    p->grid = grid_for(*p, 1);
     return ANVIL_OK;
 }
 
 static int launch_mmvq(const Plan &p, const void *W, const void *x, float *y, int32_t *sums,
-                       int nrows, int K, unsigned flags, cudaStream_t stream) {
+                       int nrows, int K, unsigned flags, cudaStream_t stream, int share = 1) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(p.grid);
+    cfg.gridDim = dim3(share > 1 ? grid_for(p, share) : p.grid);
     cfg.blockDim = dim3(p.nwarps * 32);
     cfg.dynamicSmemBytes = p.smem;
     cfg.stream = stream;
@@ -338,6 +350,7 @@ struct ChainStep {
 
 struct anvil_chain {
     std::vector<ChainStep> steps;
+    int share = 1;  // kernels meant to be co-resident per SM (see grid_for)
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
 };
@@ -483,6 +496,15 @@ void anvil_chain_destroy(anvil_chain *c) {
 
 int anvil_chain_num_steps(const anvil_chain *c) { return c ? int(c->steps.size()) : 0; }
 
+int anvil_chain_set_coresident(anvil_chain *c, int kernels_per_sm) {
+    if (!c) return fail(ANVIL_ERR_INVALID, "null chain");
+    if (c->exec) return fail(ANVIL_ERR_INVALID, "chain already instantiated");
+    if (kernels_per_sm < 1 || kernels_per_sm > 4)
+        return fail(ANVIL_ERR_INVALID, "kernels_per_sm=%d outside 1..4", kernels_per_sm);
+    c->share = kernels_per_sm;
+    return ANVIL_OK;
+}
+
 int anvil_chain_add_quantize(anvil_chain *c, const float *x, void *xq, int K, int ncols) {
     if (!c) return fail(ANVIL_ERR_INVALID, "null chain");
     if (c->exec) return fail(ANVIL_ERR_INVALID, "chain already instantiated");
@@ -560,13 +582,14 @@ static int run_steps(anvil_chain *c, bool use_pdl, cudaStream_t st) {
         if (s.quantize) {
             r = launch_quantize(s.x, s.xq, s.K, s.ncols, flags, st);
         } else if (s.fused && s.plan.mode == kModeF32) {
-            r = launch_mmvq(s.plan, s.W, s.x, s.y, nullptr, s.nrows, s.ncols_x, flags, st);
+            r = launch_mmvq(s.plan, s.W, s.x, s.y, nullptr, s.nrows, s.ncols_x, flags, st, c->share);
         } else if (s.fused) {
             r = launch_quantize(s.x, s.xq, s.K, s.ncols, flags, st);
             if (!r) r = launch_mmvq(s.plan, s.W, s.xq, s.y, nullptr, s.nrows, s.ncols_x,
-                                    use_pdl ? ANVIL_FLAG_PDL : 0u, st);
+                                    use_pdl ? ANVIL_FLAG_PDL : 0u, st, c->share);
         } else {
-            r = launch_mmvq(s.plan, s.W, s.xqin, s.y, nullptr, s.nrows, s.ncols_x, flags, st);
+            r = launch_mmvq(s.plan, s.W, s.xqin, s.y, nullptr, s.nrows, s.ncols_x, flags, st,
+                            c->share);
         }
         if (r) return r;
     }

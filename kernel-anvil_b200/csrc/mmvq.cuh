@@ -374,22 +374,23 @@ __device__ __forceinline__ int choose_lanes_per_row(int nblk, int rpb) {
     return best;
 }
 
-// Per-tile context shared by the unit steps of one block.
-template <int RPB, int NCOLS>
+// Per-tile context shared by the unit steps of one block.  A lane computes the rows
+// slot * RG + grp of the tile for slot < nslots: every lane of the warp runs the same slot
+// at the same time, so row ownership never splits a warp's instruction stream.
 struct TileCtx {
     const uint8_t *wrow0;
-    int row_bytes, nrows, r0, K, nkb, acb;
-    unsigned live;  // rows of the tile this lane computes
+    int row_bytes, nrows, r0, rows, K, nkb, acb;
+    int RG, grp, nslots;
     const uint8_t *aq;
     const float *ad, *ads;
     const int2 *as;
     int32_t *sums;
 };
 
-// One compile-time unit U of block b for every live row and column.
+// One compile-time unit U of block b for every slot and column.
 template <int QT, int NCOLS, int RPB, int MODE, int U>
-__device__ __forceinline__ void unit_step(const TileCtx<RPB, NCOLS> &t, int b,
-                                          const BlkHdr (&hdr)[RPB], float (&acc)[RPB][NCOLS]) {
+__device__ __forceinline__ void unit_step(const TileCtx &t, int b, const BlkHdr (&hdr)[RPB],
+                                          float (&acc)[RPB][NCOLS]) {
     using TR = QTraits<QT>;
     int kb0, kb1;
     unit_kb<QT, U>(b, kb0, kb1);
@@ -400,8 +401,9 @@ __device__ __forceinline__ void unit_step(const TileCtx<RPB, NCOLS> &t, int b,
         if constexpr (QT != kTypeQ8_0) load_act<QT>(v, kb1, a1);
     }
 #pragma unroll
-    for (int i = 0; i < RPB; ++i) {
-        if ((t.live >> i) & 1u) {
+    for (int sl = 0; sl < RPB; ++sl) {
+        const int i = sl * t.RG + t.grp;
+        if (sl < t.nslots && i < t.rows) {
             const uint8_t *blk = t.wrow0 + i * t.row_bytes + b * TR::bytes;
             WBytes wb;
             load_unit<QT, U>(blk, wb);
@@ -414,7 +416,7 @@ __device__ __forceinline__ void unit_step(const TileCtx<RPB, NCOLS> &t, int b,
                     if constexpr (QT != kTypeQ8_0) load_act<QT>(v, kb1, a1);
                 }
                 int isum[4];
-                acc[i][c] += dot_unit<QT, U>(blk, hdr[i], wb, a0, QT == kTypeQ8_0 ? a0 : a1, isum);
+                acc[sl][c] += dot_unit<QT, U>(blk, hdr[sl], wb, a0, QT == kTypeQ8_0 ? a0 : a1, isum);
                 if constexpr (MODE == kModeSums) {
                     const int nsub = QT == kTypeQ6_K ? t.K / 16 : t.K / 32;
                     store_sums<QT>(t.sums + (size_t(c) * t.nrows + t.r0 + i) * nsub, kb0, kb1, isum);
@@ -454,7 +456,7 @@ __device__ __forceinline__ uint32_t pack_quants(int q) {
 // ---- the kernel --------------------------------------------------------------------------
 
 template <int QT, int NCOLS, int RPB, int MODE>
-__global__ void __launch_bounds__(kMaxWarps * 32, 1) mmvq_kernel(const MmvqArgs args) {
+__global__ void __launch_bounds__(kMaxWarps * 32, NCOLS == 1 ? 2 : 1) mmvq_kernel(const MmvqArgs args) {
     using TR = QTraits<QT>;
     extern __shared__ __align__(16) uint8_t smem[];
     const int T = blockDim.x;
@@ -479,7 +481,6 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) mmvq_kernel(const MmvqArgs 
     const int wstride = gridDim.x * nwarps;
     const int my_tiles = gwarp < ntiles ? (ntiles - 1 - gwarp) / wstride + 1 : 0;
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bar) + warp * nstages;
-    uint64_t *xbar = reinterpret_cast<uint64_t *>(smem + L.bar) + nwarps * nstages;
     uint8_t *ring = smem + L.w + warp * nstages * L.stage;
 
     // Bulk copy of tile `tile` into stage `st` (lane 0 only).  The 16-byte aligned
@@ -506,7 +507,6 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) mmvq_kernel(const MmvqArgs 
     // ---- 1. start streaming weights before waiting on the producer of x ------------
     if (lane == 0) {
         for (int st = 0; st < nstages; ++st) mbar_init(&full[st], 1);
-        if (MODE == kModeF32 && warp == 0) mbar_init(xbar, 1);
         mbar_fence_init();
         for (int k = 0; k < my_tiles && k < nstages; ++k) issue(gwarp + k * wstride, k);
     }
@@ -515,25 +515,62 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) mmvq_kernel(const MmvqArgs 
 
     // ---- 2. stage the activation once per CTA ------------------------------------------
     if constexpr (MODE == kModeF32) {
-        // fp32 x arrives by one bulk copy, then each warp quantises whole Q8_1 blocks.
-        const float *xb = reinterpret_cast<const float *>(smem + L.xbuf);
-        const uint32_t xbytes = uint32_t(NCOLS) * uint32_t(K) * 4u;
-        __syncthreads();  // xbar initialised
-        if (tid == 0) {
-            mbar_arrive_expect_tx(xbar, xbytes);
-            bulk_copy_g2s(smem + L.xbuf, args.x, xbytes, xbar);
-        }
-        if (!mbar_wait_bounded(xbar, 0, kWaitLimitNs)) (void)mbar_wait_bounded(xbar, 0, kWaitLimitNs);
-        for (int blk = warp; blk < NCOLS * nkb; blk += nwarps) {
-            const Q81Lane r = quantize_lane(xb[blk * 32 + lane]);
-            const uint32_t word = pack_quants(r.q);
-            const int c = blk / nkb, kb = blk - c * nkb;
-            if ((lane & 3) == 0) {
-                const int w = lane >> 2;  // word 0..7 of the block
-                *reinterpret_cast<uint32_t *>(aq + c * acb + act_chunk<QT>(2 * kb + (w >> 2)) * 16 +
-                                              (w & 3) * 4) = word;
+        // fp32 x is staged with batched plain loads (a bulk copy here would queue behind
+        // the weight tiles already issued), then each warp quantises whole Q8_1 blocks.
+        float *xs = reinterpret_cast<float *>(smem + L.xbuf);
+        const float4 *xg = reinterpret_cast<const float4 *>(args.x);
+        const int n4 = NCOLS * K / 4;
+        for (int base = 0; base < n4; base += 4 * T) {
+            float4 v[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int i = base + j * T + tid;
+                v[j] = i < n4 ? __ldg(xg + i) : make_float4(0.f, 0.f, 0.f, 0.f);
             }
-            if (lane == 0) ad[blk] = __half2float(__float2half_rn(r.d));
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int i = base + j * T + tid;
+                if (i < n4) reinterpret_cast<float4 *>(xs)[i] = v[j];
+            }
+        }
+        __syncthreads();
+        const float *xb = xs;
+        // Four blocks per warp per pass: their reduction chains interleave (ILP) while each
+        // block keeps the exact butterfly order of the standalone quantiser.
+        const int nb = NCOLS * nkb;
+        for (int b0 = warp * 4; b0 < nb; b0 += nwarps * 4) {
+            float xv[4], am[4], sm[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                xv[j] = b0 + j < nb ? xb[(b0 + j) * 32 + lane] : 0.f;
+                am[j] = fabsf(xv[j]);
+                sm[j] = xv[j];
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    am[j] = fmaxf(am[j], __shfl_xor_sync(0xffffffffu, am[j], o));
+                    sm[j] += __shfl_xor_sync(0xffffffffu, sm[j], o);
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float d = __fdiv_rn(am[j], 127.0f);
+                const int q = am[j] == 0.0f ? 0 : int(roundf(__fdiv_rn(xv[j], d)));
+                const uint32_t word = pack_quants(q);
+                const int blk = b0 + j;
+                if (blk < nb) {
+                    const int c = blk / nkb, kb = blk - c * nkb;
+                    if ((lane & 3) == 0) {
+                        const int w = lane >> 2;  // word 0..7 of the block
+                        *reinterpret_cast<uint32_t *>(aq + c * acb +
+                                                      act_chunk<QT>(2 * kb + (w >> 2)) * 16 +
+                                                      (w & 3) * 4) = word;
+                    }
+                    if (lane == 0) ad[blk] = __half2float(__float2half_rn(d));
+                }
+            }
         }
     } else {
         // Q8_1 blocks: 9 words each ({d, s} then 8 quant words); loads batched 8 deep.
@@ -584,14 +621,13 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) mmvq_kernel(const MmvqArgs 
     __syncthreads();
 
     // ---- 3. lane -> (row group, blocks) mapping, fixed for all tiles -------------------
+    // LB lanes split a row's blocks; the warp's RG = 32/LB lane groups take rows
+    // slot * RG + grp (nslots slots; groups beyond RPB stay idle when RPB < RG).
     const int LB = choose_lanes_per_row(nblk, RPB);
     const int RG = 32 / LB;
     const int bl = lane & (LB - 1);
     const int grp = lane / LB;
-    unsigned rowmask = 0;
-#pragma unroll
-    for (int i = 0; i < RPB; ++i)
-        if (i % RG == grp) rowmask |= 1u << i;
+    const int nslots = RPB >= RG ? RPB / RG : (grp < RPB ? 1 : 0);
 
     for (int k = 0; k < my_tiles; ++k) {
         const int tile = gwarp + k * wstride;
@@ -602,14 +638,12 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) mmvq_kernel(const MmvqArgs 
         const uintptr_t s = reinterpret_cast<uintptr_t>(src);
         const uintptr_t e = s + size_t(rows) * row_bytes;
         uint8_t *wrow0 = ring + st * L.stage + int(s & 15);
-        unsigned live = rowmask & ((1u << rows) - 1u);
 
-        const bool have_w = mbar_wait_bounded(&full[st], (k / nstages) & 1, kWaitLimitNs);
+        bool have_w = mbar_wait_bounded(&full[st], (k / nstages) & 1, kWaitLimitNs);
         if (!have_w) {
             // The copy did not land in time: one more bounded wait so that it is not still
             // writing this stage when the warp moves on; the tile is then skipped.
             (void)mbar_wait_bounded(&full[st], (k / nstages) & 1, kWaitLimitNs);
-            live = 0;
         }
         if ((s | e) & 15) {  // unaligned ends: plain loads of at most 30 bytes
             const uintptr_t s_al = (s + 15) & ~uintptr_t(15), e_al = e & ~uintptr_t(15);
@@ -631,14 +665,17 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) mmvq_kernel(const MmvqArgs 
 #pragma unroll
             for (int c = 0; c < NCOLS; ++c) acc[i][c] = 0.f;
 
-        if (live) {
-            const TileCtx<RPB, NCOLS> ctx{wrow0, row_bytes, nrows, r0, K, nkb, acb, live,
-                                          aq, ad, ads, as, args.sums};
+        if (have_w) {
+            const TileCtx ctx{wrow0, row_bytes, nrows, r0, rows, K, nkb, acb, RG, grp, nslots,
+                              aq, ad, ads, as, args.sums};
             for (int b = bl; b < nblk; b += LB) {
                 BlkHdr hdr[RPB];
 #pragma unroll
-                for (int i = 0; i < RPB; ++i)
-                    if ((live >> i) & 1u) hdr[i] = load_hdr<QT>(wrow0 + i * row_bytes + b * TR::bytes);
+                for (int sl = 0; sl < RPB; ++sl) {
+                    const int i = sl * RG + grp;
+                    if (sl < nslots && i < rows)
+                        hdr[sl] = load_hdr<QT>(wrow0 + i * row_bytes + b * TR::bytes);
+                }
                 unit_step<QT, NCOLS, RPB, MODE, 0>(ctx, b, hdr, acc);
                 if constexpr (Units<QT>::n == 4) {
                     unit_step<QT, NCOLS, RPB, MODE, 1>(ctx, b, hdr, acc);
@@ -651,14 +688,17 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) mmvq_kernel(const MmvqArgs 
         // ---- 4. reduction over the LB lanes sharing a row, then store ------------------
         if constexpr (MODE != kModeSums) {
 #pragma unroll
-            for (int i = 0; i < RPB; ++i)
+            for (int sl = 0; sl < RPB; ++sl) {
+                if (sl < nslots || sl == 0) {  // uniform: nslots is 0 or equal across lanes
+                    const int i = sl * RG + grp;
 #pragma unroll
-                for (int c = 0; c < NCOLS; ++c) {
-                    float v = acc[i][c];
-                    for (int o = LB >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-                    if (bl == 0 && ((rowmask >> i) & 1u) && i < rows)
-                        args.y[size_t(c) * nrows + r0 + i] = v;
+                    for (int c = 0; c < NCOLS; ++c) {
+                        float v = acc[sl][c];
+                        for (int o = LB >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                        if (bl == 0 && sl < nslots && i < rows) args.y[size_t(c) * nrows + r0 + i] = v;
+                    }
                 }
+            }
         }
         __syncwarp();  // every lane is done with stage `st`
         if (lane == 0 && k + nstages < my_tiles) issue(tile + nstages * wstride, st);

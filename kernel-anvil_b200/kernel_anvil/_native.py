@@ -147,6 +147,7 @@ SIGNATURES = {
                                      c_int, c_int, c_int]),
     "anvil_chain_add_mmvq_f32": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p,
                                          c_int, c_int, c_int, c_int, c_int]),
+    "anvil_chain_set_coresident": (c_int, [c_void_p, c_int]),
     "anvil_chain_instantiate": (c_int, [c_void_p, c_int, c_void_p]),
     "anvil_chain_launch": (c_int, [c_void_p, c_void_p]),
     "anvil_chain_num_steps": (c_int, [c_void_p]),

@@ -143,7 +143,7 @@ class DeviceChain:
 
     def __init__(self, spec: ChainSpec, ncols: int = 1, seed: int = 0, device="cuda",
                  rank: int = 0, world: int = 1, nwarps: int = 0, rows_per_block: int = 0,
-                 configs: dict | None = None, fused: bool = True):
+                 configs: dict | None = None, fused: bool = False, coresident: int = 1):
         import torch
 
         from kernel_anvil.mmvq import Chain, q8_1_bytes
@@ -165,6 +165,8 @@ class DeviceChain:
                    for a, k in spec.inputs.items()}
         self.weights, self.outputs, self.rows = [], [], []
         self.chain = Chain()
+        if coresident != 1:
+            self.chain.set_coresident(coresident)
         quantized: set[str] = set()
         for i, gm in enumerate(spec.gemvs):
             r0, r1 = shard_rows(gm.nrows, rank, world)

@@ -231,6 +231,10 @@ class Chain:
         from kernel_anvil.quants import gemv_bytes
         self.algorithmic_bytes += gemv_bytes(info, nrows, K, ncols)
 
+    def set_coresident(self, kernels_per_sm: int) -> None:
+        """Size GEMV grids so that this many consecutive GEMVs fit on each SM together."""
+        check(self._lib.anvil_chain_set_coresident(self._h, kernels_per_sm))
+
     def instantiate(self, pdl: bool = True, stream: torch.cuda.Stream | None = None) -> None:
         s = stream if stream is not None else torch.cuda.current_stream()
         check(self._lib.anvil_chain_instantiate(self._h, 1 if pdl else 0, s.cuda_stream))
