@@ -154,26 +154,25 @@ static bool supported_type(int t) {
     return t == kTypeQ4_K || t == kTypeQ5_K || t == kTypeQ6_K || t == kTypeQ8_0;
 }
 
-static MmvqKernelFn kernel_for(int t, int ncols, int rpb, int mode) {
+static MmvqKernelFn kernel_for(int t, int ncols, int rpb, int lbt, int mode) {
     switch (t) {
-    case kTypeQ4_K: return mmvq_kernel_q4k(ncols, rpb, mode);
-    case kTypeQ5_K: return mmvq_kernel_q5k(ncols, rpb, mode);
-    case kTypeQ6_K: return mmvq_kernel_q6k(ncols, rpb, mode);
-    case kTypeQ8_0: return mmvq_kernel_q80(ncols, rpb, mode);
+    case kTypeQ4_K: return mmvq_kernel_q4k(ncols, rpb, lbt, mode);
+    case kTypeQ5_K: return mmvq_kernel_q5k(ncols, rpb, lbt, mode);
+    case kTypeQ6_K: return mmvq_kernel_q6k(ncols, rpb, lbt, mode);
+    case kTypeQ8_0: return mmvq_kernel_q80(ncols, rpb, lbt, mode);
     default: return nullptr;
     }
 }
 
-// Built-in B200 default when neither the caller nor the smithy table chose: 4 warps, and
-// tiles of about 6 KB (rows_per_block = largest power of two with rpb * row_bytes <= 6 KB).
+// Built-in B200 default when neither the caller nor the smithy table chose (measured on
+// the Qwen3-8B shape set with the nwarps x rows_per_block sweep): 8 warps; tiles of 4 rows
+// unless that leaves most warps of the GPU idle (small N), then 2 or 1.
 static void default_config(int t, int nrows, int K, int ncols, int *nw, int *rpb) {
-    (void)nrows;
+    (void)t;
+    (void)K;
     (void)ncols;
-    const int row_bytes = (K / mmvq_type_qk(t)) * mmvq_type_bytes(t);
-    int r = 1;
-    while (r < 8 && 2 * r * row_bytes <= 6144) r *= 2;
-    *nw = 4;
-    *rpb = r;
+    *nw = 8;
+    *rpb = nrows >= 4096 ? 4 : nrows >= 2048 ? 2 : 1;
 }
 
 struct Plan {
@@ -245,7 +244,9 @@ static int plan_mmvq(int t, int nrows, int K, int ncols, int nwarps, int rpb, in
                         K, ncols);
         }
     }
-    p->fn = kernel_for(t, ncols, rpb, mode);
+    // Lanes per row: the compile-time variants (16, 32) when the heuristic picks them.
+    const int lbt = host_lanes_per_row(K / qk, rpb);
+    p->fn = kernel_for(t, ncols, rpb, lbt, mode);
     p->mode = mode;
     if (!p->fn) return fail(ANVIL_ERR_UNSUPPORTED, "no kernel for ncols=%d rpb=%d", ncols, rpb);
     p->nwarps = nwarps;

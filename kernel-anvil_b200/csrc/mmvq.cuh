@@ -374,23 +374,24 @@ __device__ __forceinline__ int choose_lanes_per_row(int nblk, int rpb) {
     return best;
 }
 
-// Per-tile context shared by the unit steps of one block.  A lane computes the rows
-// slot * RG + grp of the tile for slot < nslots: every lane of the warp runs the same slot
-// at the same time, so row ownership never splits a warp's instruction stream.
+// Per-tile context shared by the unit steps of one block.  A lane computes rows
+// slot * RG + grp of the tile: every lane of the warp runs the same slot at the same time,
+// so row ownership never splits a warp's instruction stream.  Slots past the tile's last
+// row still compute (on stale stage bytes, inside the stage) and are simply not stored.
 struct TileCtx {
-    const uint8_t *wrow0;
-    int row_bytes, nrows, r0, rows, K, nkb, acb;
-    int RG, grp, nslots;
+    const uint8_t *lane_row0;  // stage row of slot 0 for this lane's group
+    int slot_stride;           // bytes between consecutive slots (RG rows)
+    int nrows, r0, rows, K, nkb, acb, RG, grp;
     const uint8_t *aq;
     const float *ad, *ads;
     const int2 *as;
     int32_t *sums;
 };
 
-// One compile-time unit U of block b for every slot and column.
-template <int QT, int NCOLS, int RPB, int MODE, int U>
-__device__ __forceinline__ void unit_step(const TileCtx &t, int b, const BlkHdr (&hdr)[RPB],
-                                          float (&acc)[RPB][NCOLS]) {
+// One compile-time unit U of block b for the NS slots and every column.
+template <int QT, int NCOLS, int NS, int MODE, int U>
+__device__ __forceinline__ void unit_step(const TileCtx &t, int b, const BlkHdr (&hdr)[NS],
+                                          float (&acc)[NS][NCOLS]) {
     using TR = QTraits<QT>;
     int kb0, kb1;
     unit_kb<QT, U>(b, kb0, kb1);
@@ -400,24 +401,25 @@ __device__ __forceinline__ void unit_step(const TileCtx &t, int b, const BlkHdr 
         load_act<QT>(v, kb0, a0);
         if constexpr (QT != kTypeQ8_0) load_act<QT>(v, kb1, a1);
     }
+    const uint8_t *blk0 = t.lane_row0 + b * TR::bytes;
 #pragma unroll
-    for (int sl = 0; sl < RPB; ++sl) {
-        const int i = sl * t.RG + t.grp;
-        if (sl < t.nslots && i < t.rows) {
-            const uint8_t *blk = t.wrow0 + i * t.row_bytes + b * TR::bytes;
-            WBytes wb;
-            load_unit<QT, U>(blk, wb);
+    for (int sl = 0; sl < NS; ++sl) {
+        const uint8_t *blk = blk0 + sl * t.slot_stride;
+        WBytes wb;
+        load_unit<QT, U>(blk, wb);
 #pragma unroll
-            for (int c = 0; c < NCOLS; ++c) {
-                if constexpr (NCOLS > 1) {
-                    const ActView v{t.aq + c * t.acb, t.ad + c * t.nkb, t.ads + c * t.nkb,
-                                    t.as + c * t.nkb};
-                    load_act<QT>(v, kb0, a0);
-                    if constexpr (QT != kTypeQ8_0) load_act<QT>(v, kb1, a1);
-                }
-                int isum[4];
-                acc[sl][c] += dot_unit<QT, U>(blk, hdr[sl], wb, a0, QT == kTypeQ8_0 ? a0 : a1, isum);
-                if constexpr (MODE == kModeSums) {
+        for (int c = 0; c < NCOLS; ++c) {
+            if constexpr (NCOLS > 1) {
+                const ActView v{t.aq + c * t.acb, t.ad + c * t.nkb, t.ads + c * t.nkb,
+                                t.as + c * t.nkb};
+                load_act<QT>(v, kb0, a0);
+                if constexpr (QT != kTypeQ8_0) load_act<QT>(v, kb1, a1);
+            }
+            int isum[4];
+            acc[sl][c] += dot_unit<QT, U>(blk, hdr[sl], wb, a0, QT == kTypeQ8_0 ? a0 : a1, isum);
+            if constexpr (MODE == kModeSums) {
+                const int i = sl * t.RG + t.grp;
+                if (i < t.rows) {
                     const int nsub = QT == kTypeQ6_K ? t.K / 16 : t.K / 32;
                     store_sums<QT>(t.sums + (size_t(c) * t.nrows + t.r0 + i) * nsub, kb0, kb1, isum);
                 }
@@ -455,7 +457,25 @@ __device__ __forceinline__ uint32_t pack_quants(int q) {
 
 // ---- the kernel --------------------------------------------------------------------------
 
-template <int QT, int NCOLS, int RPB, int MODE>
+// Host-side twin of choose_lanes_per_row (same arithmetic).
+inline int host_lanes_per_row(int nblk, int rpb) {
+    int best = 32;
+    float best_u = -1.f;
+    for (int lb = 32; lb >= 1; lb >>= 1) {
+        const int rg = 32 / lb;
+        const int per_lane = (nblk + lb - 1) / lb;
+        const float r = float(rpb) / float(rg);
+        const float u = float(nblk) / float(lb * per_lane) * (r < 1.f ? r : 1.f);
+        if (u > best_u + 1e-6f) {
+            best_u = u;
+            best = lb;
+        }
+    }
+    return best;
+}
+
+// LBT: lanes per row fixed at compile time (16 or 32), or 0 for the runtime choice.
+template <int QT, int NCOLS, int RPB, int MODE, int LBT>
 __global__ void __launch_bounds__(kMaxWarps * 32, NCOLS == 1 ? 2 : 1) mmvq_kernel(const MmvqArgs args) {
     using TR = QTraits<QT>;
     extern __shared__ __align__(16) uint8_t smem[];
@@ -573,65 +593,71 @@ __global__ void __launch_bounds__(kMaxWarps * 32, NCOLS == 1 ? 2 : 1) mmvq_kerne
             }
         }
     } else {
-        // Q8_1 blocks: 9 words each ({d, s} then 8 quant words); loads batched 8 deep.
+        // Q8_1 blocks, one per thread: 9 words ({d, s}, then 8 quant words) loaded together,
+        // written to the swizzled layout with the block's d8, d8 * sum(q) and half sums.
         const uint32_t *xw = reinterpret_cast<const uint32_t *>(args.x);
-        const int nw = NCOLS * nkb * 9;
-        for (int base = 0; base < nw; base += 8 * T) {
-            uint32_t v[8];
+        for (int c = 0; c < NCOLS; ++c) {
+            uint8_t *aqc = aq + c * acb;
+            for (int kb = tid; kb < nkb; kb += T) {
+                const uint32_t *src = xw + (size_t(c) * nkb + kb) * 9;
+                uint32_t v[9];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int i = base + j * T + tid;
-                v[j] = i < nw ? __ldg(xw + i) : 0u;
-            }
+                for (int w = 0; w < 9; ++w) v[w] = __ldg(src + w);
+                uint4 *d0 = reinterpret_cast<uint4 *>(aqc + act_chunk<QT>(2 * kb) * 16);
+                uint4 *d1 = reinterpret_cast<uint4 *>(aqc + act_chunk<QT>(2 * kb + 1) * 16);
+                *d0 = make_uint4(v[1], v[2], v[3], v[4]);
+                *d1 = make_uint4(v[5], v[6], v[7], v[8]);
+                int lo = 0, hi = 0;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int i = base + j * T + tid;
-                if (i < nw) {
-                    const int blk = i / 9, w = i - blk * 9;  // blk = c * nkb + kb
-                    if (w == 0) {
-                        ad[blk] = h2f(v[j]);
-                    } else {
-                        const int c = blk / nkb, kb = blk - c * nkb;
-                        *reinterpret_cast<uint32_t *>(aq + c * acb +
-                                                      act_chunk<QT>(2 * kb + ((w - 1) >> 2)) * 16 +
-                                                      ((w - 1) & 3) * 4) = v[j];
-                    }
+                for (int w = 0; w < 4; ++w) {
+                    lo = __dp4a(int(v[1 + w]), 0x01010101, lo);
+                    hi = __dp4a(int(v[5 + w]), 0x01010101, hi);
                 }
+                const float d8 = h2f(v[0]);
+                ad[c * nkb + kb] = d8;
+                as[c * nkb + kb] = make_int2(lo, hi);
+                ads[c * nkb + kb] = d8 * float(lo + hi);
             }
         }
     }
-    __syncthreads();
-    for (int i = tid; i < NCOLS * nkb; i += T) {
-        const int c = i / nkb, kb = i - c * nkb;
-        const uint8_t *base = aq + c * acb;
-        const uint4 q0 = *reinterpret_cast<const uint4 *>(base + act_chunk<QT>(2 * kb) * 16);
-        const uint4 q1 = *reinterpret_cast<const uint4 *>(base + act_chunk<QT>(2 * kb + 1) * 16);
-        int lo = 0, hi = 0;
-        lo = __dp4a(int(q0.x), 0x01010101, lo);
-        lo = __dp4a(int(q0.y), 0x01010101, lo);
-        lo = __dp4a(int(q0.z), 0x01010101, lo);
-        lo = __dp4a(int(q0.w), 0x01010101, lo);
-        hi = __dp4a(int(q1.x), 0x01010101, hi);
-        hi = __dp4a(int(q1.y), 0x01010101, hi);
-        hi = __dp4a(int(q1.z), 0x01010101, hi);
-        hi = __dp4a(int(q1.w), 0x01010101, hi);
-        as[i] = make_int2(lo, hi);
-        ads[i] = ad[i] * float(lo + hi);
+    if constexpr (MODE == kModeF32) {
+        __syncthreads();  // quants of the fused path are complete; derive the block sums
+        for (int i = tid; i < NCOLS * nkb; i += T) {
+            const int c = i / nkb, kb = i - c * nkb;
+            const uint8_t *base = aq + c * acb;
+            const uint4 q0 = *reinterpret_cast<const uint4 *>(base + act_chunk<QT>(2 * kb) * 16);
+            const uint4 q1 = *reinterpret_cast<const uint4 *>(base + act_chunk<QT>(2 * kb + 1) * 16);
+            int lo = 0, hi = 0;
+            lo = __dp4a(int(q0.x), 0x01010101, lo);
+            lo = __dp4a(int(q0.y), 0x01010101, lo);
+            lo = __dp4a(int(q0.z), 0x01010101, lo);
+            lo = __dp4a(int(q0.w), 0x01010101, lo);
+            hi = __dp4a(int(q1.x), 0x01010101, hi);
+            hi = __dp4a(int(q1.y), 0x01010101, hi);
+            hi = __dp4a(int(q1.z), 0x01010101, hi);
+            hi = __dp4a(int(q1.w), 0x01010101, hi);
+            as[i] = make_int2(lo, hi);
+            ads[i] = ad[i] * float(lo + hi);
+        }
     }
     __syncthreads();
 
     // ---- 3. lane -> (row group, blocks) mapping, fixed for all tiles -------------------
     // LB lanes split a row's blocks; the warp's RG = 32/LB lane groups take rows
-    // slot * RG + grp (nslots slots; groups beyond RPB stay idle when RPB < RG).
-    const int LB = choose_lanes_per_row(nblk, RPB);
+    // slot * RG + grp.  With a compile-time LB the slot count NS is static.
+    const int LB = LBT > 0 ? LBT : choose_lanes_per_row(nblk, RPB);
     const int RG = 32 / LB;
     const int bl = lane & (LB - 1);
     const int grp = lane / LB;
-    const int nslots = RPB >= RG ? RPB / RG : (grp < RPB ? 1 : 0);
+    constexpr int NS = LBT > 0 ? (RPB >= 32 / (LBT > 0 ? LBT : 32) ? RPB / (32 / (LBT > 0 ? LBT : 32)) : 1) : RPB;
+    // Runtime-LB kernels walk all RPB slots and mask the ones past nslots.
+    const int nslots = LBT > 0 ? NS : (RPB >= RG ? RPB / RG : 1);
+    const bool grp_live = grp < RPB;  // groups beyond the tile's rows (RPB < RG) stay idle
 
+    int st = 0;
+    uint32_t phase = 0;
     for (int k = 0; k < my_tiles; ++k) {
         const int tile = gwarp + k * wstride;
-        const int st = k % nstages;
         const int r0 = tile * RPB;
         const int rows = min(RPB, nrows - r0);
         const uint8_t *src = W + size_t(r0) * size_t(row_bytes);
@@ -639,11 +665,11 @@ __global__ void __launch_bounds__(kMaxWarps * 32, NCOLS == 1 ? 2 : 1) mmvq_kerne
         const uintptr_t e = s + size_t(rows) * row_bytes;
         uint8_t *wrow0 = ring + st * L.stage + int(s & 15);
 
-        bool have_w = mbar_wait_bounded(&full[st], (k / nstages) & 1, kWaitLimitNs);
+        bool have_w = mbar_wait_bounded(&full[st], phase, kWaitLimitNs);
         if (!have_w) {
             // The copy did not land in time: one more bounded wait so that it is not still
             // writing this stage when the warp moves on; the tile is then skipped.
-            (void)mbar_wait_bounded(&full[st], (k / nstages) & 1, kWaitLimitNs);
+            (void)mbar_wait_bounded(&full[st], phase, kWaitLimitNs);
         }
         if ((s | e) & 15) {  // unaligned ends: plain loads of at most 30 bytes
             const uintptr_t s_al = (s + 15) & ~uintptr_t(15), e_al = e & ~uintptr_t(15);
@@ -659,28 +685,51 @@ __global__ void __launch_bounds__(kMaxWarps * 32, NCOLS == 1 ? 2 : 1) mmvq_kerne
             __syncwarp();
         }
 
-        float acc[RPB][NCOLS];
+        float acc[NS][NCOLS];
 #pragma unroll
-        for (int i = 0; i < RPB; ++i)
+        for (int i = 0; i < NS; ++i)
 #pragma unroll
             for (int c = 0; c < NCOLS; ++c) acc[i][c] = 0.f;
 
-        if (have_w) {
-            const TileCtx ctx{wrow0, row_bytes, nrows, r0, rows, K, nkb, acb, RG, grp, nslots,
-                              aq, ad, ads, as, args.sums};
+        if (have_w && grp_live) {
+            const TileCtx ctx{wrow0 + grp * row_bytes, RG * row_bytes, nrows, r0, rows, K, nkb,
+                              acb, RG, grp, aq, ad, ads, as, args.sums};
             for (int b = bl; b < nblk; b += LB) {
-                BlkHdr hdr[RPB];
+                if (LBT > 0 || nslots == NS) {
+                    // slots sl < NS are rows sl * RG + grp <= RPB - 1: inside the stage
+                    BlkHdr hdr[NS];
 #pragma unroll
-                for (int sl = 0; sl < RPB; ++sl) {
-                    const int i = sl * RG + grp;
-                    if (sl < nslots && i < rows)
-                        hdr[sl] = load_hdr<QT>(wrow0 + i * row_bytes + b * TR::bytes);
-                }
-                unit_step<QT, NCOLS, RPB, MODE, 0>(ctx, b, hdr, acc);
-                if constexpr (Units<QT>::n == 4) {
-                    unit_step<QT, NCOLS, RPB, MODE, 1>(ctx, b, hdr, acc);
-                    unit_step<QT, NCOLS, RPB, MODE, 2>(ctx, b, hdr, acc);
-                    unit_step<QT, NCOLS, RPB, MODE, 3>(ctx, b, hdr, acc);
+                    for (int sl = 0; sl < NS; ++sl)
+                        hdr[sl] = load_hdr<QT>(ctx.lane_row0 + sl * ctx.slot_stride + b * TR::bytes);
+                    unit_step<QT, NCOLS, NS, MODE, 0>(ctx, b, hdr, acc);
+                    if constexpr (Units<QT>::n == 4) {
+                        unit_step<QT, NCOLS, NS, MODE, 1>(ctx, b, hdr, acc);
+                        unit_step<QT, NCOLS, NS, MODE, 2>(ctx, b, hdr, acc);
+                        unit_step<QT, NCOLS, NS, MODE, 3>(ctx, b, hdr, acc);
+                    }
+                } else {
+                    // runtime LB with fewer slots than RPB: only slot 0 .. nslots-1 are rows
+                    // of this lane; run them through the one-slot path.
+                    for (int sl = 0; sl < nslots; ++sl) {
+                        TileCtx c1 = ctx;
+                        c1.lane_row0 = ctx.lane_row0 + sl * ctx.slot_stride;
+                        c1.grp = grp + sl * RG;
+                        const BlkHdr h1[1] = {load_hdr<QT>(c1.lane_row0 + b * TR::bytes)};
+                        float a1[1][NCOLS];
+#pragma unroll
+                        for (int c = 0; c < NCOLS; ++c) a1[0][c] = 0.f;
+                        unit_step<QT, NCOLS, 1, MODE, 0>(c1, b, h1, a1);
+                        if constexpr (Units<QT>::n == 4) {
+                            unit_step<QT, NCOLS, 1, MODE, 1>(c1, b, h1, a1);
+                            unit_step<QT, NCOLS, 1, MODE, 2>(c1, b, h1, a1);
+                            unit_step<QT, NCOLS, 1, MODE, 3>(c1, b, h1, a1);
+                        }
+#pragma unroll
+                        for (int q = 0; q < NS; ++q)
+                            if (q == sl)
+#pragma unroll
+                                for (int c = 0; c < NCOLS; ++c) acc[q][c] += a1[0][c];
+                    }
                 }
             }
         }
@@ -688,29 +737,39 @@ __global__ void __launch_bounds__(kMaxWarps * 32, NCOLS == 1 ? 2 : 1) mmvq_kerne
         // ---- 4. reduction over the LB lanes sharing a row, then store ------------------
         if constexpr (MODE != kModeSums) {
 #pragma unroll
-            for (int sl = 0; sl < RPB; ++sl) {
-                if (sl < nslots || sl == 0) {  // uniform: nslots is 0 or equal across lanes
+            for (int sl = 0; sl < NS; ++sl) {
+                if (LBT > 0 || sl < nslots || sl == 0) {  // uniform across the warp
                     const int i = sl * RG + grp;
 #pragma unroll
                     for (int c = 0; c < NCOLS; ++c) {
                         float v = acc[sl][c];
-                        for (int o = LB >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-                        if (bl == 0 && sl < nslots && i < rows) args.y[size_t(c) * nrows + r0 + i] = v;
+                        if constexpr (LBT > 0) {
+#pragma unroll
+                            for (int o = LBT >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                        } else {
+                            for (int o = LB >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                        }
+                        if (bl == 0 && grp_live && sl < nslots && i < rows)
+                            args.y[size_t(c) * nrows + r0 + i] = v;
                     }
                 }
             }
         }
         __syncwarp();  // every lane is done with stage `st`
         if (lane == 0 && k + nstages < my_tiles) issue(tile + nstages * wstride, st);
+        if (++st == nstages) {
+            st = 0;
+            phase ^= 1u;
+        }
     }
 }
 
 // Host-side kernel table access, one instantiation file per type.
 using MmvqKernelFn = void (*)(MmvqArgs);
-MmvqKernelFn mmvq_kernel_q4k(int ncols, int rpb, int mode);
-MmvqKernelFn mmvq_kernel_q5k(int ncols, int rpb, int mode);
-MmvqKernelFn mmvq_kernel_q6k(int ncols, int rpb, int mode);
-MmvqKernelFn mmvq_kernel_q80(int ncols, int rpb, int mode);
+MmvqKernelFn mmvq_kernel_q4k(int ncols, int rpb, int lbt, int mode);
+MmvqKernelFn mmvq_kernel_q5k(int ncols, int rpb, int lbt, int mode);
+MmvqKernelFn mmvq_kernel_q6k(int ncols, int rpb, int lbt, int mode);
+MmvqKernelFn mmvq_kernel_q80(int ncols, int rpb, int lbt, int mode);
 // Reads and clears the device status word of that type's translation unit (current device).
 int mmvq_kernel_q4k_take_status();
 int mmvq_kernel_q5k_take_status();
@@ -719,38 +778,48 @@ int mmvq_kernel_q80_take_status();
 
 }  // namespace anvil
 
-// Builds the [ncols 1..8] x [rpb 1,2,4,8] x [mode] table for one type.
+// Builds the [ncols 1..8] x [rpb 1,2,4,8] x [mode] x [lanes per row 16 / 32 / runtime]
+// table for one type.  lbt is 16 or 32 for the compile-time variants, anything else for
+// the runtime-LB kernel.
 #define ANVIL_MMVQ_TABLE(FN, QT)                                                          \
     namespace anvil {                                                                     \
-    template <int NC, int R>                                                              \
+    template <int NC, int R, int LBT>                                                     \
     static MmvqKernelFn FN##_mode(int mode) {                                             \
         switch (mode) {                                                                   \
-        case kModeQ81: return mmvq_kernel<QT, NC, R, kModeQ81>;                           \
-        case kModeF32: return mmvq_kernel<QT, NC, R, kModeF32>;                           \
-        case kModeSums: return mmvq_kernel<QT, NC, R, kModeSums>;                         \
+        case kModeQ81: return mmvq_kernel<QT, NC, R, kModeQ81, LBT>;                      \
+        case kModeF32: return mmvq_kernel<QT, NC, R, kModeF32, LBT>;                      \
+        case kModeSums: return mmvq_kernel<QT, NC, R, kModeSums, LBT>;                    \
         default: return nullptr;                                                          \
         }                                                                                 \
+    }                                                                                     \
+    template <int NC, int R>                                                              \
+    static MmvqKernelFn FN##_lb(int lbt, int mode) {                                      \
+        if constexpr (NC == 1) {                                                          \
+            if (lbt == 16) return FN##_mode<NC, R, 16>(mode);                             \
+            if (lbt == 32) return FN##_mode<NC, R, 32>(mode);                             \
+        }                                                                                 \
+        return FN##_mode<NC, R, 0>(mode);                                                 \
     }                                                                                     \
     template <int NC>                                                                     \
-    static MmvqKernelFn FN##_pick(int rpb, int mode) {                                    \
+    static MmvqKernelFn FN##_pick(int rpb, int lbt, int mode) {                           \
         switch (rpb) {                                                                    \
-        case 1: return FN##_mode<NC, 1>(mode);                                            \
-        case 2: return FN##_mode<NC, 2>(mode);                                            \
-        case 4: return FN##_mode<NC, 4>(mode);                                            \
-        case 8: return FN##_mode<NC, 8>(mode);                                            \
+        case 1: return FN##_lb<NC, 1>(lbt, mode);                                         \
+        case 2: return FN##_lb<NC, 2>(lbt, mode);                                         \
+        case 4: return FN##_lb<NC, 4>(lbt, mode);                                         \
+        case 8: return FN##_lb<NC, 8>(lbt, mode);                                         \
         default: return nullptr;                                                          \
         }                                                                                 \
     }                                                                                     \
-    MmvqKernelFn FN(int ncols, int rpb, int mode) {                                       \
+    MmvqKernelFn FN(int ncols, int rpb, int lbt, int mode) {                              \
         switch (ncols) {                                                                  \
-        case 1: return FN##_pick<1>(rpb, mode);                                           \
-        case 2: return FN##_pick<2>(rpb, mode);                                           \
-        case 3: return FN##_pick<3>(rpb, mode);                                           \
-        case 4: return FN##_pick<4>(rpb, mode);                                           \
-        case 5: return FN##_pick<5>(rpb, mode);                                           \
-        case 6: return FN##_pick<6>(rpb, mode);                                           \
-        case 7: return FN##_pick<7>(rpb, mode);                                           \
-        case 8: return FN##_pick<8>(rpb, mode);                                           \
+        case 1: return FN##_pick<1>(rpb, lbt, mode);                                      \
+        case 2: return FN##_pick<2>(rpb, lbt, mode);                                      \
+        case 3: return FN##_pick<3>(rpb, lbt, mode);                                      \
+        case 4: return FN##_pick<4>(rpb, lbt, mode);                                      \
+        case 5: return FN##_pick<5>(rpb, lbt, mode);                                      \
+        case 6: return FN##_pick<6>(rpb, lbt, mode);                                      \
+        case 7: return FN##_pick<7>(rpb, lbt, mode);                                      \
+        case 8: return FN##_pick<8>(rpb, lbt, mode);                                      \
         default: return nullptr;                                                          \
         }                                                                                 \
     }                                                                                     \
