@@ -164,15 +164,20 @@ static MmvqKernelFn kernel_for(int t, int ncols, int rpb, int lbt, int mode) {
     }
 }
 
-// Built-in B200 default when neither the caller nor the smithy table chose (measured on
-// the Qwen3-8B shape set with the nwarps x rows_per_block sweep): 8 warps; tiles of 4 rows
-// unless that leaves most warps of the GPU idle (small N), then 2 or 1.
+// Built-in B200 default when neither the caller nor the smithy table chose, from the
+// nwarps x rows_per_block sweep over the Qwen3-8B shapes: 4 warps with 4-row tiles (2 rows
+// when K >= 8192); small N (< 2048 rows) prefers 8 warps of 1-row tiles so every warp has
+// a row.
 static void default_config(int t, int nrows, int K, int ncols, int *nw, int *rpb) {
     (void)t;
-    (void)K;
     (void)ncols;
-    *nw = 8;
-    *rpb = nrows >= 4096 ? 4 : nrows >= 2048 ? 2 : 1;
+    if (nrows < 2048) {
+        *nw = 8;
+        *rpb = 1;
+    } else {
+        *nw = 4;
+        *rpb = K >= 8192 ? 2 : 4;
+    }
 }
 
 struct Plan {
