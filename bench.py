@@ -231,11 +231,15 @@ def dominant_kernel(dc, stream, steps: int, warmup: int) -> dict:
 
 
 def traffic_per_launch() -> float | None:
-    p = ROOT / "profiles" / "mmvq_q4k_qwen3_8b_traffic.json"
+    """dram read+write bytes per Q4_K MMVQ launch from the committed ncu launch list."""
+    p = ROOT / "profiles" / "mmvq_launches_qwen3_8b.md"
     try:
-        return float(json.loads(p.read_text())["dram_bytes_per_launch"])
-    except Exception:
-        return None
+        for line in p.read_text().splitlines():
+            if line.startswith("dram_bytes_per_launch:"):
+                return float(line.split(":", 1)[1])
+    except OSError:
+        pass
+    return None
 
 
 def run_anvil(args) -> None:
