@@ -1,0 +1,82 @@
+"""Kernel profiling for bottleneck analysis (B200 replacement of kernel_anvil/profile.py:37-91).
+
+``profile_kernel`` times a callable with CUDA events and returns ProfileMetrics.  When the
+config names an MMVQ launch (``quant``/``n``/``k`` keys, as the gguf-optimize runner passes),
+registers, shared memory and occupancy come from the library's real launch plan instead of
+the reference's estimates.  ``ncu_metrics`` runs a command under ncu for DRAM counters (the
+role rocprofv3 played for the reference, kernel_anvil/llama_sweep.py:64-136).
+"""
+from __future__ import annotations
+
+import csv
+import io
+import shutil
+import subprocess
+
+from kernel_anvil.analyze import ProfileMetrics
+from kernel_anvil.specs import GpuSpec
+from kernel_anvil.verify import _benchmark
+
+
+def _mmvq_resources(config: dict) -> tuple[int, int, int] | None:
+    """(registers/thread, smem bytes, threads/block) of the MMVQ launch a config describes."""
+    try:
+        from kernel_anvil import mmvq as ops
+
+        plan = ops.plan(config["quant"], config["n"], config["k"], config.get("ncols", 1),
+                        config.get("nwarps", 0), config.get("rows_per_block", 0))
+    except Exception:
+        return None
+    return config.get("regs_per_thread", 0), plan["smem_bytes"], plan["nwarps"] * 32
+
+
+def profile_kernel(kernel_fn, config: dict, data_bytes: int | None = None,
+                   gpu_spec: GpuSpec | None = None, warmup: int = 5, runs: int = 20) -> ProfileMetrics:
+    latency_us = _benchmark(kernel_fn, config, warmup, runs)
+    bw = data_bytes / (latency_us * 1e-6) / 1e9 if data_bytes and latency_us > 0 else 0.0
+    regs, smem, threads = 0, 0, config.get("nwarps", config.get("num_warps", 4)) * 32
+    res = _mmvq_resources(config)
+    if res is not None:
+        regs, smem, threads = res
+    occ, factor = 0.0, "unknown"
+    if gpu_spec is not None and (regs or smem):
+        occ, factor = gpu_spec.occupancy(regs, smem, threads)
+    return ProfileMetrics(duration_ns=latency_us * 1000, regs_per_thread=regs, smem_bytes=smem,
+                          spill_bytes=0, bandwidth_gbs=bw, occupancy_pct=occ, limiting_factor=factor,
+                          threads_per_block=threads)
+
+
+NCU_METRICS = ("gpu__time_duration.sum", "dram__bytes_read.sum", "dram__bytes_write.sum")
+
+
+def parse_ncu_csv(text: str) -> list[dict]:
+    """Rows of an `ncu --csv` metrics log as {kernel, metric: value} dicts (one per launch)."""
+    lines = text.splitlines()
+    start = next((i for i, ln in enumerate(lines) if ln.startswith('"ID"')), None)
+    if start is None:
+        return []
+    reader = csv.reader(io.StringIO("\n".join(lines[start:])))
+    hdr = next(reader)
+    ki, mi, ui, vi, idi = (hdr.index(k) for k in ("Kernel Name", "Metric Name", "Metric Unit",
+                                                   "Metric Value", "ID"))
+    scale = {"byte": 1, "Kbyte": 1e3, "Mbyte": 1e6, "Gbyte": 1e9, "nsecond": 1e-3, "ns": 1e-3,
+             "usecond": 1.0, "us": 1.0, "msecond": 1e3, "ms": 1e3}
+    launches: dict[str, dict] = {}
+    for r in reader:
+        if len(r) <= vi:
+            continue
+        d = launches.setdefault(r[idi], {"kernel": r[ki].split("(")[0].replace("void ", "")})
+        d[r[mi]] = float(r[vi].replace(",", "")) * scale.get(r[ui], 1.0)
+    return list(launches.values())
+
+
+def ncu_metrics(cmd: list[str], kernel_regex: str = "mmvq", launches: int = 1, skip: int = 0,
+                metrics=NCU_METRICS, timeout: int = 600) -> list[dict]:
+    """Run `cmd` under ncu (clocks left alone) and return per-launch metrics; times in µs."""
+    ncu = shutil.which("ncu") or "/usr/local/cuda/bin/ncu"
+    full = [ncu, "--clock-control", "none", "--csv", "--metrics", ",".join(metrics),
+            "-k", f"regex:{kernel_regex}", "-s", str(skip), "-c", str(launches), *cmd]
+    r = subprocess.run(full, capture_output=True, text=True, timeout=timeout)
+    if r.returncode != 0:
+        raise RuntimeError(f"ncu failed ({r.returncode}): {r.stderr[-2000:]}")
+    return parse_ncu_csv(r.stdout)
