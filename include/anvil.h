@@ -127,6 +127,20 @@ int anvil_mmvq_f32_ex(int ggml_type, const void *W, const float *x, void *xq, fl
                       int nrows, int ncols_x, int ncols_dst, int nwarps, int rows_per_block,
                       unsigned flags, anvil_stream_t stream);
 
+/* anvil_mmvq_f32 without caller scratch and without any device allocation: the Q8_1
+ * intermediate lives in a 1 MiB static device buffer inside libanvil.  No counterpart in
+ * the reference.  For hosts that may not allocate device memory while decoding (a
+ * device budget reserved before the first token; cudaFree synchronising the device).
+ * Limit: ncols_dst * (ncols_x/32) * 36 <= 1048576 bytes (K <= 932064 for one column,
+ * 116480 for eight), else ANVIL_ERR_INVALID and nothing is launched.  Set-up: the first
+ * call on each device (that device current) looks the buffer's address up with
+ * cudaGetSymbolAddress; make it outside any stream capture.  The buffer needs no zeroing.
+ * All calls on a device share it: calls whose launches overlap (unordered streams,
+ * several threads) race, so order them. */
+int anvil_mmvq_f32_noalloc(int ggml_type, const void *W, const float *x, float *y, int nrows,
+                           int ncols_x, int ncols_dst, int nwarps, int rows_per_block,
+                           anvil_stream_t stream);
+
 /* Reads and clears the device status words of the current device: the OR of
  * anvil_device_status flags set by kernels whose bounded waits gave up (0 = none),
  * or a negative anvil_status.  Synchronous. */

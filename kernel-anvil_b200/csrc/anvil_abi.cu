@@ -641,3 +641,71 @@ int anvil_chain_launch(anvil_chain *c, anvil_stream_t stream) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------
+// Allocation-free fp32 GEMV (anvil_mmvq_f32_noalloc).  Same result as anvil_mmvq_f32's
+// two-launch path -- quantise x to Q8_1, then the Q8_1 GEMV -- but the Q8_1 intermediate
+// lives in the file-scope device buffer below instead of caller scratch, so the call
+// allocates no device memory and needs none from the caller.  It serves callers that may
+// not allocate while decoding: hosts that reserve their whole device budget before the
+// first token (llama.cpp's ggml allocator sizes its compute buffers up front, and a later
+// cudaMalloc can fail or fragment what is left), and hosts on a latency-critical path,
+// where cudaFree would synchronise the whole device.
+//
+// Set-up: the first call on each device, with that device current, looks the buffer's
+// device address up with cudaGetSymbolAddress and keeps it; make that first call outside
+// any stream capture.  Nothing in the buffer has to start at zero: the quantiser writes
+// every byte the GEMV then reads.  All calls on one device share the buffer, so calls
+// whose launches overlap (different streams without ordering between them, or several
+// host threads) race on it: order them on one stream or with events.
+// ---------------------------------------------------------------------------------
+namespace anvil {
+
+// 1 MiB = ncols * (K/32) * 36 bytes of Q8_1 blocks: K up to 932,064 for one column,
+// 116,480 for eight.
+constexpr size_t kStaticXqBytes = size_t(1) << 20;
+static __device__ __align__(256) uint8_t g_static_xq[kStaticXqBytes];
+static void *g_static_xq_addr[kMaxDevices];  // device address of g_static_xq, per device
+static std::mutex g_static_xq_mu;
+
+// Device address of g_static_xq on `dev` (which must be the current device), looked up
+// once per device.
+static int static_xq_addr(int dev, void **out) {
+    std::lock_guard<std::mutex> lock(g_static_xq_mu);
+    if (!g_static_xq_addr[dev]) {
+        void *ptr = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress((void **)&ptr, g_static_xq);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_static_xq)");
+        g_static_xq_addr[dev] = ptr;
+    }
+    *out = g_static_xq_addr[dev];
+    return ANVIL_OK;
+}
+
+}  // namespace anvil
+
+extern "C" int anvil_mmvq_f32_noalloc(int ggml_type, const void *W, const float *x, float *y,
+                                      int nrows, int ncols_x, int ncols_dst, int nwarps,
+                                      int rows_per_block, anvil_stream_t stream) {
+    if (!x) return fail(ANVIL_ERR_INVALID, "null pointer argument");
+    if (ncols_x <= 0 || ncols_x % 32 != 0)
+        return fail(ANVIL_ERR_INVALID, "K=%d is not a positive multiple of 32", ncols_x);
+    if (ncols_dst < 1) return fail(ANVIL_ERR_INVALID, "ncols=%d", ncols_dst);
+    const size_t need = size_t(ncols_dst) * size_t(ncols_x / 32) * kQ8_1Bytes;
+    if (need > kStaticXqBytes)
+        return fail(ANVIL_ERR_INVALID,
+                    "anvil_mmvq_f32_noalloc: the Q8_1 activation needs %zu bytes (%d columns of "
+                    "K=%d), more than its %zu-byte static buffer; use anvil_mmvq_f32 with caller "
+                    "scratch", need, ncols_dst, ncols_x, kStaticXqBytes);
+    int dev;
+    if (int s = current_device(&dev)) return s;
+    void *xq = nullptr;
+    if (int s = static_xq_addr(dev, &xq)) return s;
+    if (int s = check_mmvq_ptrs(ggml_type, W, xq, y)) return s;
+    Plan p;
+    if (int s = plan_mmvq(ggml_type, nrows, ncols_x, ncols_dst, nwarps, rows_per_block, kModeQ81, &p))
+        return s;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (int s = launch_quantize(x, xq, ncols_x, ncols_dst, 0, st)) return s;
+    return launch_mmvq(p, W, xq, y, nullptr, nrows, ncols_x, ANVIL_FLAG_PDL, st);
+}

@@ -136,6 +136,8 @@ SIGNATURES = {
                                c_int, c_int, c_void_p]),
     "anvil_mmvq_f32_ex": (c_int, [c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
                                   c_int, c_int, c_uint, c_void_p]),
+    "anvil_mmvq_f32_noalloc": (c_int, [c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
+                                       c_int, c_int, c_void_p]),
     "anvil_take_device_status": (c_int, []),
     "anvil_mmvq_block_sums": (c_int, [c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
                                       c_int, c_void_p]),
