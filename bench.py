@@ -349,6 +349,9 @@ def run_anvil(args) -> None:
 
     status = ops.take_device_status()
     if graph is not None:
+        # the graph holds NCCL work: release it before the process group goes away
+        launch = e2e_step = None
+        graph.reset()
         del graph
     dc.close()
     if world > 1:
