@@ -116,7 +116,8 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
 }
 
 // Bulk (non-tensor) async copy global -> shared, completion signalled on `bar`.
-// dst, src 16-byte aligned; bytes a multiple of 16.  No multicast.
+// dst, src 16-byte aligned; bytes a multiple of 16.  Only this CTA's shared memory is
+// written (no cluster-wide delivery).
 __device__ __forceinline__ void bulk_copy_g2s(void *dst, const void *src, uint32_t bytes,
                                               uint64_t *bar) {
     asm volatile(
