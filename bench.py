@@ -3,23 +3,32 @@
 
 A "step" is one token's pass over the chain: every distinct input quantised to Q8_1
 and every weight matrix multiplied once (the default workload, qwen3_8b: 253 GEMVs over
-4.51 GB of Q4_K/Q6_K weights plus 145 quantisations).  Weights are synthetic (seeded,
-drawn on the GPU in GGUF block layout with the workload's value distributions) and far
-larger than L2, so every step streams them from HBM.
+4.51 GB of Q4_K/Q6_K weights, 145 distinct inputs).  Weights are synthetic (seeded, drawn
+on the GPU in GGUF block layout with the workload's value distributions) and far larger
+than L2, so every step streams them from HBM.
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl anvil|reference]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME]
+                  [--executor persistent|graph] [--impl anvil|reference]
+
+Executors: "graph" replays a CUDA graph of separate quantize + MMVQ launches with
+programmatic dependent launch; "persistent" runs the token as one cooperative kernel (groups
+of GEMVs sharing an input, Q8_1 quantisation inside the kernel, a grid barrier before each
+group that depends on earlier ones).  The default, "auto", takes the graph on one GPU and
+the persistent kernel on several (no collective library in the data path).
 
 One JSON line is printed by rank 0:
   value        chain bytes / device time, whole job (GB/s): weights + Q8_1 reads + fp32
-               outputs, timed with CUDA events around K graph replays, max over ranks
+               outputs, timed with CUDA events around K launches, max over ranks
   e2e          the same metric through the public API with the step's fp32 inputs copied
                host->device from pinned memory and the logits copied back, every step
-  roofline     the dominant kernel (Q4_K MMVQ): algorithmic bytes per launch / average
-               launch time measured here with CUDA events, against measured HBM copy bandwidth
+  roofline     the dominant kernel: algorithmic bytes per launch / average launch time
+               measured here with CUDA events, against measured HBM copy bandwidth
   cpu_baseline the CPU oracle (oracle/, all host threads) on a bounded sample of the same
                workload (layer 0 of the chain), rank 0 at N=1 only
-With N > 1 (torchrun) each rank holds a row shard of every matrix and each GEMV's fp32
-output is all-gathered with NCCL (captured in the CUDA graph): strong scaling.
+With N > 1 (torchrun) each rank holds a row shard of every matrix (strong scaling).  The
+persistent executor writes each output row into every rank's output buffer over NVLink
+(CUDA IPC peer stores) inside the kernel; the graph executor all-gathers each GEMV's
+output with NCCL inside the CUDA graph.
 --impl reference times the CPU oracle port on the same workload (rank 0 only).
 """
 from __future__ import annotations
@@ -55,7 +64,12 @@ def parse_args():
     ap.add_argument("--quantize", choices=["fused", "separate"], default="separate",
                     help="quantise each GEMV input in its own kernel or inside the GEMV (fused)")
     ap.add_argument("--coresident", type=int, default=1,
-                    help="GEMV kernels sized to share each SM (2: the next GEMV prefetches during this one)")
+                    help="graph executor: GEMV kernels sized to share each SM")
+    ap.add_argument("--executor", choices=["auto", "persistent", "graph"], default="auto",
+                    help="one persistent kernel per token, or a CUDA graph of per-GEMV launches "
+                         "(auto: graph on one GPU, persistent with peer stores on several)")
+    ap.add_argument("--nwarps", type=int, default=0, help="persistent executor: warps per CTA (0 = 8)")
+    ap.add_argument("--ctas-per-sm", type=int, default=0, help="persistent executor: CTAs per SM (0 = 1)")
     return ap.parse_args()
 
 
@@ -230,15 +244,16 @@ def dominant_kernel(dc, stream, steps: int, warmup: int) -> dict:
     return {"launches_per_step": n, "bytes_per_launch": nbytes / n, "ms_per_launch": ms / n}
 
 
-def traffic_per_launch() -> float | None:
-    """dram read+write bytes per Q4_K MMVQ launch from the committed ncu launch list."""
-    p = ROOT / "profiles" / "mmvq_launches_qwen3_8b.md"
-    try:
-        for line in p.read_text().splitlines():
-            if line.startswith("dram_bytes_per_launch:"):
-                return float(line.split(":", 1)[1])
-    except OSError:
-        pass
+def traffic_per_launch(kernel: str) -> float | None:
+    """dram read+write bytes per launch of `kernel` from the committed ncu summaries (a line
+    `<kernel> dram_bytes_per_launch: N`); None when not captured."""
+    for p in sorted((ROOT / "profiles").glob("*.md")):
+        try:
+            for line in p.read_text().splitlines():
+                if line.startswith(f"{kernel} dram_bytes_per_launch:"):
+                    return float(line.split(":", 1)[1])
+        except OSError:
+            pass
     return None
 
 
@@ -261,18 +276,25 @@ def run_anvil(args) -> None:
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
 
     spec = get_chain(args.workload)
+    if args.executor == "auto":
+        args.executor = "graph" if world == 1 else "persistent"
+    persistent = args.executor == "persistent"
     dc = DeviceChain(spec, rank=rank, world=world, device=dev, fused=args.quantize == "fused",
-                     coresident=args.coresident)
+                     coresident=args.coresident, executor=args.executor,
+                     dist=dist if world > 1 else None, nwarps=args.nwarps,
+                     ctas_per_sm=args.ctas_per_sm)
     stream = torch.cuda.Stream(device=dev)
     hbm_peak, peak_kind = measured_peaks()
     total_bytes = spec.algorithmic_bytes()  # whole job: all shards together
+    rank_bytes = dc.algorithmic_bytes       # this rank's shard
 
     graph = None
-    if world == 1:
+    launches_per_step = dc.launches_per_step
+    n_quantize = dc.chain.n_quantize if dc.chain else 0
+    if world == 1 or persistent:
         with torch.cuda.stream(stream):
             dc.instantiate(pdl=True)
         launch = dc.launch
-        launches_per_step = dc.chain.n_mmvq + dc.chain.n_quantize
     else:
         from kernel_anvil.sharded import ShardedStep
         step = ShardedStep(dc, dist)
@@ -282,7 +304,6 @@ def run_anvil(args) -> None:
             with torch.cuda.graph(graph, stream=stream):
                 step.eager()
         launch = graph.replay
-        launches_per_step = dc.chain.n_mmvq + dc.chain.n_quantize
 
     def barrier():
         if world > 1:
@@ -301,6 +322,7 @@ def run_anvil(args) -> None:
     clk = clocks.stop()
     torch.cuda.synchronize()
     barrier()
+    ms_rank = ms
     if world > 1:
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -335,19 +357,36 @@ def run_anvil(args) -> None:
            "ms_per_step": round(ms_e2e, 4)}
 
     # ---- dominant kernel roofline -----------------------------------------------------------
-    dk = dominant_kernel(dc, stream, args.steps, args.warmup)
-    achieved = dk["bytes_per_launch"] / (dk["ms_per_launch"] * 1e-3) / 1e9
-    traffic = traffic_per_launch()
-    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
-                "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
-                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
-                else "fallback 6.65 TB/s",
-                "kernel": "mmvq_kernel<Q4_K, ncols=1> (all Q4_K GEMVs of one step, PDL graph)",
-                "launches_per_step": dk["launches_per_step"],
-                "bytes_per_launch": round(dk["bytes_per_launch"]),
-                "us_per_launch": round(dk["ms_per_launch"] * 1e3, 3)}
+    peak_source = (f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                   else "fallback 6.65 TB/s")
+    if persistent:
+        # one launch per token: the kernel is the step; this rank's bytes over its time
+        achieved = rank_bytes / (ms_rank * 1e-3) / 1e9
+        roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                    "frac": round(achieved / hbm_peak, 4),
+                    "traffic": traffic_per_launch(f"pchain_kernel {args.workload}"),
+                    "peak_source": peak_source,
+                    "kernel": f"pchain_kernel<ncols={dc.ncols}> (whole token, one cooperative launch)",
+                    "launches_per_step": 1, "bytes_per_launch": rank_bytes,
+                    "us_per_launch": round(ms_rank * 1e3, 3)}
+    else:
+        dk = dominant_kernel(dc, stream, args.steps, args.warmup)
+        achieved = dk["bytes_per_launch"] / (dk["ms_per_launch"] * 1e-3) / 1e9
+        roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                    "frac": round(achieved / hbm_peak, 4), "traffic": traffic_per_launch("mmvq_kernel"),
+                    "peak_source": peak_source,
+                    "kernel": "mmvq_kernel<Q4_K, ncols=1> (all Q4_K GEMVs of one step, PDL graph)",
+                    "launches_per_step": dk["launches_per_step"],
+                    "bytes_per_launch": round(dk["bytes_per_launch"]),
+                    "us_per_launch": round(dk["ms_per_launch"] * 1e3, 3)}
 
     status = ops.take_device_status()
+    pinfo, n_groups = None, 0
+    if persistent:
+        from kernel_anvil.pchain import take_status
+        status |= take_status()
+        pinfo = dc.pchain.info()
+        n_groups = dc.pchain.n_groups
     if graph is not None:
         # the graph holds NCCL work: release it before the process group goes away
         launch = e2e_step = None
@@ -365,14 +404,22 @@ def run_anvil(args) -> None:
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "int8 dp4a / fp32", "data": "synthetic",
         "config": {"workload": f"{args.workload} per-token GEMV chain",
-                   "gemvs_per_step": len(spec.gemvs), "quantizations_per_step": dc.chain.n_quantize,
+                   "gemvs_per_step": len(spec.gemvs),
+                   "quantizations_per_step": n_groups if persistent else n_quantize,
                    "bytes_per_step": total_bytes, "weight_bytes": spec.weight_bytes(),
                    "us_per_token": round(ms * 1e3, 1), "pct_of_hbm_peak": round(100 * value / hbm_peak, 1),
                    "pct_of_8TBps": round(100 * value / 8000.0, 1),
                    "l2": "inputs larger than L2 (weights stream from HBM every step)",
-                   "parallelism": f"row-shard x{world} + NCCL all-gather" if world > 1 else "single GPU",
-                   "graph": "CUDA graph, programmatic dependent launch between kernels",
-                   "quantize": args.quantize, "coresident_kernels_per_sm": args.coresident},
+                   "parallelism": (f"row-shard x{world}, " + ("outputs written to every rank over NVLink "
+                                   "(CUDA IPC peer stores) inside the kernel" if persistent else
+                                   "NCCL all-gather per GEMV")) if world > 1 else "single GPU",
+                   "executor": ("one persistent cooperative kernel per token: groups of GEMVs sharing an "
+                                "input, Q8_1 quantisation in-kernel, grid barrier between dependent groups"
+                                if persistent else
+                                "CUDA graph of quantize + MMVQ launches, programmatic dependent launch"),
+                   "quantize": "in-kernel per group" if persistent else args.quantize,
+                   **({"persistent": pinfo} if persistent else
+                      {"coresident_kernels_per_sm": args.coresident})},
         "e2e": e2e, "roofline": roofline, "gpu_launches": launches_per_step * args.steps,
         "device_status": status,
     }

@@ -192,6 +192,58 @@ int anvil_chain_instantiate(anvil_chain *chain, int use_pdl, anvil_stream_t stre
 int anvil_chain_launch(anvil_chain *chain, anvil_stream_t stream);
 int anvil_chain_num_steps(const anvil_chain *chain);
 
+/* ---- persistent chain: one cooperative launch per token ------------------ */
+
+/* The same per-token GEMV sequence as anvil_chain, run by one persistent kernel.  No
+ * counterpart kernel in the reference (its chain is a stream of separate mul_mat_vec_q
+ * launches, docs/decode-pipeline-breakdown.md:20-21); each GEMV computes exactly what
+ * anvil_mmvq computes for its rows.
+ *
+ * Groups: GEMVs added after anvil_pchain_add_group read that group's fp32 input x
+ * (ncols x K, 16-byte aligned), which every CTA quantises to Q8_1 itself with the
+ * arithmetic of anvil_quantize_q8_1.  wait_prev = 1 makes the group wait until every
+ * GEMV before it has finished (a grid barrier; 0 = independent, e.g. k after q).
+ * The weight stream runs ahead across groups.
+ *
+ * Ranks: world > 1 row-shards every matrix.  Rank r passes its rows [row0, row0 + nrows)
+ * of an nrows_full-row matrix, and y[q] = rank q's full output buffer (ncols x
+ * nrows_full, reachable from this GPU: a peer mapping from anvil_ipc_open); each output
+ * row is written to all ranks' buffers.  counters[q] = rank q's array of at least
+ * (number of groups) zeroed uint32 words, the same layout on every rank; every rank must
+ * build the same groups with the same nwarps / ctas_per_sm.  With world = 1, y[0] is the
+ * output and counters are allocated by the chain unless set.
+ *
+ * Every wait in the kernel is bounded (2 s); one that gives up sets a flag read by
+ * anvil_pchain_take_status (2 = barrier, 1 = weight copy) and the chain must be rebuilt. */
+#define ANVIL_MAX_RANKS 8
+typedef struct anvil_pchain anvil_pchain;
+
+anvil_pchain *anvil_pchain_create(int world, int rank);
+void anvil_pchain_destroy(anvil_pchain *chain);
+int anvil_pchain_add_group(anvil_pchain *chain, const float *x, int K, int ncols, int wait_prev);
+/* rows_per_block: rows per weight tile (0 = built-in default); lanes per row are chosen
+ * to keep the most lanes busy (read back with anvil_pchain_gemv_shape). */
+int anvil_pchain_add_gemv(anvil_pchain *chain, int ggml_type, const void *W, int nrows, int row0,
+                          int nrows_full, float *const *y, int rows_per_block);
+int anvil_pchain_set_counters(anvil_pchain *chain, uint32_t *const *counters);
+/* nwarps per CTA (0 = 8), CTAs per SM (0 = 1); allocates the device descriptors. */
+int anvil_pchain_instantiate(anvil_pchain *chain, int nwarps, int ctas_per_sm);
+/* One token: a cooperative launch on `stream`.  Not for stream capture. */
+int anvil_pchain_launch(anvil_pchain *chain, anvil_stream_t stream);
+int anvil_pchain_info(const anvil_pchain *chain, int *grid, int *nwarps, int *ring_bytes,
+                      int *smem_bytes, int *ngroups);
+int anvil_pchain_gemv_shape(const anvil_pchain *chain, int index, int *rows_per_block,
+                            int *lanes_per_row);
+/* Reads and clears the persistent kernel's device status flags (current device). */
+int anvil_pchain_take_status(void);
+
+/* Device buffers shared between the ranks' processes (CUDA IPC): allocate (zeroed) and
+ * export a 64-byte handle; open a peer's handle into this process; close; free. */
+int anvil_ipc_alloc(size_t bytes, void **ptr, void *handle);
+int anvil_ipc_open(const void *handle, void **ptr);
+int anvil_ipc_close(void *ptr);
+int anvil_ipc_free(void *ptr);
+
 /* ---- smithy runtime config (replaces patches/smithy-config.h) ------------ */
 
 /* patches/smithy-config.h:44-50: <=128 -> 0, <=1024 -> 1, <=4096 -> 2, <=16384 -> 3, else 4. */

@@ -14,6 +14,7 @@
 #include <vector>
 
 #include "anvil.h"
+#include "anvil_host.h"
 #include "mmvq.cuh"
 
 namespace anvil {
@@ -62,7 +63,7 @@ static int take_quantize_status() {
 // ---------------------------------------------------------------------------------
 static thread_local std::string t_last_error;
 
-static int fail(int status, const char *fmt, ...) {
+int fail(int status, const char *fmt, ...) {
     char buf[512];
     va_list ap;
     va_start(ap, fmt);
@@ -72,7 +73,7 @@ static int fail(int status, const char *fmt, ...) {
     return status;
 }
 
-static int cuda_fail(cudaError_t e, const char *what) {
+int cuda_fail(cudaError_t e, const char *what) {
     return fail(ANVIL_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
 }
 
@@ -103,14 +104,14 @@ struct FnKeyHash {
 static std::unordered_map<FnKey, int, FnKeyHash> g_occ_cache;
 static std::unordered_map<uint64_t, bool> g_attr_set;  // (fn, dev) -> max smem attribute set
 
-static int current_device(int *dev) {
+int current_device(int *dev) {
     cudaError_t e = cudaGetDevice(dev);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
     if (*dev < 0 || *dev >= kMaxDevices) return fail(ANVIL_ERR_UNSUPPORTED, "device %d", *dev);
     return ANVIL_OK;
 }
 
-static int sm_count(int dev, int *out) {
+int sm_count(int dev, int *out) {
     int n = g_dev[dev].sm_count.load(std::memory_order_relaxed);
     if (n == 0) {
         cudaError_t e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);

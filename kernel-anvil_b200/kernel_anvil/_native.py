@@ -67,7 +67,7 @@ def _sources() -> list[Path]:
 
 
 def _headers() -> list[Path]:
-    return sorted(CSRC.glob("*.cuh")) + sorted(INCLUDE.glob("*.h"))
+    return sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.h")) + sorted(INCLUDE.glob("*.h"))
 
 
 def needs_build() -> bool:
@@ -153,6 +153,20 @@ SIGNATURES = {
     "anvil_chain_instantiate": (c_int, [c_void_p, c_int, c_void_p]),
     "anvil_chain_launch": (c_int, [c_void_p, c_void_p]),
     "anvil_chain_num_steps": (c_int, [c_void_p]),
+    "anvil_pchain_create": (c_void_p, [c_int, c_int]),
+    "anvil_pchain_destroy": (None, [c_void_p]),
+    "anvil_pchain_add_group": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int]),
+    "anvil_pchain_add_gemv": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_void_p, c_int]),
+    "anvil_pchain_set_counters": (c_int, [c_void_p, c_void_p]),
+    "anvil_pchain_instantiate": (c_int, [c_void_p, c_int, c_int]),
+    "anvil_pchain_launch": (c_int, [c_void_p, c_void_p]),
+    "anvil_pchain_info": (c_int, [c_void_p, _PI, _PI, _PI, _PI, _PI]),
+    "anvil_pchain_gemv_shape": (c_int, [c_void_p, c_int, _PI, _PI]),
+    "anvil_pchain_take_status": (c_int, []),
+    "anvil_ipc_alloc": (c_int, [ctypes.c_size_t, ctypes.POINTER(c_void_p), c_void_p]),
+    "anvil_ipc_open": (c_int, [c_void_p, ctypes.POINTER(c_void_p)]),
+    "anvil_ipc_close": (c_int, [c_void_p]),
+    "anvil_ipc_free": (c_int, [c_void_p]),
     "anvil_smithy_bucket": (c_int, [c_int]),
     "anvil_smithy_set_model": (None, [c_char_p]),
     "anvil_smithy_load": (c_int, [c_char_p]),

@@ -51,6 +51,13 @@ class ChainSpec:
     def weight_bytes(self) -> int:
         return sum(g.nrows * resolve_type(g.qt).row_bytes(g.K) for g in self.gemvs)
 
+    def head(self, n: int, name: str | None = None) -> "ChainSpec":
+        """The chain's first n GEMVs (with their inputs): a smaller case of the same shapes."""
+        gemvs = self.gemvs[:n]
+        used = {g.input for g in gemvs}
+        return ChainSpec(name or f"{self.name}[:{n}]", list(gemvs),
+                         {a: k for a, k in self.inputs.items() if a in used})
+
 
 def _layered(name: str, n_layers: int, per_layer, tail=()) -> ChainSpec:
     spec = ChainSpec(name, [])
@@ -135,23 +142,34 @@ def shard_rows(nrows: int, rank: int, world: int) -> tuple[int, int]:
 
 
 class DeviceChain:
-    """Weights, activations and outputs of a ChainSpec on one GPU, plus its anvil Chain.
+    """Weights, activations and outputs of a ChainSpec on one GPU, plus its executor.
 
-    With world > 1 every matrix holds only this rank's row shard (shard_rows); outputs
-    are the local slices.  Weights are drawn on the device (quants.make_weights_device).
+    With world > 1 every matrix holds only this rank's row shard (shard_rows).  Weights
+    are drawn on the device (quants.make_weights_device).
+
+    executor="graph": the anvil Chain (a CUDA graph of quantize + MMVQ launches with
+    programmatic dependent launch); outputs are this rank's slices, (ncols, rows).
+    executor="persistent": one persistent kernel per token (pchain.PersistentChain).
+    GEMVs sharing an input form a group, and every group waits for the groups before it
+    (a decoder layer's data flow).  outputs are full (ncols, nrows) vectors; with world > 1
+    they live in CUDA-IPC memory that every rank writes its rows into (needs `dist`).
     """
 
     def __init__(self, spec: ChainSpec, ncols: int = 1, seed: int = 0, device="cuda",
                  rank: int = 0, world: int = 1, nwarps: int = 0, rows_per_block: int = 0,
-                 configs: dict | None = None, fused: bool = False, coresident: int = 1):
+                 configs: dict | None = None, fused: bool = False, coresident: int = 1,
+                 executor: str = "graph", dist=None, ctas_per_sm: int = 0):
         import torch
 
         from kernel_anvil.mmvq import Chain, q8_1_bytes
         from kernel_anvil.quants import make_weights_device
 
+        if executor not in ("graph", "persistent"):
+            raise ValueError(f"executor must be 'graph' or 'persistent', not {executor!r}")
         self.spec = spec
         self.ncols = ncols
         self.rank, self.world = rank, world
+        self.executor = executor
         g = torch.Generator(device=device)
         g.manual_seed(seed + 7919)
         # All fp32 inputs live in one buffer so a step's inputs arrive with one copy.
@@ -161,45 +179,99 @@ class DeviceChain:
         for a, k in spec.inputs.items():
             self.x[a] = self.x_all[off:off + k * ncols].view(ncols, k)
             off += k * ncols
-        self.xq = {a: torch.empty(q8_1_bytes(k, ncols), dtype=torch.uint8, device=device)
-                   for a, k in spec.inputs.items()}
-        self.weights, self.outputs, self.rows = [], [], []
-        self.chain = Chain()
-        if coresident != 1:
-            self.chain.set_coresident(coresident)
-        quantized: set[str] = set()
+        self.weights, self.outputs, self.rows, self.launch_cfg = [], [], [], []
         for i, gm in enumerate(spec.gemvs):
             r0, r1 = shard_rows(gm.nrows, rank, world)
-            n = r1 - r0
-            W = make_weights_device(gm.qt, n, gm.K, seed=seed * 100003 + i * 31 + rank, device=device)
-            y = torch.empty((ncols, n), dtype=torch.float32, device=device)
+            self.weights.append(make_weights_device(gm.qt, r1 - r0, gm.K,
+                                                    seed=seed * 100003 + i * 31 + rank, device=device))
+            self.rows.append((r0, r1))
             nw, rpb = nwarps, rows_per_block
             if configs and (gm.qt, gm.nrows, gm.K) in configs:
                 c = configs[(gm.qt, gm.nrows, gm.K)]
                 nw, rpb = c["nwarps"], c["rows_per_block"]
-            if fused:
-                # each GEMV quantises its fp32 input in its own prologue
-                self.chain.add_mmvq_f32(W, gm.qt, self.x[gm.input], self.xq[gm.input], y, nrows=n,
-                                        K=gm.K, ncols=ncols, nwarps=nw, rows_per_block=rpb)
-            else:
-                if gm.input not in quantized:
-                    self.chain.add_quantize(self.x[gm.input], self.xq[gm.input])
-                    quantized.add(gm.input)
-                self.chain.add_mmvq(W, gm.qt, self.xq[gm.input], y, nrows=n, K=gm.K, ncols=ncols,
-                                    nwarps=nw, rows_per_block=rpb)
-            self.weights.append(W)
-            self.outputs.append(y)
-            self.rows.append((r0, r1))
+            self.launch_cfg.append((nw, rpb))
+        self.chain = None
+        self.pchain = None
+        self.arena = None
+        if executor == "graph":
+            self.xq = {a: torch.empty(q8_1_bytes(k, ncols), dtype=torch.uint8, device=device)
+                       for a, k in spec.inputs.items()}
+            self.chain = Chain()
+            if coresident != 1:
+                self.chain.set_coresident(coresident)
+            quantized: set[str] = set()
+            for gm, W, (r0, r1), (nw, rpb) in zip(spec.gemvs, self.weights, self.rows, self.launch_cfg):
+                n = r1 - r0
+                y = torch.empty((ncols, n), dtype=torch.float32, device=device)
+                if fused:
+                    # each GEMV quantises its fp32 input in its own prologue
+                    self.chain.add_mmvq_f32(W, gm.qt, self.x[gm.input], self.xq[gm.input], y, nrows=n,
+                                            K=gm.K, ncols=ncols, nwarps=nw, rows_per_block=rpb)
+                else:
+                    if gm.input not in quantized:
+                        self.chain.add_quantize(self.x[gm.input], self.xq[gm.input])
+                        quantized.add(gm.input)
+                    self.chain.add_mmvq(W, gm.qt, self.xq[gm.input], y, nrows=n, K=gm.K, ncols=ncols,
+                                        nwarps=nw, rows_per_block=rpb)
+                self.outputs.append(y)
+        else:
+            self._build_persistent(device, nwarps, ctas_per_sm, dist)
+
+    def _build_persistent(self, device, nwarps: int, ctas_per_sm: int, dist) -> None:
+        import torch
+
+        from kernel_anvil.pchain import PeerArena, PersistentChain
+
+        spec, ncols = self.spec, self.ncols
+        ngroups_max = len(spec.gemvs) + 1
+        if self.world > 1:
+            if dist is None:
+                raise ValueError("a sharded persistent chain needs the process group (dist)")
+            layout = [(f"y{i}", ncols * gm.nrows * 4) for i, gm in enumerate(spec.gemvs)]
+            layout.append(("counters", ngroups_max * 4))
+            self.arena = PeerArena(layout, dist)
+            for i, gm in enumerate(spec.gemvs):
+                self.outputs.append(self.arena.local_tensor(f"y{i}", (ncols, gm.nrows)))
+        else:
+            for gm in spec.gemvs:
+                self.outputs.append(torch.empty((ncols, gm.nrows), dtype=torch.float32, device=device))
+        pc = PersistentChain(self.world, self.rank)
+        prev = None
+        for i, (gm, W, (r0, r1), (_, rpb)) in enumerate(zip(spec.gemvs, self.weights, self.rows,
+                                                             self.launch_cfg)):
+            if gm.input != prev:
+                pc.add_group(self.x[gm.input], wait=True)
+                prev = gm.input
+            ys = self.arena.ptrs(f"y{i}") if self.arena else [self.outputs[i].data_ptr()]
+            pc.add_gemv(W, gm.qt, ys, nrows=r1 - r0, row0=r0, nrows_full=gm.nrows, rows_per_block=rpb)
+        if self.arena:
+            pc.set_counters(self.arena.ptrs("counters"))
+        pc.instantiate(nwarps=nwarps, ctas_per_sm=ctas_per_sm)
+        self.pchain = pc
 
     @property
     def algorithmic_bytes(self) -> int:
-        return self.chain.algorithmic_bytes
+        return self.chain.algorithmic_bytes if self.chain else self.pchain.algorithmic_bytes
+
+    @property
+    def launches_per_step(self) -> int:
+        return self.chain.n_mmvq + self.chain.n_quantize if self.chain else 1
 
     def instantiate(self, pdl: bool = True) -> None:
-        self.chain.instantiate(pdl=pdl)
+        if self.chain:
+            self.chain.instantiate(pdl=pdl)
 
     def launch(self) -> None:
-        self.chain.launch()
+        if self.chain:
+            self.chain.launch()
+        else:
+            self.pchain.launch()
 
     def close(self) -> None:
-        self.chain.close()
+        if self.chain:
+            self.chain.close()
+        if self.pchain:
+            self.pchain.close()
+        if self.arena:
+            self.arena.close()
+            self.arena = None

@@ -147,6 +147,20 @@ def block_sums(W: torch.Tensor, qt, xq: torch.Tensor, nrows: int | None = None, 
     return out
 
 
+def host_lanes_per_row(nblk: int, rpb: int) -> int:
+    """Lanes per row the single-GEMV kernel uses for rows of nblk blocks in tiles of rpb
+    rows (the twin of host_lanes_per_row in csrc/mmvq.cuh): the power of two that keeps the
+    most lanes busy, preferring more lanes on ties."""
+    best, best_u, lb = 32, -1.0, 32
+    while lb >= 1:
+        per_lane = -(-nblk // lb)
+        u = nblk / (lb * per_lane) * min(rpb / (32 // lb), 1.0)
+        if u > best_u + 1e-6:
+            best, best_u = lb, u
+        lb //= 2
+    return best
+
+
 def plan(qt, nrows: int, K: int, ncols: int = 1, nwarps: int = 0, rows_per_block: int = 0) -> dict:
     """Launch geometry the library would use: nwarps, rows_per_block, grid, smem bytes."""
     info = resolve_type(qt)
