@@ -68,6 +68,9 @@ def parse_args():
     ap.add_argument("--executor", choices=["auto", "persistent", "graph"], default="auto",
                     help="one persistent kernel per token, or a CUDA graph of per-GEMV launches "
                          "(auto: graph on one GPU, persistent with peer stores on several)")
+    ap.add_argument("--grouped", type=int, default=1,
+                    help="graph executor: one launch per run of same-type GEMVs on one input (1) "
+                         "quantising in the kernel, or one launch per GEMV (0)")
     ap.add_argument("--nwarps", type=int, default=0, help="persistent executor: warps per CTA (0 = 8)")
     ap.add_argument("--ctas-per-sm", type=int, default=0, help="persistent executor: CTAs per SM (0 = 1)")
     return ap.parse_args()
@@ -282,7 +285,7 @@ def run_anvil(args) -> None:
     dc = DeviceChain(spec, rank=rank, world=world, device=dev, fused=args.quantize == "fused",
                      coresident=args.coresident, executor=args.executor,
                      dist=dist if world > 1 else None, nwarps=args.nwarps,
-                     ctas_per_sm=args.ctas_per_sm)
+                     ctas_per_sm=args.ctas_per_sm, grouped=bool(args.grouped) and not persistent)
     stream = torch.cuda.Stream(device=dev)
     hbm_peak, peak_kind = measured_peaks()
     total_bytes = spec.algorithmic_bytes()  # whole job: all shards together
@@ -418,6 +421,7 @@ def run_anvil(args) -> None:
                                 if persistent else
                                 "CUDA graph of quantize + MMVQ launches, programmatic dependent launch"),
                    "quantize": "in-kernel per group" if persistent else args.quantize,
+                   "grouped_launches": bool(args.grouped) and not persistent,
                    **({"persistent": pinfo} if persistent else
                       {"coresident_kernels_per_sm": args.coresident})},
         "e2e": e2e, "roofline": roofline, "gpu_launches": launches_per_step * args.steps,

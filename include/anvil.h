@@ -141,6 +141,20 @@ int anvil_mmvq_f32_noalloc(int ggml_type, const void *W, const float *x, float *
                            int ncols_x, int ncols_dst, int nwarps, int rows_per_block,
                            anvil_stream_t stream);
 
+/* Several GEMVs of one weight type that read the same activation (attention q/k/v,
+ * ffn gate/up) in one launch: segment s multiplies W[s] (nrows[s] rows of ncols_x
+ * columns) into y[s] (ncols_dst x nrows[s]), for s < nseg (1..4).  Each output equals
+ * anvil_mmvq's for that matrix alone.  Replaces a run of mul_mat_vec_q launches on one
+ * input (docs/decode-pipeline-breakdown.md:20-21; the fused gate/up of the reference's
+ * profile, docs/vulkan-vs-rocm-analysis.md:103-106).  _f32: fp32 x as anvil_mmvq_f32
+ * (quantised in the kernel when it fits, else into xq). */
+int anvil_mmvq_grouped(int ggml_type, int nseg, const void *const *W, const void *xq,
+                       float *const *y, const int *nrows, int ncols_x, int ncols_dst, int nwarps,
+                       int rows_per_block, unsigned flags, anvil_stream_t stream);
+int anvil_mmvq_grouped_f32(int ggml_type, int nseg, const void *const *W, const float *x,
+                           void *xq, float *const *y, const int *nrows, int ncols_x, int ncols_dst,
+                           int nwarps, int rows_per_block, unsigned flags, anvil_stream_t stream);
+
 /* Reads and clears the device status words of the current device: the OR of
  * anvil_device_status flags set by kernels whose bounded waits gave up (0 = none),
  * or a negative anvil_status.  Synchronous. */
@@ -181,6 +195,14 @@ int anvil_chain_add_mmvq(anvil_chain *chain, int ggml_type, const void *W, const
 int anvil_chain_add_mmvq_f32(anvil_chain *chain, int ggml_type, const void *W, const float *x,
                              void *xq, float *y, int nrows, int ncols_x, int ncols_dst,
                              int nwarps, int rows_per_block);
+/* Grouped GEMV steps: anvil_mmvq_grouped (Q8_1 input from an earlier quantize step) and
+ * anvil_mmvq_grouped_f32 semantics. */
+int anvil_chain_add_mmvq_grouped(anvil_chain *chain, int ggml_type, int nseg, const void *const *W,
+                                 const void *xq, float *const *y, const int *nrows, int ncols_x,
+                                 int ncols_dst, int nwarps, int rows_per_block);
+int anvil_chain_add_mmvq_grouped_f32(anvil_chain *chain, int ggml_type, int nseg, const void *const *W,
+                                     const float *x, void *xq, float *const *y, const int *nrows,
+                                     int ncols_x, int ncols_dst, int nwarps, int rows_per_block);
 /* Sizes every GEMV grid so that `kernels_per_sm` consecutive GEMVs (1..4) fit on each SM
  * together: with programmatic dependent launch the next GEMV's CTAs are then resident
  * while the current one runs and stream their first weight tiles early.  Default 1 (each

@@ -269,10 +269,37 @@ static int plan_mmvq(int t, int nrows, int K, int ncols, int nwarps, int rpb, in
     return ANVIL_OK;
 }
 
-static int launch_mmvq(const Plan &p, const void *W, const void *x, float *y, int32_t *sums,
-                       int nrows, int K, unsigned flags, cudaStream_t stream, int share = 1) {
+// Segments of one launch: GEMVs of the plan's type that read the same activation.
+struct Segs {
+    int n;
+    const void *W[kMaxSeg];
+    float *y[kMaxSeg];
+    int rows[kMaxSeg];
+};
+
+static int launch_mmvq_segs(const Plan &p, const Segs &sg, const void *x, int32_t *sums, int K,
+                            unsigned flags, cudaStream_t stream, int share = 1) {
+    MmvqArgs a;
+    a.x = x;
+    a.sums = sums;
+    a.K = K;
+    a.nstages = p.nstages;
+    a.nseg = sg.n;
+    long tiles = 0;
+    for (int i = 0; i < kMaxSeg; ++i) {
+        const bool live = i < sg.n;
+        a.segW[i] = live ? static_cast<const uint8_t *>(sg.W[i]) : nullptr;
+        a.segY[i] = live ? sg.y[i] : nullptr;
+        a.segRows[i] = live ? sg.rows[i] : 0;
+        a.segTile[i] = int(tiles);
+        if (live) tiles += (sg.rows[i] + p.rpb - 1) / p.rpb;
+    }
+    a.segTile[kMaxSeg] = int(tiles);
+    if (sg.n < kMaxSeg) a.segTile[sg.n] = int(tiles);
+    Plan q = p;
+    q.ctas_needed = (tiles + p.nwarps - 1) / p.nwarps;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(share > 1 ? grid_for(p, share) : p.grid);
+    cfg.gridDim = dim3(grid_for(q, share));
     cfg.blockDim = dim3(p.nwarps * 32);
     cfg.dynamicSmemBytes = p.smem;
     cfg.stream = stream;
@@ -283,17 +310,19 @@ static int launch_mmvq(const Plan &p, const void *W, const void *x, float *y, in
         cfg.attrs = attr;
         cfg.numAttrs = 1;
     }
-    MmvqArgs a;
-    a.W = static_cast<const uint8_t *>(W);
-    a.x = x;
-    a.y = y;
-    a.sums = sums;
-    a.nrows = nrows;
-    a.K = K;
-    a.nstages = p.nstages;
     cudaError_t e = cudaLaunchKernelEx(&cfg, p.fn, a);
     if (e != cudaSuccess) return cuda_fail(e, "mmvq launch");
     return ANVIL_OK;
+}
+
+static int launch_mmvq(const Plan &p, const void *W, const void *x, float *y, int32_t *sums,
+                       int nrows, int K, unsigned flags, cudaStream_t stream, int share = 1) {
+    Segs sg{};
+    sg.n = 1;
+    sg.W[0] = W;
+    sg.y[0] = y;
+    sg.rows[0] = nrows;
+    return launch_mmvq_segs(p, sg, x, sums, K, flags, stream, share);
 }
 
 static int check_mmvq_ptrs(int t, const void *W, const void *xq, const void *out) {
@@ -353,6 +382,7 @@ struct ChainStep {
     float *y;
     int nrows, ncols_x, ncols_dst, nwarps, rpb;
     Plan plan;
+    Segs segs;  // the GEMVs of an mmvq step (one, or several sharing the activation)
 };
 
 struct anvil_chain {
@@ -465,6 +495,58 @@ int anvil_mmvq_f32(int ggml_type, const void *W, const float *x, void *xq, float
                              rows_per_block, 0, stream);
 }
 
+// Checks and packs the segments of a grouped GEMV; *total = their rows together.
+static int make_segs(int t, int nseg, const void *const *W, float *const *y, const int *nrows,
+                     Segs *sg, int *total) {
+    if (nseg < 1 || nseg > kMaxSeg) return fail(ANVIL_ERR_INVALID, "nseg=%d outside 1..%d", nseg, kMaxSeg);
+    if (!W || !y || !nrows) return fail(ANVIL_ERR_INVALID, "null pointer argument");
+    sg->n = nseg;
+    long sum = 0;
+    for (int i = 0; i < nseg; ++i) {
+        if (int s = check_mmvq_ptrs(t, W[i], W[i], y[i])) return s;
+        if (nrows[i] <= 0) return fail(ANVIL_ERR_INVALID, "nrows[%d]=%d", i, nrows[i]);
+        sg->W[i] = W[i];
+        sg->y[i] = y[i];
+        sg->rows[i] = nrows[i];
+        sum += nrows[i];
+    }
+    if (sum > (1L << 30)) return fail(ANVIL_ERR_INVALID, "too many rows");
+    *total = int(sum);
+    return ANVIL_OK;
+}
+
+int anvil_mmvq_grouped(int ggml_type, int nseg, const void *const *W, const void *xq,
+                       float *const *y, const int *nrows, int ncols_x, int ncols_dst, int nwarps,
+                       int rows_per_block, unsigned flags, anvil_stream_t stream) {
+    Segs sg;
+    int total;
+    if (int s = make_segs(ggml_type, nseg, W, y, nrows, &sg, &total)) return s;
+    if (!xq) return fail(ANVIL_ERR_INVALID, "null pointer argument");
+    if (reinterpret_cast<uintptr_t>(xq) & 3) return fail(ANVIL_ERR_ALIGN, "xq must be 4-byte aligned");
+    Plan p;
+    if (int s = plan_mmvq(ggml_type, total, ncols_x, ncols_dst, nwarps, rows_per_block, kModeQ81, &p))
+        return s;
+    return launch_mmvq_segs(p, sg, xq, nullptr, ncols_x, flags, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int anvil_mmvq_grouped_f32(int ggml_type, int nseg, const void *const *W, const float *x,
+                           void *xq, float *const *y, const int *nrows, int ncols_x, int ncols_dst,
+                           int nwarps, int rows_per_block, unsigned flags, anvil_stream_t stream) {
+    Segs sg;
+    int total;
+    if (int s = make_segs(ggml_type, nseg, W, y, nrows, &sg, &total)) return s;
+    if (!x || !xq) return fail(ANVIL_ERR_INVALID, "null pointer argument");
+    if (reinterpret_cast<uintptr_t>(xq) & 3) return fail(ANVIL_ERR_ALIGN, "xq must be 4-byte aligned");
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    Plan p;
+    if (plan_fused(ggml_type, x, total, ncols_x, ncols_dst, nwarps, rows_per_block, &p))
+        return launch_mmvq_segs(p, sg, x, nullptr, ncols_x, flags, st);
+    if (int s = plan_mmvq(ggml_type, total, ncols_x, ncols_dst, nwarps, rows_per_block, kModeQ81, &p))
+        return s;
+    if (int s = launch_quantize(x, xq, ncols_x, ncols_dst, flags, st)) return s;
+    return launch_mmvq_segs(p, sg, xq, nullptr, ncols_x, ANVIL_FLAG_PDL, st);
+}
+
 int anvil_mmvq_block_sums(int ggml_type, const void *W, const void *xq, int32_t *sums,
                           int nrows, int ncols_x, int ncols_dst, int nwarps, int rows_per_block,
                           anvil_stream_t stream) {
@@ -543,6 +625,10 @@ int anvil_chain_add_mmvq(anvil_chain *c, int ggml_type, const void *W, const voi
     s.ncols_dst = ncols_dst;
     s.nwarps = nwarps;
     s.rpb = rows_per_block;
+    s.segs.n = 1;
+    s.segs.W[0] = W;
+    s.segs.y[0] = y;
+    s.segs.rows[0] = nrows;
     if (int st = plan_mmvq(ggml_type, nrows, ncols_x, ncols_dst, nwarps, rows_per_block, kModeQ81,
                            &s.plan))
         return st;
@@ -572,8 +658,71 @@ int anvil_chain_add_mmvq_f32(anvil_chain *c, int ggml_type, const void *W, const
     s.ncols_dst = ncols_dst;
     s.nwarps = nwarps;
     s.rpb = rows_per_block;
+    s.segs.n = 1;
+    s.segs.W[0] = W;
+    s.segs.y[0] = y;
+    s.segs.rows[0] = nrows;
     if (!plan_fused(ggml_type, x, nrows, ncols_x, ncols_dst, nwarps, rows_per_block, &s.plan)) {
         if (int st = plan_mmvq(ggml_type, nrows, ncols_x, ncols_dst, nwarps, rows_per_block,
+                               kModeQ81, &s.plan))
+            return st;
+    }
+    c->steps.push_back(s);
+    return ANVIL_OK;
+}
+
+int anvil_chain_add_mmvq_grouped(anvil_chain *c, int ggml_type, int nseg, const void *const *W,
+                                 const void *xq, float *const *y, const int *nrows, int ncols_x,
+                                 int ncols_dst, int nwarps, int rows_per_block) {
+    if (!c) return fail(ANVIL_ERR_INVALID, "null chain");
+    if (c->exec) return fail(ANVIL_ERR_INVALID, "chain already instantiated");
+    ChainStep s = {};
+    int total;
+    if (int st = make_segs(ggml_type, nseg, W, y, nrows, &s.segs, &total)) return st;
+    if (!xq) return fail(ANVIL_ERR_INVALID, "null pointer argument");
+    if (reinterpret_cast<uintptr_t>(xq) & 3) return fail(ANVIL_ERR_ALIGN, "xq must be 4-byte aligned");
+    s.type = ggml_type;
+    s.W = W[0];
+    s.xqin = xq;
+    s.y = y[0];
+    s.nrows = total;
+    s.ncols_x = ncols_x;
+    s.ncols_dst = ncols_dst;
+    s.nwarps = nwarps;
+    s.rpb = rows_per_block;
+    if (int st = plan_mmvq(ggml_type, total, ncols_x, ncols_dst, nwarps, rows_per_block, kModeQ81,
+                           &s.plan))
+        return st;
+    c->steps.push_back(s);
+    return ANVIL_OK;
+}
+
+int anvil_chain_add_mmvq_grouped_f32(anvil_chain *c, int ggml_type, int nseg, const void *const *W,
+                                     const float *x, void *xq, float *const *y, const int *nrows,
+                                     int ncols_x, int ncols_dst, int nwarps, int rows_per_block) {
+    if (!c) return fail(ANVIL_ERR_INVALID, "null chain");
+    if (c->exec) return fail(ANVIL_ERR_INVALID, "chain already instantiated");
+    ChainStep s = {};
+    int total;
+    if (int st = make_segs(ggml_type, nseg, W, y, nrows, &s.segs, &total)) return st;
+    if (!x || !xq) return fail(ANVIL_ERR_INVALID, "null pointer argument");
+    if (reinterpret_cast<uintptr_t>(xq) & 3) return fail(ANVIL_ERR_ALIGN, "xq must be 4-byte aligned");
+    s.fused = true;
+    s.type = ggml_type;
+    s.W = W[0];
+    s.x = x;
+    s.xq = xq;
+    s.xqin = xq;
+    s.y = y[0];
+    s.nrows = total;
+    s.ncols_x = ncols_x;
+    s.K = ncols_x;
+    s.ncols = ncols_dst;
+    s.ncols_dst = ncols_dst;
+    s.nwarps = nwarps;
+    s.rpb = rows_per_block;
+    if (!plan_fused(ggml_type, x, total, ncols_x, ncols_dst, nwarps, rows_per_block, &s.plan)) {
+        if (int st = plan_mmvq(ggml_type, total, ncols_x, ncols_dst, nwarps, rows_per_block,
                                kModeQ81, &s.plan))
             return st;
     }
@@ -589,14 +738,13 @@ static int run_steps(anvil_chain *c, bool use_pdl, cudaStream_t st) {
         if (s.quantize) {
             r = launch_quantize(s.x, s.xq, s.K, s.ncols, flags, st);
         } else if (s.fused && s.plan.mode == kModeF32) {
-            r = launch_mmvq(s.plan, s.W, s.x, s.y, nullptr, s.nrows, s.ncols_x, flags, st, c->share);
+            r = launch_mmvq_segs(s.plan, s.segs, s.x, nullptr, s.ncols_x, flags, st, c->share);
         } else if (s.fused) {
             r = launch_quantize(s.x, s.xq, s.K, s.ncols, flags, st);
-            if (!r) r = launch_mmvq(s.plan, s.W, s.xq, s.y, nullptr, s.nrows, s.ncols_x,
-                                    use_pdl ? ANVIL_FLAG_PDL : 0u, st, c->share);
+            if (!r) r = launch_mmvq_segs(s.plan, s.segs, s.xq, nullptr, s.ncols_x,
+                                         use_pdl ? ANVIL_FLAG_PDL : 0u, st, c->share);
         } else {
-            r = launch_mmvq(s.plan, s.W, s.xqin, s.y, nullptr, s.nrows, s.ncols_x, flags, st,
-                            c->share);
+            r = launch_mmvq_segs(s.plan, s.segs, s.xqin, nullptr, s.ncols_x, flags, st, c->share);
         }
         if (r) return r;
     }

@@ -142,94 +142,6 @@ __device__ void pc_arrive(const PcArgs &a, int g) {
     }
 }
 
-// roundf(x / d) with x / d the correctly rounded IEEE quotient, |x| <= 127 d, without
-// a division in the common case.  t = x * rd with rd = 1/d rounded differs from the exact
-// x / d by at most |x/d| (2^-24 + 2^-24 + 2^-48) < 127.5 * 2^-23 ~ 1.6e-5, and the rounded
-// quotient differs from the exact one by at most 0.5 ulp < 127.5 * 2^-24 ~ 7.6e-6.  Both
-// therefore round to the same integer unless t lies within 2.4e-5 of a half-integer; there
-// (and 1e-4 is the margin used) the quotient is taken with the division itself.
-__device__ __forceinline__ int quant_q8(float x, float d, float rd) {
-    const float t = x * rd;
-    const float f = fabsf(t) - floorf(fabsf(t));  // fractional part of |t|
-    if (fabsf(f - 0.5f) > 1e-4f) return int(roundf(t));
-    return int(roundf(__fdiv_rn(x, d)));
-}
-
-// ---- activation staging: fused Q8_1 quantisation into the swizzled layout ---------------
-
-// One 16-value chunk per thread and pass (two chunks in flight per thread); the two
-// chunks of a Q8_1 block sit on adjacent lanes, which combine amax and the half sums.
-// Passes a warp has no chunk in are skipped whole (the shuffles stay warp-uniform).
-template <int NCOLS, int FAM>
-__device__ __forceinline__ void pc_stage(const float *__restrict__ x, int K, uint8_t *aq,
-                                         float *ad, float *ads, int2 *as) {
-    constexpr int QTS = FAM == 0 ? kTypeQ4_K : kTypeQ8_0;  // swizzle family
-    const int T = blockDim.x, tid = threadIdx.x;
-    const int wbase = tid & ~31;
-    const int nkb = K >> 5, nch = 2 * nkb, acb = act_col_bytes(nkb);
-    const int total = NCOLS * nch;
-    for (int base = 0; base < total; base += 2 * T) {
-        float4 v[2][4];
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-            const int c = base + j * T + tid;
-            if (c < total) {
-                const int col = c / nch, cc = c - col * nch;
-                const float4 *src = reinterpret_cast<const float4 *>(x + size_t(col) * K + cc * 16);
-#pragma unroll
-                for (int k = 0; k < 4; ++k) v[j][k] = __ldg(src + k);
-            } else {
-#pragma unroll
-                for (int k = 0; k < 4; ++k) v[j][k] = make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-        }
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-            if (base + j * T + wbase >= total) continue;  // whole warp past the end
-            const int c = base + j * T + tid;
-            float am = 0.f;
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                am = fmaxf(am, fabsf(v[j][k].x));
-                am = fmaxf(am, fabsf(v[j][k].y));
-                am = fmaxf(am, fabsf(v[j][k].z));
-                am = fmaxf(am, fabsf(v[j][k].w));
-            }
-            am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
-            const float d = __fdiv_rn(am, 127.0f);
-            const float dn = am == 0.0f ? 1.0f : d;  // all quants are 0 then; no 0/0
-            const float rd = __frcp_rn(dn);
-            uint32_t w[4];
-            int s = 0;
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const float e[4] = {v[j][k].x, v[j][k].y, v[j][k].z, v[j][k].w};
-                uint32_t word = 0;
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const int q = am == 0.0f ? 0 : quant_q8(e[i], dn, rd);
-                    word |= (uint32_t(q) & 0xFFu) << (8 * i);
-                }
-                w[k] = word;
-                s = __dp4a(int(word), 0x01010101, s);
-            }
-            const int so = __shfl_xor_sync(0xffffffffu, s, 1);
-            if (c < total) {
-                const int col = c / nch, cc = c - col * nch;
-                *reinterpret_cast<uint4 *>(aq + col * acb + act_chunk<QTS>(cc) * 16) =
-                    make_uint4(w[0], w[1], w[2], w[3]);
-                if ((cc & 1) == 0) {
-                    const int i = col * nkb + (cc >> 1);
-                    const float dh = __half2float(__float2half_rn(d));
-                    ad[i] = dh;
-                    as[i] = make_int2(s, so);
-                    ads[i] = dh * float(s + so);
-                }
-            }
-        }
-    }
-}
-
 // ---- tile arithmetic -------------------------------------------------------------------
 
 // Dots of one staged tile (rows r0 .. r0 + rows - 1 of GEMV `gm`, a device descriptor) and
@@ -501,10 +413,10 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) pchain_kernel(const __grid_
         float *ads = ad + NCOLS * nkb;
         int2 *as = reinterpret_cast<int2 *>(
             (reinterpret_cast<uintptr_t>(ads + NCOLS * nkb) + 15) & ~uintptr_t(15));
-        if (cur.family == 0)
-            pc_stage<NCOLS, 0>(cur.x, K, aq, ad, ads, as);
-        else
-            pc_stage<NCOLS, 1>(cur.x, K, aq, ad, ads, as);
+        if (cur.family == 0)  // K-quant swizzle
+            stage_f32_q8_1<kTypeQ4_K, NCOLS>(cur.x, K, aq, ad, ads, as);
+        else                  // Q8_0 swizzle
+            stage_f32_q8_1<kTypeQ8_0, NCOLS>(cur.x, K, aq, ad, ads, as);
         __syncthreads();
 
         // ---- 3. this warp's tiles of the group -------------------------------------------

@@ -46,13 +46,41 @@ constexpr int kModeQ81 = 0;
 constexpr int kModeF32 = 1;
 constexpr int kModeSums = 2;
 
+constexpr int kMaxSeg = 4;  // matrices of one launch (GEMVs sharing the activation)
+
 struct MmvqArgs {
-    const uint8_t *W;   // weights, raw GGUF blocks, row-major
     const void *x;      // Q8_1 blocks (kModeQ81 / kModeSums) or fp32 values (kModeF32)
-    float *y;           // ncols x nrows outputs
-    int32_t *sums;      // kModeSums output
-    int nrows, K, nstages;
+    int32_t *sums;      // kModeSums output (one segment)
+    int K, nstages;
+    // Segments: GEMVs of one weight type reading x, dealt as one tile sequence.
+    // Segment s: weights segW[s] (raw GGUF blocks, row-major), segRows[s] rows, outputs
+    // segY[s] (ncols x segRows[s]); its tiles are [segTile[s], segTile[s + 1]).
+    int nseg;
+    const uint8_t *segW[kMaxSeg];
+    float *segY[kMaxSeg];
+    int segRows[kMaxSeg];
+    int segTile[kMaxSeg + 1];
 };
+
+// Segment holding tile `tile` (segments are few: a linear scan).
+__device__ __forceinline__ int mmvq_segment(const MmvqArgs &a, int tile) {
+    int s = 0;
+    while (s + 1 < a.nseg && tile >= a.segTile[s + 1]) ++s;
+    return s;
+}
+
+// roundf(x / d) with x / d the correctly rounded IEEE quotient, |x| <= 127 d (d > 0), without
+// a division in the common case.  t = x * rd with rd = 1/d rounded differs from the exact
+// x / d by at most |x/d| (2^-24 + 2^-24 + 2^-48) < 127.5 * 2^-23 ~ 1.6e-5, and the rounded
+// quotient differs from the exact one by at most 0.5 ulp < 127.5 * 2^-24 ~ 7.6e-6.  Both
+// therefore round to the same integer unless t lies within 2.4e-5 of a half-integer; there
+// (1e-4 is the margin used) the quotient is taken with the division itself.
+__device__ __forceinline__ int quant_q8(float x, float d, float rd) {
+    const float t = x * rd;
+    const float f = fabsf(t) - floorf(fabsf(t));  // fractional part of |t|
+    if (fabsf(f - 0.5f) > 1e-4f) return int(roundf(t));
+    return int(roundf(__fdiv_rn(x, d)));
+}
 
 struct MmvqSmem {
     int bar, w, stage, xbuf, aq, ad, ads, as, total;
@@ -79,7 +107,7 @@ __host__ __device__ inline MmvqSmem mmvq_smem_layout(int qt, int K, int ncols, i
     // +32 per stage: up to 15 bytes of head misalignment plus one word of funnel over-read.
     L.stage = ((rpb * row_bytes + 32) + 15) & ~15;
     L.xbuf = L.w + nwarps * nstages * L.stage;
-    L.aq = L.xbuf + (mode == kModeF32 ? ncols * K * 4 : 0);
+    L.aq = L.xbuf;  // the fused mode quantises straight from registers (no fp32 copy)
     L.ad = L.aq + ncols * act_col_bytes(nkb);
     L.ads = L.ad + ncols * nkb * 4;
     L.as = (L.ads + ncols * nkb * 4 + 15) & ~15;
@@ -455,6 +483,83 @@ __device__ __forceinline__ uint32_t pack_quants(int q) {
     return b | (b1 << 8) | (b2 << 16) | (b3 << 24);
 }
 
+// ---- fused Q8_1 staging from fp32 ------------------------------------------------------
+
+// Quantises fp32 x (NCOLS columns of K) to Q8_1 straight into the swizzled shared layout,
+// with d8, d8 * sum(q) and the half sums, by the arithmetic of quantize_q8_1 (d = amax/127
+// by IEEE division, q = roundf(x / d) through quant_q8).  One 16-value chunk per thread
+// and pass, two chunks in flight per thread; the two chunks of a Q8_1 block sit on
+// adjacent lanes, which combine amax and the half sums.  Passes a warp has no chunk in
+// are skipped whole (the shuffles stay warp-uniform).  x is 16-byte aligned.
+template <int QT, int NCOLS>
+__device__ __forceinline__ void stage_f32_q8_1(const float *__restrict__ x, int K, uint8_t *aq,
+                                               float *ad, float *ads, int2 *as) {
+    const int T = blockDim.x, tid = threadIdx.x;
+    const int wbase = tid & ~31;
+    const int nkb = K >> 5, nch = 2 * nkb, acb = act_col_bytes(nkb);
+    const int total = NCOLS * nch;
+    for (int base = 0; base < total; base += 2 * T) {
+        float4 v[2][4];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const int c = base + j * T + tid;
+            if (c < total) {
+                const int col = c / nch, cc = c - col * nch;
+                const float4 *src = reinterpret_cast<const float4 *>(x + size_t(col) * K + cc * 16);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) v[j][k] = __ldg(src + k);
+            } else {
+#pragma unroll
+                for (int k = 0; k < 4; ++k) v[j][k] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            if (base + j * T + wbase >= total) continue;  // whole warp past the end
+            const int c = base + j * T + tid;
+            float am = 0.f;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                am = fmaxf(am, fabsf(v[j][k].x));
+                am = fmaxf(am, fabsf(v[j][k].y));
+                am = fmaxf(am, fabsf(v[j][k].z));
+                am = fmaxf(am, fabsf(v[j][k].w));
+            }
+            am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+            const float d = __fdiv_rn(am, 127.0f);
+            const float dn = am == 0.0f ? 1.0f : d;  // all quants are 0 then; no 0/0
+            const float rd = __frcp_rn(dn);
+            uint32_t w[4];
+            int s = 0;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float e[4] = {v[j][k].x, v[j][k].y, v[j][k].z, v[j][k].w};
+                uint32_t word = 0;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int q = am == 0.0f ? 0 : quant_q8(e[i], dn, rd);
+                    word |= (uint32_t(q) & 0xFFu) << (8 * i);
+                }
+                w[k] = word;
+                s = __dp4a(int(word), 0x01010101, s);
+            }
+            const int so = __shfl_xor_sync(0xffffffffu, s, 1);
+            if (c < total) {
+                const int col = c / nch, cc = c - col * nch;
+                *reinterpret_cast<uint4 *>(aq + col * acb + act_chunk<QT>(cc) * 16) =
+                    make_uint4(w[0], w[1], w[2], w[3]);
+                if ((cc & 1) == 0) {
+                    const int i = col * nkb + (cc >> 1);
+                    const float dh = __half2float(__float2half_rn(d));
+                    ad[i] = dh;
+                    as[i] = make_int2(s, so);
+                    ads[i] = dh * float(s + so);
+                }
+            }
+        }
+    }
+}
+
 // ---- the kernel --------------------------------------------------------------------------
 
 // Host-side twin of choose_lanes_per_row (same arithmetic).
@@ -476,14 +581,15 @@ inline int host_lanes_per_row(int nblk, int rpb) {
 
 // LBT: lanes per row fixed at compile time (16 or 32), or 0 for the runtime choice.
 template <int QT, int NCOLS, int RPB, int MODE, int LBT>
-__global__ void __launch_bounds__(kMaxWarps * 32, NCOLS == 1 ? 2 : 1) mmvq_kernel(const MmvqArgs args) {
+__global__ void __launch_bounds__(kMaxWarps * 32, NCOLS == 1 ? 2 : 1)
+    mmvq_kernel(const __grid_constant__ MmvqArgs args) {
     using TR = QTraits<QT>;
     extern __shared__ __align__(16) uint8_t smem[];
     const int T = blockDim.x;
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
     const int nwarps = T >> 5;
-    const int K = args.K, nrows = args.nrows, nstages = args.nstages;
+    const int K = args.K, nstages = args.nstages;
     const int nkb = K >> 5;
     const int acb = act_col_bytes(nkb);
     const int nblk = K / TR::qk;
@@ -493,10 +599,9 @@ __global__ void __launch_bounds__(kMaxWarps * 32, NCOLS == 1 ? 2 : 1) mmvq_kerne
     float *ad = reinterpret_cast<float *>(smem + L.ad);
     float *ads = reinterpret_cast<float *>(smem + L.ads);
     int2 *as = reinterpret_cast<int2 *>(smem + L.as);
-    const uint8_t *W = args.W;
 
-    // Warp-tiles of RPB rows are dealt round-robin over all warps of the grid.
-    const int ntiles = (nrows + RPB - 1) / RPB;
+    // Warp-tiles of RPB rows (of one segment) are dealt round-robin over all warps.
+    const int ntiles = args.segTile[args.nseg];
     const int gwarp = blockIdx.x * nwarps + warp;
     const int wstride = gridDim.x * nwarps;
     const int my_tiles = gwarp < ntiles ? (ntiles - 1 - gwarp) / wstride + 1 : 0;
@@ -507,8 +612,10 @@ __global__ void __launch_bounds__(kMaxWarps * 32, NCOLS == 1 ? 2 : 1) mmvq_kerne
     // interior of the row range goes through the copy engine; a range that does not start
     // or end on 16 bytes leaves at most 15 + 15 bytes for plain loads (below).
     auto issue = [&](int tile, int st) {
-        const uint8_t *src = W + size_t(tile) * RPB * size_t(row_bytes);
-        const int rows = min(RPB, nrows - tile * RPB);
+        const int sg = mmvq_segment(args, tile);
+        const int lt = tile - args.segTile[sg];
+        const uint8_t *src = args.segW[sg] + size_t(lt) * RPB * size_t(row_bytes);
+        const int rows = min(RPB, args.segRows[sg] - lt * RPB);
         const uintptr_t s = reinterpret_cast<uintptr_t>(src);
         const uintptr_t e = s + size_t(rows) * row_bytes;
         const uintptr_t s_al = (s + 15) & ~uintptr_t(15), e_al = e & ~uintptr_t(15);
@@ -535,63 +642,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, NCOLS == 1 ? 2 : 1) mmvq_kerne
 
     // ---- 2. stage the activation once per CTA ------------------------------------------
     if constexpr (MODE == kModeF32) {
-        // fp32 x is staged with batched plain loads (a bulk copy here would queue behind
-        // the weight tiles already issued), then each warp quantises whole Q8_1 blocks.
-        float *xs = reinterpret_cast<float *>(smem + L.xbuf);
-        const float4 *xg = reinterpret_cast<const float4 *>(args.x);
-        const int n4 = NCOLS * K / 4;
-        for (int base = 0; base < n4; base += 4 * T) {
-            float4 v[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int i = base + j * T + tid;
-                v[j] = i < n4 ? __ldg(xg + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int i = base + j * T + tid;
-                if (i < n4) reinterpret_cast<float4 *>(xs)[i] = v[j];
-            }
-        }
-        __syncthreads();
-        const float *xb = xs;
-        // Four blocks per warp per pass: their reduction chains interleave (ILP) while each
-        // block keeps the exact butterfly order of the standalone quantiser.
-        const int nb = NCOLS * nkb;
-        for (int b0 = warp * 4; b0 < nb; b0 += nwarps * 4) {
-            float xv[4], am[4], sm[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                xv[j] = b0 + j < nb ? xb[(b0 + j) * 32 + lane] : 0.f;
-                am[j] = fabsf(xv[j]);
-                sm[j] = xv[j];
-            }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    am[j] = fmaxf(am[j], __shfl_xor_sync(0xffffffffu, am[j], o));
-                    sm[j] += __shfl_xor_sync(0xffffffffu, sm[j], o);
-                }
-            }
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const float d = __fdiv_rn(am[j], 127.0f);
-                const int q = am[j] == 0.0f ? 0 : int(roundf(__fdiv_rn(xv[j], d)));
-                const uint32_t word = pack_quants(q);
-                const int blk = b0 + j;
-                if (blk < nb) {
-                    const int c = blk / nkb, kb = blk - c * nkb;
-                    if ((lane & 3) == 0) {
-                        const int w = lane >> 2;  // word 0..7 of the block
-                        *reinterpret_cast<uint32_t *>(aq + c * acb +
-                                                      act_chunk<QT>(2 * kb + (w >> 2)) * 16 +
-                                                      (w & 3) * 4) = word;
-                    }
-                    if (lane == 0) ad[blk] = __half2float(__float2half_rn(d));
-                }
-            }
-        }
+        stage_f32_q8_1<QT, NCOLS>(static_cast<const float *>(args.x), K, aq, ad, ads, as);
     } else {
         // Q8_1 blocks, one per thread: 9 words ({d, s}, then 8 quant words) loaded together,
         // written to the swizzled layout with the block's d8, d8 * sum(q) and half sums.
@@ -620,26 +671,6 @@ __global__ void __launch_bounds__(kMaxWarps * 32, NCOLS == 1 ? 2 : 1) mmvq_kerne
             }
         }
     }
-    if constexpr (MODE == kModeF32) {
-        __syncthreads();  // quants of the fused path are complete; derive the block sums
-        for (int i = tid; i < NCOLS * nkb; i += T) {
-            const int c = i / nkb, kb = i - c * nkb;
-            const uint8_t *base = aq + c * acb;
-            const uint4 q0 = *reinterpret_cast<const uint4 *>(base + act_chunk<QT>(2 * kb) * 16);
-            const uint4 q1 = *reinterpret_cast<const uint4 *>(base + act_chunk<QT>(2 * kb + 1) * 16);
-            int lo = 0, hi = 0;
-            lo = __dp4a(int(q0.x), 0x01010101, lo);
-            lo = __dp4a(int(q0.y), 0x01010101, lo);
-            lo = __dp4a(int(q0.z), 0x01010101, lo);
-            lo = __dp4a(int(q0.w), 0x01010101, lo);
-            hi = __dp4a(int(q1.x), 0x01010101, hi);
-            hi = __dp4a(int(q1.y), 0x01010101, hi);
-            hi = __dp4a(int(q1.z), 0x01010101, hi);
-            hi = __dp4a(int(q1.w), 0x01010101, hi);
-            as[i] = make_int2(lo, hi);
-            ads[i] = ad[i] * float(lo + hi);
-        }
-    }
     __syncthreads();
 
     // ---- 3. lane -> (row group, blocks) mapping, fixed for all tiles -------------------
@@ -658,9 +689,11 @@ __global__ void __launch_bounds__(kMaxWarps * 32, NCOLS == 1 ? 2 : 1) mmvq_kerne
     uint32_t phase = 0;
     for (int k = 0; k < my_tiles; ++k) {
         const int tile = gwarp + k * wstride;
-        const int r0 = tile * RPB;
+        const int sg = mmvq_segment(args, tile);
+        const int nrows = args.segRows[sg];
+        const int r0 = (tile - args.segTile[sg]) * RPB;
         const int rows = min(RPB, nrows - r0);
-        const uint8_t *src = W + size_t(r0) * size_t(row_bytes);
+        const uint8_t *src = args.segW[sg] + size_t(r0) * size_t(row_bytes);
         const uintptr_t s = reinterpret_cast<uintptr_t>(src);
         const uintptr_t e = s + size_t(rows) * row_bytes;
         uint8_t *wrow0 = ring + st * L.stage + int(s & 15);
@@ -750,7 +783,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, NCOLS == 1 ? 2 : 1) mmvq_kerne
                             for (int o = LB >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
                         }
                         if (bl == 0 && grp_live && sl < nslots && i < rows)
-                            args.y[size_t(c) * nrows + r0 + i] = v;
+                            args.segY[sg][size_t(c) * nrows + r0 + i] = v;
                     }
                 }
             }

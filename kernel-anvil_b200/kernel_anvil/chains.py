@@ -148,7 +148,10 @@ class DeviceChain:
     are drawn on the device (quants.make_weights_device).
 
     executor="graph": the anvil Chain (a CUDA graph of quantize + MMVQ launches with
-    programmatic dependent launch); outputs are this rank's slices, (ncols, rows).
+    programmatic dependent launch); outputs are this rank's slices, (ncols, rows).  With
+    grouped=True, consecutive GEMVs of one quant type on the same input (q/k, gate/up) are
+    one launch (anvil_mmvq_grouped; with fused=True the launch quantises the fp32 input
+    itself, anvil_mmvq_grouped_f32).
     executor="persistent": one persistent kernel per token (pchain.PersistentChain).
     GEMVs sharing an input form a group, and every group waits for the groups before it
     (a decoder layer's data flow).  outputs are full (ncols, nrows) vectors; with world > 1
@@ -158,7 +161,7 @@ class DeviceChain:
     def __init__(self, spec: ChainSpec, ncols: int = 1, seed: int = 0, device="cuda",
                  rank: int = 0, world: int = 1, nwarps: int = 0, rows_per_block: int = 0,
                  configs: dict | None = None, fused: bool = False, coresident: int = 1,
-                 executor: str = "graph", dist=None, ctas_per_sm: int = 0):
+                 executor: str = "graph", dist=None, ctas_per_sm: int = 0, grouped: bool = False):
         import torch
 
         from kernel_anvil.mmvq import Chain, q8_1_bytes
@@ -200,7 +203,34 @@ class DeviceChain:
             if coresident != 1:
                 self.chain.set_coresident(coresident)
             quantized: set[str] = set()
+            if grouped:
+                self.outputs = [torch.empty((ncols, r1 - r0), dtype=torch.float32, device=device)
+                                for r0, r1 in self.rows]
+                i = 0
+                while i < len(spec.gemvs):
+                    j = i + 1
+                    while (j < len(spec.gemvs) and j - i < 4 and spec.gemvs[j].input == spec.gemvs[i].input
+                           and spec.gemvs[j].qt == spec.gemvs[i].qt):
+                        j += 1
+                    gm = spec.gemvs[i]
+                    nw, rpb = self.launch_cfg[i]
+                    rows = [r1 - r0 for r0, r1 in self.rows[i:j]]
+                    if fused:
+                        self.chain.add_mmvq_grouped_f32(
+                            self.weights[i:j], gm.qt, self.x[gm.input], self.xq[gm.input],
+                            self.outputs[i:j], rows, K=gm.K, ncols=ncols, nwarps=nw,
+                            rows_per_block=rpb)
+                    else:
+                        if gm.input not in quantized:
+                            self.chain.add_quantize(self.x[gm.input], self.xq[gm.input])
+                            quantized.add(gm.input)
+                        self.chain.add_mmvq_grouped(self.weights[i:j], gm.qt, self.xq[gm.input],
+                                                    self.outputs[i:j], rows, K=gm.K, ncols=ncols,
+                                                    nwarps=nw, rows_per_block=rpb)
+                    i = j
             for gm, W, (r0, r1), (nw, rpb) in zip(spec.gemvs, self.weights, self.rows, self.launch_cfg):
+                if grouped:
+                    break
                 n = r1 - r0
                 y = torch.empty((ncols, n), dtype=torch.float32, device=device)
                 if fused:
@@ -255,7 +285,7 @@ class DeviceChain:
 
     @property
     def launches_per_step(self) -> int:
-        return self.chain.n_mmvq + self.chain.n_quantize if self.chain else 1
+        return self.chain.n_launches if self.chain else 1
 
     def instantiate(self, pdl: bool = True) -> None:
         if self.chain:

@@ -21,6 +21,7 @@ from kernel_anvil._native import ANVIL_FLAG_PDL, AnvilError, check
 from kernel_anvil.quants import Q8_1_BLOCK_SIZE, QuantTypeInfo, resolve_type
 
 MAX_COLS = 8
+MAX_SEGMENTS = 4  # matrices of one grouped launch
 
 
 def _stream_ptr() -> int:
@@ -127,6 +128,42 @@ def mmvq_f32(W: torch.Tensor, qt, x: torch.Tensor, nwarps: int = 0, rows_per_blo
     return out
 
 
+def _seg_arrays(Ws, ys, nrows):
+    n = len(Ws)
+    if not 1 <= n <= MAX_SEGMENTS or len(ys) != n or len(nrows) != n:
+        raise AnvilError(_native.ANVIL_ERR_INVALID, f"1..{MAX_SEGMENTS} matrices with one output each")
+    return ((ctypes.c_void_p * n)(*[w.data_ptr() for w in Ws]),
+            (ctypes.c_void_p * n)(*[y.data_ptr() for y in ys]),
+            (ctypes.c_int * n)(*nrows))
+
+
+def mmvq_grouped_f32(Ws: list, qt, x: torch.Tensor, nwarps: int = 0, rows_per_block: int = 0,
+                     xq_scratch: torch.Tensor | None = None, outs: list | None = None,
+                     pdl: bool = False) -> list:
+    """[W @ dequant(Q8_1(x)) for W in Ws] in one launch: matrices of one quant type reading the
+    same fp32 x (ncols, K).  Each output equals mmvq_f32(W, qt, x) alone."""
+    info = resolve_type(qt)
+    _require_cuda("x", x, torch.float32)
+    x2 = x.reshape(1, -1) if x.dim() == 1 else x
+    ncols, K = x2.shape
+    rows = []
+    for W in Ws:
+        _require_cuda("W", W, torch.uint8)
+        rows.append(_shape_args(W, info, None, K)[0])
+    if xq_scratch is None:
+        xq_scratch = torch.empty(q8_1_bytes(K, ncols), dtype=torch.uint8, device=x.device)
+    if outs is None:
+        outs = [torch.empty((ncols, n), dtype=torch.float32, device=x.device) for n in rows]
+    for y in outs:
+        _require_cuda("out", y, torch.float32)
+    Wa, ya, ra = _seg_arrays(Ws, outs, rows)
+    check(_native.lib().anvil_mmvq_grouped_f32(info.ggml_type, len(Ws), Wa, x2.data_ptr(),
+                                               xq_scratch.data_ptr(), ya, ra, K, ncols, nwarps,
+                                               rows_per_block, ANVIL_FLAG_PDL if pdl else 0,
+                                               _stream_ptr()))
+    return outs
+
+
 def block_sums(W: torch.Tensor, qt, xq: torch.Tensor, nrows: int | None = None, K: int | None = None,
                ncols: int | None = None, nwarps: int = 0, rows_per_block: int = 0) -> torch.Tensor:
     """The production kernel's exact int32 block dots, shape (ncols, nrows, nsub).
@@ -195,6 +232,7 @@ class Chain:
         self.algorithmic_bytes = 0
         self.n_mmvq = 0
         self.n_quantize = 0
+        self.n_launches = 0
 
     def add_quantize(self, x: torch.Tensor, xq: torch.Tensor) -> None:
         _require_cuda("x", x, torch.float32)
@@ -206,6 +244,7 @@ class Chain:
         check(self._lib.anvil_chain_add_quantize(self._h, x2.data_ptr(), xq.data_ptr(), K, ncols))
         self._keep += [x, xq]
         self.n_quantize += 1
+        self.n_launches += 1
 
     def add_mmvq(self, W: torch.Tensor, qt, xq: torch.Tensor, y: torch.Tensor, nrows: int | None = None,
                  K: int | None = None, ncols: int = 1, nwarps: int = 0, rows_per_block: int = 0) -> None:
@@ -220,6 +259,7 @@ class Chain:
                                              y.data_ptr(), nrows, K, ncols, nwarps, rows_per_block))
         self._keep += [W, xq, y]
         self.n_mmvq += 1
+        self.n_launches += 1
         self.weight_bytes += nrows * info.row_bytes(K)
         from kernel_anvil.quants import gemv_bytes
         self.algorithmic_bytes += gemv_bytes(info, nrows, K, ncols)
@@ -241,9 +281,58 @@ class Chain:
                                                  nwarps, rows_per_block))
         self._keep += [W, x, xq_scratch, y]
         self.n_mmvq += 1
+        self.n_launches += 1
         self.weight_bytes += nrows * info.row_bytes(K)
         from kernel_anvil.quants import gemv_bytes
         self.algorithmic_bytes += gemv_bytes(info, nrows, K, ncols)
+
+    def add_mmvq_grouped(self, Ws: list, qt, xq: torch.Tensor, ys: list, nrows: list, K: int,
+                         ncols: int = 1, nwarps: int = 0, rows_per_block: int = 0) -> None:
+        """One launch for several GEMVs of type qt reading the Q8_1 activation xq."""
+        info = resolve_type(qt)
+        _require_cuda("xq", xq, torch.uint8)
+        if xq.numel() < q8_1_bytes(K, ncols):
+            raise AnvilError(_native.ANVIL_ERR_INVALID, "xq is too small")
+        for W, y, n in zip(Ws, ys, nrows):
+            _require_cuda("W", W, torch.uint8)
+            _require_cuda("y", y, torch.float32)
+            if W.numel() < n * info.row_bytes(K) or y.numel() < ncols * n:
+                raise AnvilError(_native.ANVIL_ERR_INVALID, "W or y is too small")
+        Wa, ya, ra = _seg_arrays(Ws, ys, nrows)
+        check(self._lib.anvil_chain_add_mmvq_grouped(self._h, info.ggml_type, len(Ws), Wa,
+                                                     xq.data_ptr(), ya, ra, K, ncols, nwarps,
+                                                     rows_per_block))
+        self._keep += [*Ws, xq, *ys]
+        from kernel_anvil.quants import gemv_bytes
+        for n in nrows:
+            self.n_mmvq += 1
+            self.weight_bytes += n * info.row_bytes(K)
+            self.algorithmic_bytes += gemv_bytes(info, n, K, ncols)
+        self.n_launches += 1
+
+    def add_mmvq_grouped_f32(self, Ws: list, qt, x: torch.Tensor, xq_scratch: torch.Tensor, ys: list,
+                             nrows: list, K: int, ncols: int = 1, nwarps: int = 0,
+                             rows_per_block: int = 0) -> None:
+        """One launch for several GEMVs of type qt reading fp32 x (see mmvq_grouped_f32)."""
+        info = resolve_type(qt)
+        _require_cuda("x", x, torch.float32)
+        _require_cuda("xq_scratch", xq_scratch, torch.uint8)
+        for W, y, n in zip(Ws, ys, nrows):
+            _require_cuda("W", W, torch.uint8)
+            _require_cuda("y", y, torch.float32)
+            if W.numel() < n * info.row_bytes(K) or y.numel() < ncols * n:
+                raise AnvilError(_native.ANVIL_ERR_INVALID, "W or y is too small")
+        Wa, ya, ra = _seg_arrays(Ws, ys, nrows)
+        check(self._lib.anvil_chain_add_mmvq_grouped_f32(self._h, info.ggml_type, len(Ws), Wa,
+                                                         x.data_ptr(), xq_scratch.data_ptr(), ya, ra,
+                                                         K, ncols, nwarps, rows_per_block))
+        self._keep += [*Ws, x, xq_scratch, *ys]
+        from kernel_anvil.quants import gemv_bytes
+        for n in nrows:
+            self.n_mmvq += 1
+            self.weight_bytes += n * info.row_bytes(K)
+            self.algorithmic_bytes += gemv_bytes(info, n, K, ncols)
+        self.n_launches += 1
 
     def set_coresident(self, kernels_per_sm: int) -> None:
         """Size GEMV grids so that this many consecutive GEMVs fit on each SM together."""

@@ -203,3 +203,55 @@ def test_argument_errors():
 def test_no_device_wait_gave_up():
     torch.cuda.synchronize()
     assert ops.take_device_status() == 0
+
+
+# ---- grouped launches: several GEMVs on one input -------------------------------------
+
+@pytest.mark.parametrize("qt,rows,K", [("Q4_K", (4096, 1024, 1024), 4096), ("Q6_K", (700, 129), 2048),
+                                       ("Q8_0", (2048, 1024, 1024, 3), 1024), ("Q5_K", (512,), 4096)])
+@pytest.mark.parametrize("ncols", [1, 3])
+def test_grouped_matches_single(qt, rows, K, ncols):
+    Ws = [dev(make_weights(qt, n, K, seed=40 + i)) for i, n in enumerate(rows)]
+    x = dev(make_activation(K, ncols=ncols, seed=41))
+    ys = ops.mmvq_grouped_f32(Ws, qt, x, nwarps=4, rows_per_block=4)
+    for W, n, y in zip(Ws, rows, ys):
+        ref = ops.mmvq_f32(W, qt, x, nwarps=4, rows_per_block=4)
+        torch.cuda.synchronize()
+        assert torch.equal(y, ref)  # same launch shape: the same arithmetic in the same order
+    # the built-in launch shape, against the oracle
+    ys = ops.mmvq_grouped_f32(Ws, qt, x)
+    xq = oracle.quantize_q8_1(x.cpu().numpy())
+    for W, n, y in zip(Ws, rows, ys):
+        y_ref = oracle.mmvq(qt, W.cpu().numpy(), xq, n, K, ncols)
+        assert oracle.max_rel_err(y.cpu().numpy(), y_ref) <= Y_TOL
+
+
+def test_grouped_chain_equals_per_gemv_chain():
+    from kernel_anvil.chains import DeviceChain, get_chain
+
+    spec = get_chain("qwen3_8b").head(14)
+    a = DeviceChain(spec, executor="graph")
+    b = DeviceChain(spec, executor="graph", grouped=True)
+    c = DeviceChain(spec, executor="graph", grouped=True, fused=True)
+    assert c.launches_per_step < b.launches_per_step < a.launches_per_step
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        for dc in (a, b, c):
+            dc.instantiate()
+            dc.launch()
+    torch.cuda.synchronize()
+    assert ops.take_device_status() == 0
+    for ya, yb, yc in zip(a.outputs, b.outputs, c.outputs):
+        torch.testing.assert_close(yb, ya, rtol=1e-5, atol=1e-5 * float(ya.abs().max()))
+        torch.testing.assert_close(yc, ya, rtol=1e-5, atol=1e-5 * float(ya.abs().max()))
+    for dc in (a, b, c):
+        dc.close()
+
+
+def test_grouped_argument_errors():
+    W = dev(make_weights("Q4_K", 8, 1024))
+    x = dev(make_activation(1024))
+    with pytest.raises(AnvilError, match="1..4"):
+        ops.mmvq_grouped_f32([W] * 5, "Q4_K", x)
+    with pytest.raises(AnvilError, match="1..4"):
+        ops.mmvq_grouped_f32([], "Q4_K", x)
