@@ -25,10 +25,12 @@ One JSON line is printed by rank 0:
                measured here with CUDA events, against measured HBM copy bandwidth
   cpu_baseline the CPU oracle (oracle/, all host threads) on a bounded sample of the same
                workload (layer 0 of the chain), rank 0 at N=1 only
-With N > 1 (torchrun) each rank holds a row shard of every matrix (strong scaling).  The
-persistent executor writes each output row into every rank's output buffer over NVLink
-(CUDA IPC peer stores) inside the kernel; the graph executor all-gathers each GEMV's
-output with NCCL inside the CUDA graph.
+With N > 1 (torchrun), --multi replicas (default) runs one full chain per GPU on its own
+inputs: independent token streams, no collective in the data path, weak scaling (the
+8B-class workloads fit one GPU).  --multi rows shards every matrix by rows across the GPUs
+(strong scaling): the persistent executor writes each output row into every rank's output
+buffer over NVLink (CUDA IPC peer stores) inside the kernel; the graph executor
+all-gathers each GEMV's output with NCCL inside the CUDA graph.
 --impl reference times the CPU oracle port on the same workload (rank 0 only).
 """
 from __future__ import annotations
@@ -58,6 +60,8 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--workload", default="qwen3_8b")
+    ap.add_argument("--gemvs", type=int, default=0,
+                    help="only the workload's first N GEMVs (a smaller case of the same shapes)")
     ap.add_argument("--impl", default="anvil", choices=["anvil", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -71,6 +75,10 @@ def parse_args():
     ap.add_argument("--grouped", type=int, default=1,
                     help="graph executor: one launch per run of same-type GEMVs on one input (1) "
                          "quantising in the kernel, or one launch per GEMV (0)")
+    ap.add_argument("--multi", choices=["replicas", "rows"], default="replicas",
+                    help="N > 1: one full chain per GPU (independent token streams, no collective; "
+                         "weak scaling) or every matrix row-sharded across the GPUs with the outputs "
+                         "exchanged (strong scaling)")
     ap.add_argument("--nwarps", type=int, default=0, help="persistent executor: warps per CTA (0 = 8)")
     ap.add_argument("--ctas-per-sm", type=int, default=0, help="persistent executor: CTAs per SM (0 = 1)")
     return ap.parse_args()
@@ -224,7 +232,8 @@ def time_graph(launch, stream, steps: int) -> float:
 
 
 def dominant_kernel(dc, stream, steps: int, warmup: int) -> dict:
-    """Q4_K MMVQ launches of one chain step, replayed as their own PDL graph."""
+    """The Q4_K MMVQ launches of one chain step, launched as in the chain (one launch per
+    run of Q4_K GEMVs on one input when grouped) and replayed as their own PDL graph."""
     import torch
 
     from kernel_anvil.mmvq import Chain
@@ -232,12 +241,23 @@ def dominant_kernel(dc, stream, steps: int, warmup: int) -> dict:
 
     ch = Chain()
     nbytes, n = 0, 0
-    for gm, W, y, (r0, r1) in zip(dc.spec.gemvs, dc.weights, dc.outputs, dc.rows):
-        if gm.qt != "Q4_K":
-            continue
-        ch.add_mmvq(W, gm.qt, dc.xq[gm.input], y, nrows=r1 - r0, K=gm.K, ncols=dc.ncols)
-        nbytes += gemv_bytes(gm.qt, r1 - r0, gm.K, dc.ncols)
-        n += 1
+    gemvs = list(zip(dc.spec.gemvs, dc.weights, dc.outputs, dc.rows))
+    i = 0
+    while i < len(gemvs):
+        gm = gemvs[i][0]
+        j = i + 1
+        if dc.grouped:
+            while (j < len(gemvs) and j - i < 4 and gemvs[j][0].input == gm.input
+                   and gemvs[j][0].qt == gm.qt):
+                j += 1
+        if gm.qt == "Q4_K":
+            run = gemvs[i:j]
+            rows = [r1 - r0 for _, _, _, (r0, r1) in run]
+            ch.add_mmvq_grouped([w for _, w, _, _ in run], gm.qt, dc.xq[gm.input],
+                                [y for _, _, y, _ in run], rows, K=gm.K, ncols=dc.ncols)
+            nbytes += sum(gemv_bytes(gm.qt, r, gm.K, dc.ncols) for r in rows)
+            n += 1
+        i = j
     with torch.cuda.stream(stream):
         ch.instantiate(pdl=True)
         for _ in range(warmup):
@@ -279,22 +299,27 @@ def run_anvil(args) -> None:
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
 
     spec = get_chain(args.workload)
+    if args.gemvs:
+        spec = spec.head(args.gemvs)
+    shard = world > 1 and args.multi == "rows"
     if args.executor == "auto":
-        args.executor = "graph" if world == 1 else "persistent"
+        args.executor = "persistent" if shard else "graph"
     persistent = args.executor == "persistent"
-    dc = DeviceChain(spec, rank=rank, world=world, device=dev, fused=args.quantize == "fused",
+    # replicas: every rank runs the whole chain on its own inputs (seeded per rank)
+    dc = DeviceChain(spec, rank=rank if shard else 0, world=world if shard else 1, device=dev,
+                     seed=0 if shard else rank, fused=args.quantize == "fused",
                      coresident=args.coresident, executor=args.executor,
-                     dist=dist if world > 1 else None, nwarps=args.nwarps,
+                     dist=dist if shard else None, nwarps=args.nwarps,
                      ctas_per_sm=args.ctas_per_sm, grouped=bool(args.grouped) and not persistent)
     stream = torch.cuda.Stream(device=dev)
     hbm_peak, peak_kind = measured_peaks()
-    total_bytes = spec.algorithmic_bytes()  # whole job: all shards together
+    total_bytes = spec.algorithmic_bytes() * (1 if shard or world == 1 else world)  # whole job
     rank_bytes = dc.algorithmic_bytes       # this rank's shard
 
     graph = None
     launches_per_step = dc.launches_per_step
     n_quantize = dc.chain.n_quantize if dc.chain else 0
-    if world == 1 or persistent:
+    if not shard or persistent:
         with torch.cuda.stream(stream):
             dc.instantiate(pdl=True)
         launch = dc.launch
@@ -376,9 +401,10 @@ def run_anvil(args) -> None:
         dk = dominant_kernel(dc, stream, args.steps, args.warmup)
         achieved = dk["bytes_per_launch"] / (dk["ms_per_launch"] * 1e-3) / 1e9
         roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
-                    "frac": round(achieved / hbm_peak, 4), "traffic": traffic_per_launch("mmvq_kernel"),
+                    "frac": round(achieved / hbm_peak, 4),
+                    "traffic": traffic_per_launch(f"mmvq_kernel {args.workload}"),
                     "peak_source": peak_source,
-                    "kernel": "mmvq_kernel<Q4_K, ncols=1> (all Q4_K GEMVs of one step, PDL graph)",
+                    "kernel": "mmvq_kernel<Q4_K, ncols=1> (all Q4_K launches of one step, PDL graph)",
                     "launches_per_step": dk["launches_per_step"],
                     "bytes_per_launch": round(dk["bytes_per_launch"]),
                     "us_per_launch": round(dk["ms_per_launch"] * 1e3, 3)}
@@ -404,7 +430,8 @@ def run_anvil(args) -> None:
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "higher_is_better": True, "scaling": "strong" if shard or world == 1 else "weak",
+        "vs_baseline": None,
         "dtype": "int8 dp4a / fp32", "data": "synthetic",
         "config": {"workload": f"{args.workload} per-token GEMV chain",
                    "gemvs_per_step": len(spec.gemvs),
@@ -413,9 +440,11 @@ def run_anvil(args) -> None:
                    "us_per_token": round(ms * 1e3, 1), "pct_of_hbm_peak": round(100 * value / hbm_peak, 1),
                    "pct_of_8TBps": round(100 * value / 8000.0, 1),
                    "l2": "inputs larger than L2 (weights stream from HBM every step)",
-                   "parallelism": (f"row-shard x{world}, " + ("outputs written to every rank over NVLink "
-                                   "(CUDA IPC peer stores) inside the kernel" if persistent else
-                                   "NCCL all-gather per GEMV")) if world > 1 else "single GPU",
+                   "parallelism": ((f"row-shard x{world}, " + ("outputs written to every rank over NVLink "
+                                    "(CUDA IPC peer stores) inside the kernel" if persistent else
+                                    "NCCL all-gather per GEMV")) if shard else
+                                   f"{world} replicas: one full chain per GPU on its own inputs, no "
+                                   "collective in the data path" if world > 1 else "single GPU"),
                    "executor": ("one persistent cooperative kernel per token: groups of GEMVs sharing an "
                                 "input, Q8_1 quantisation in-kernel, grid barrier between dependent groups"
                                 if persistent else

@@ -173,6 +173,7 @@ class DeviceChain:
         self.ncols = ncols
         self.rank, self.world = rank, world
         self.executor = executor
+        self.grouped = grouped and executor == "graph"
         g = torch.Generator(device=device)
         g.manual_seed(seed + 7919)
         # All fp32 inputs live in one buffer so a step's inputs arrive with one copy.
