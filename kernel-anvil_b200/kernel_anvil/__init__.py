@@ -8,3 +8,11 @@ include/anvil.h).  Importing the package does not load the library.
 __version__ = "0.2.0"
 
 from kernel_anvil.codegen import generate_config_header, generate_runtime_config  # noqa: F401,E402
+
+
+def optimize(model, quant="Q8_0", verbose: bool = True, **launch):
+    """Replace a model's nn.Linear layers with QuantLinear (see kernel_anvil.model.optimize);
+    the reference's top-level kernel_anvil.optimize(model)."""
+    from kernel_anvil.model import optimize as _optimize
+
+    return _optimize(model, quant=quant, verbose=verbose, **launch)
