@@ -114,10 +114,9 @@ int anvil_mmvq_ex(int ggml_type, const void *W, const void *xq, float *y, int nr
                   anvil_stream_t stream);
 
 /* GEMV from fp32 activations: y = W . dequant(Q8_1(x)), bit-identical to calling
- * anvil_quantize_q8_1 then anvil_mmvq.  When x is 16-byte aligned and its K * ncols
- * fp32 values fit in shared memory next to the weight ring, one kernel quantises x in
- * its prologue (every CTA, in shared memory) and xq is not touched; otherwise the two
- * launches run and xq receives the Q8_1 blocks.  xq is scratch of
+ * anvil_quantize_q8_1 then anvil_mmvq.  When x is 16-byte aligned and the launch fits,
+ * one kernel quantises x in its prologue (every CTA, from registers into shared memory)
+ * and xq is not touched; otherwise the two launches run and xq receives the Q8_1 blocks.  xq is scratch of
  * ncols * (K/32) * 36 bytes whose contents are unspecified afterwards.
  * anvil_mmvq_f32_ex takes anvil_flags (ANVIL_FLAG_PDL). */
 int anvil_mmvq_f32(int ggml_type, const void *W, const float *x, void *xq, float *y, int nrows,
@@ -230,8 +229,9 @@ int anvil_chain_num_steps(const anvil_chain *chain);
  * Ranks: world > 1 row-shards every matrix.  Rank r passes its rows [row0, row0 + nrows)
  * of an nrows_full-row matrix, and y[q] = rank q's full output buffer (ncols x
  * nrows_full, reachable from this GPU: a peer mapping from anvil_ipc_open); each output
- * row is written to all ranks' buffers.  counters[q] = rank q's array of at least
- * (number of groups) zeroed uint32 words, the same layout on every rank; every rank must
+ * row ends up in all ranks' buffers (this rank's copy first, the peers' at the end of the
+ * group).  counters[q] = rank q's array of at least 2 x (number of groups) zeroed uint32
+ * words, the same layout on every rank; every rank must
  * build the same groups with the same nwarps / ctas_per_sm.  With world = 1, y[0] is the
  * output and counters are allocated by the chain unless set.
  *

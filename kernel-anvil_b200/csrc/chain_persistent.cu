@@ -21,10 +21,12 @@
 //   * Dots.  The tile arithmetic is the MMVQ kernel's (unit_step, load_hdr; lane-per-block
 //     decode with compile-time lanes per row), so for the same rows per tile and lanes per
 //     row the outputs are bit-identical to anvil_mmvq's.
-//   * Ranks.  With world > 1 each rank holds a row shard of every matrix and writes each
-//     output row into the full output buffer of every rank (peer pointers over NVLink);
-//     barriers then count the CTAs of all ranks (system-scope fences).  The exchange is
-//     the all-gather of the row-sharded GEMV, fused into its epilogue.
+//   * Ranks.  With world > 1 each rank holds a row shard of every matrix and writes its
+//     output rows into its own copy of the full output; at the end of a group the rank's
+//     last CTA copies the rank's rows into every peer's copy (peer pointers over NVLink),
+//     then counts the rank on every rank's group counter (one system-scope release per
+//     rank and group).  The exchange is the all-gather of the row-sharded GEMV, inside the
+//     kernel.
 //
 // Co-residency of all CTAs (required by the barriers) comes from the cooperative launch.
 // Every wait is bounded; a wait that gives up raises a device status flag and the kernel
@@ -107,7 +109,8 @@ __device__ __forceinline__ bool pc_failed() {
 // Relaxed polling; the fence after the last read orders what follows (acquire).
 __device__ void pc_wait_counters(const PcArgs &a, int from, int to, uint32_t target) {
     const bool sys = a.world > 1;
-    const uint32_t *base = a.counters[a.rank];
+    // one CTA count per group on one GPU; one rank count per group across GPUs
+    const uint32_t *base = a.counters[a.rank] + (sys ? a.ngroups : 0);
     uint64_t t0 = 0;
     for (int g = from; g < to; ++g) {
         for (uint32_t it = 0;; ++it) {
@@ -130,15 +133,65 @@ __device__ void pc_wait_counters(const PcArgs &a, int from, int to, uint32_t tar
         asm volatile("fence.acq_rel.gpu;" ::: "memory");
 }
 
-// Thread 0 of a CTA, after the CTA's barrier: publish the CTA's outputs of group g and
-// count its arrival on every rank (release: fence, then the increments).
-__device__ void pc_arrive(const PcArgs &a, int g) {
-    if (a.world > 1) {
-        asm volatile("fence.acq_rel.sys;" ::: "memory");
-        for (int q = 0; q < a.world; ++q) red_relaxed_add(a.counters[q] + g, 1u, true);
-    } else {
+__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t *p, uint32_t v) {
+    uint32_t old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
+// Copies this rank's output rows of the group's GEMVs from its own buffer into every peer's
+// (16-byte stores where both sides allow them).  Whole CTA.
+template <int NCOLS>
+__device__ void pc_push_outputs(const PcArgs &a, const PcGroup &grp) {
+    const int T = blockDim.x, tid = threadIdx.x;
+    for (int m = grp.first; m < grp.first + grp.count; ++m) {
+        const PcGemv *gm = a.gemvs + m;
+        const int n = gm->nrows, r0 = gm->row0, nf = gm->nrows_full;
+        for (int c = 0; c < NCOLS; ++c) {
+            const float *src = gm->y[a.rank] + size_t(c) * nf + r0;
+            for (int q = 0; q < a.world; ++q) {
+                if (q == a.rank) continue;
+                float *dst = gm->y[q] + size_t(c) * nf + r0;
+                if (((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0 &&
+                    (n & 3) == 0) {
+                    const float4 *s4 = reinterpret_cast<const float4 *>(src);
+                    float4 *d4 = reinterpret_cast<float4 *>(dst);
+                    for (int i = tid; i < (n >> 2); i += T) d4[i] = s4[i];
+                } else {
+                    for (int i = tid; i < n; i += T) dst[i] = src[i];
+                }
+            }
+        }
+    }
+}
+
+// The CTA's arrival at the end of group g (whole CTA, after its barrier).  One GPU: thread 0
+// publishes the CTA's outputs (release fence) and counts the CTA.  Several GPUs: the CTAs
+// count themselves on this GPU; the last one (it sees every CTA's outputs through the
+// acquire-release count) copies the rank's output rows to every peer, then one system-scope
+// release and one count per rank on every rank's group counter.
+template <int NCOLS>
+__device__ void pc_arrive(const PcArgs &a, const PcGroup &grp, int g, int *s_last) {
+    if (a.world == 1) {
+        if (threadIdx.x == 0) {
+            asm volatile("fence.acq_rel.gpu;" ::: "memory");
+            red_relaxed_add(a.counters[0] + g, 1u, false);
+        }
+        return;
+    }
+    if (threadIdx.x == 0) {
         asm volatile("fence.acq_rel.gpu;" ::: "memory");
-        red_relaxed_add(a.counters[0] + g, 1u, false);
+        const uint32_t old = atom_add_acq_rel_gpu(a.counters[a.rank] + g, 1u);
+        *s_last = old + 1u == (a.epoch + 1u) * gridDim.x;
+    }
+    __syncthreads();
+    if (*s_last) {
+        pc_push_outputs<NCOLS>(a, grp);
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            asm volatile("fence.acq_rel.sys;" ::: "memory");
+            for (int q = 0; q < a.world; ++q) red_relaxed_add(a.counters[q] + a.ngroups + g, 1u, true);
+        }
     }
 }
 
@@ -151,7 +204,7 @@ __device__ void pc_arrive(const PcArgs &a, int g) {
 template <int QT, int NCOLS, int RPB, int LBT>
 __device__ __noinline__ void pc_tile(const PcGemv *__restrict__ gm, const uint8_t *wrow0, int r0,
                                      int rows, const uint8_t *aq, const float *ad,
-                                     const float *ads, const int2 *as, int K, int world) {
+                                     const float *ads, const int2 *as, int K, int rank) {
     using TR = QTraits<QT>;
     constexpr int RG = 32 / LBT;
     constexpr int NS = RPB >= RG ? RPB / RG : 1;
@@ -192,19 +245,19 @@ __device__ __noinline__ void pc_tile(const PcGemv *__restrict__ gm, const uint8_
             for (int o = LBT >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
             if (bl == 0 && grp < RPB && i < rows) {
                 const size_t off = size_t(c) * nfull + row0 + r0 + i;
-                for (int q = 0; q < world; ++q) gm->y[q][off] = v;
+                gm->y[rank][off] = v;  // this rank's buffer; peers get the slice at group end
             }
         }
     }
 }
 
 
-#define ANVIL_PC_TILE_ARGS gm, wrow0, r0, rows, aq, ad, ads, as, K, world
+#define ANVIL_PC_TILE_ARGS gm, wrow0, r0, rows, aq, ad, ads, as, K, rank
 
 template <int QT, int NCOLS>
 __device__ __forceinline__ void pc_tile_variant(int variant, const PcGemv *gm, const uint8_t *wrow0,
                                                 int r0, int rows, const uint8_t *aq, const float *ad,
-                                                const float *ads, const int2 *as, int K, int world) {
+                                                const float *ads, const int2 *as, int K, int rank) {
     switch (variant) {
     case kV1x32: pc_tile<QT, NCOLS, 1, 32>(ANVIL_PC_TILE_ARGS); break;
     case kV2x32: pc_tile<QT, NCOLS, 2, 32>(ANVIL_PC_TILE_ARGS); break;
@@ -223,7 +276,7 @@ template <int NCOLS>
 __device__ __forceinline__ void pc_tile_any(int type, int variant, const PcGemv *gm,
                                             const uint8_t *wrow0, int r0, int rows,
                                             const uint8_t *aq, const float *ad, const float *ads,
-                                            const int2 *as, int K, int world) {
+                                            const int2 *as, int K, int rank) {
     switch (type) {
     case kTypeQ4_K: pc_tile_variant<kTypeQ4_K, NCOLS>(variant, ANVIL_PC_TILE_ARGS); break;
     case kTypeQ5_K: pc_tile_variant<kTypeQ5_K, NCOLS>(variant, ANVIL_PC_TILE_ARGS); break;
@@ -360,7 +413,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) pchain_kernel(const __grid_
     uint8_t *act_base = smem + a.act_off;
     // Set once a bounded wait of this CTA (or, at the launch start, of any kernel of this
     // library) has given up: later weight waits then use a 1 ms bound.
-    __shared__ int s_failed;
+    __shared__ int s_failed, s_last;
     if (tid == 0) s_failed = 0;
 
     PcWarp w;
@@ -396,7 +449,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) pchain_kernel(const __grid_
         const int K = cur.K;
         // ---- 1. dependencies -------------------------------------------------------------
         if (tid == 0) {
-            const uint32_t per_epoch = gridDim.x * uint32_t(a.world);
+            const uint32_t per_epoch = a.world > 1 ? uint32_t(a.world) : gridDim.x;
             if (g == 0) {
                 if (pc_failed()) s_failed = 1;
                 if (a.world > 1 && a.epoch > 0)
@@ -464,7 +517,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) pchain_kernel(const __grid_
             }
             if (have_w)
                 pc_tile_any<NCOLS>(cc.type, cc.variant, a.gemvs + cc.m, wrow0, r0, rows, aq, ad, ads,
-                                   as, K, a.world);
+                                   as, K, a.rank);
             __syncwarp();  // every lane is done with the tile's ring bytes
             r.c_total += (wrap ? w.R - r.c_pos : 0u) + alloc;
             r.c_pos = pos + alloc;
@@ -473,7 +526,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) pchain_kernel(const __grid_
         }
         // ---- 4. arrive -------------------------------------------------------------------
         __syncthreads();  // all warps done with this group's activation and outputs
-        if (tid == 0) pc_arrive(a, g);
+        pc_arrive<NCOLS>(a, cur, g, &s_last);
     }
 }
 
@@ -760,9 +813,9 @@ int anvil_pchain_instantiate(anvil_pchain *c, int nwarps, int ctas_per_sm) {
     if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy(gemvs)");
     for (size_t m = 0; m < dg.size(); ++m) c->gemvs[m].d = dg[m];
     if (c->world == 1 && !c->counters[0]) {
-        e = cudaMalloc(&c->own_counters, sizeof(uint32_t) * c->groups.size());
+        e = cudaMalloc(&c->own_counters, 2 * sizeof(uint32_t) * c->groups.size());
         if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(counters)");
-        e = cudaMemset(c->own_counters, 0, sizeof(uint32_t) * c->groups.size());
+        e = cudaMemset(c->own_counters, 0, 2 * sizeof(uint32_t) * c->groups.size());
         if (e != cudaSuccess) return cuda_fail(e, "cudaMemset(counters)");
         c->counters[0] = c->own_counters;
     }

@@ -259,7 +259,7 @@ class DeviceChain:
             if dist is None:
                 raise ValueError("a sharded persistent chain needs the process group (dist)")
             layout = [(f"y{i}", ncols * gm.nrows * 4) for i, gm in enumerate(spec.gemvs)]
-            layout.append(("counters", ngroups_max * 4))
+            layout.append(("counters", 2 * ngroups_max * 4))  # CTA counts, then rank counts
             self.arena = PeerArena(layout, dist)
             for i, gm in enumerate(spec.gemvs):
                 self.outputs.append(self.arena.local_tensor(f"y{i}", (ncols, gm.nrows)))
