@@ -25,7 +25,8 @@
  *     column c of a K-long input starts at element c * K (fp32) or at byte
  *     c * (K / 32) * 36 (Q8_1).  Output column c starts at element c * nrows.
  *   - ggml type ids follow ggml.h (kernel_anvil/codegen.py:22-31):
- *     Q8_0 = 8, Q4_K = 12, Q5_K = 13, Q6_K = 14.
+ *     Q4_0 = 2, Q4_1 = 3, Q5_0 = 6, Q5_1 = 7, Q8_0 = 8, Q4_K = 12, Q5_K = 13, Q6_K = 14
+ *     (the persistent chain takes Q8_0 and the K-quants).
  *   - Thread-safe: the smithy table is guarded by a reader/writer lock; the launch
  *     entry points keep no mutable shared state besides one-time function attributes.
  */
@@ -54,6 +55,10 @@ enum anvil_status {
 };
 
 enum anvil_ggml_type {
+    ANVIL_TYPE_Q4_0 = 2,
+    ANVIL_TYPE_Q4_1 = 3,
+    ANVIL_TYPE_Q5_0 = 6,
+    ANVIL_TYPE_Q5_1 = 7,
     ANVIL_TYPE_Q8_0 = 8,
     ANVIL_TYPE_Q8_1 = 9,
     ANVIL_TYPE_Q4_K = 12,

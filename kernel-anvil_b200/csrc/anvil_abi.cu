@@ -152,7 +152,8 @@ static int prepare_fn(const void *fn, int dev, int threads, int smem, int *occ) 
 // Geometry and launch planning
 // ---------------------------------------------------------------------------------
 static bool supported_type(int t) {
-    return t == kTypeQ4_K || t == kTypeQ5_K || t == kTypeQ6_K || t == kTypeQ8_0;
+    return t == kTypeQ4_K || t == kTypeQ5_K || t == kTypeQ6_K || t == kTypeQ8_0 || t == kTypeQ4_0 ||
+           t == kTypeQ4_1 || t == kTypeQ5_0 || t == kTypeQ5_1;
 }
 
 static MmvqKernelFn kernel_for(int t, int ncols, int rpb, int lbt, int mode) {
@@ -161,6 +162,10 @@ static MmvqKernelFn kernel_for(int t, int ncols, int rpb, int lbt, int mode) {
     case kTypeQ5_K: return mmvq_kernel_q5k(ncols, rpb, lbt, mode);
     case kTypeQ6_K: return mmvq_kernel_q6k(ncols, rpb, lbt, mode);
     case kTypeQ8_0: return mmvq_kernel_q80(ncols, rpb, lbt, mode);
+    case kTypeQ4_0: return mmvq_kernel_q40(ncols, rpb, lbt, mode);
+    case kTypeQ4_1: return mmvq_kernel_q41(ncols, rpb, lbt, mode);
+    case kTypeQ5_0: return mmvq_kernel_q50(ncols, rpb, lbt, mode);
+    case kTypeQ5_1: return mmvq_kernel_q51(ncols, rpb, lbt, mode);
     default: return nullptr;
     }
 }
@@ -401,6 +406,10 @@ const char *anvil_last_error(void) { return t_last_error.c_str(); }
 int anvil_type_geometry(int ggml_type, int *qk, int *block_bytes) {
     int q = 0, b = 0;
     switch (ggml_type) {
+    case ANVIL_TYPE_Q4_0: q = 32; b = 18; break;
+    case ANVIL_TYPE_Q4_1: q = 32; b = 20; break;
+    case ANVIL_TYPE_Q5_0: q = 32; b = 22; break;
+    case ANVIL_TYPE_Q5_1: q = 32; b = 24; break;
     case ANVIL_TYPE_Q8_0: q = 32; b = 34; break;
     case ANVIL_TYPE_Q8_1: q = 32; b = 36; break;
     case ANVIL_TYPE_Q4_K: q = 256; b = 144; break;
@@ -562,9 +571,11 @@ int anvil_mmvq_block_sums(int ggml_type, const void *W, const void *xq, int32_t 
 // flags (0 = no bounded wait gave up) or a negative status.
 int anvil_take_device_status(void) {
     int v = 0;
-    int parts[5] = {take_quantize_status(), mmvq_kernel_q4k_take_status(),
+    int parts[9] = {take_quantize_status(), mmvq_kernel_q4k_take_status(),
                     mmvq_kernel_q5k_take_status(), mmvq_kernel_q6k_take_status(),
-                    mmvq_kernel_q80_take_status()};
+                    mmvq_kernel_q80_take_status(), mmvq_kernel_q40_take_status(),
+                    mmvq_kernel_q41_take_status(), mmvq_kernel_q50_take_status(),
+                    mmvq_kernel_q51_take_status()};
     for (int x : parts) {
         if (x < 0) return fail(ANVIL_ERR_CUDA, "reading device status failed");
         v |= x;

@@ -5,6 +5,11 @@
 //   Q4_K (144 B / 256 weights): d f16 @0, dmin f16 @2, scales[12] @4, qs[128] @16
 //   Q5_K (176 B / 256 weights): d @0, dmin @2, scales[12] @4, qh[32] @16, qs[128] @48
 //   Q6_K (210 B / 256 weights): ql[128] @0, qh[64] @128, scales int8[16] @192, d f16 @208
+//   Q4_0 ( 18 B /  32 weights): d f16 @0, qs[16] @2 (nibbles; weight e < 16 = low nibble
+//                                of qs[e], e >= 16 = high nibble of qs[e-16]; q - 8)
+//   Q4_1 ( 20 B /  32 weights): d f16 @0, m f16 @2, qs[16] @4 (x = d q + m)
+//   Q5_0 ( 22 B /  32 weights): d f16 @0, qh u32 @2 (bit e = bit 4 of weight e), qs[16] @6; q - 16
+//   Q5_1 ( 24 B /  32 weights): d f16 @0, m f16 @2, qh u32 @4, qs[16] @8 (x = d q + m)
 //   Q8_0 ( 34 B /  32 weights): d f16 @0, qs int8[32] @2
 //   Q8_1 ( 36 B /  32 values ): d f16 @0, s f16 @2, qs int8[32] @4   (GPU layout)
 // (gguf-py quants.py:396-401, 504-523, 527-549, 554-572; kernel_anvil/hip_codegen.py:101-102,
@@ -16,6 +21,10 @@
 
 namespace anvil {
 
+constexpr int kTypeQ4_0 = 2;
+constexpr int kTypeQ4_1 = 3;
+constexpr int kTypeQ5_0 = 6;
+constexpr int kTypeQ5_1 = 7;
 constexpr int kTypeQ8_0 = 8;
 constexpr int kTypeQ8_1 = 9;
 constexpr int kTypeQ4_K = 12;
@@ -38,6 +47,18 @@ template <> struct QTraits<kTypeQ5_K> {
 };
 template <> struct QTraits<kTypeQ6_K> {
     static constexpr int qk = 256, bytes = 210, units = 4, sub = 16;
+};
+template <> struct QTraits<kTypeQ4_0> {
+    static constexpr int qk = 32, bytes = 18, units = 1, sub = 32;
+};
+template <> struct QTraits<kTypeQ4_1> {
+    static constexpr int qk = 32, bytes = 20, units = 1, sub = 32;
+};
+template <> struct QTraits<kTypeQ5_0> {
+    static constexpr int qk = 32, bytes = 22, units = 1, sub = 32;
+};
+template <> struct QTraits<kTypeQ5_1> {
+    static constexpr int qk = 32, bytes = 24, units = 1, sub = 32;
 };
 template <> struct QTraits<kTypeQ8_0> {
     static constexpr int qk = 32, bytes = 34, units = 1, sub = 32;

@@ -640,7 +640,10 @@ int anvil_pchain_add_gemv(anvil_pchain *c, int ggml_type, const void *W, int nro
     if (c->groups.empty()) return fail(ANVIL_ERR_INVALID, "add a group first");
     int qk, bb;
     if (int s = anvil_type_geometry(ggml_type, &qk, &bb)) return s;
-    if (ggml_type == ANVIL_TYPE_Q8_1) return fail(ANVIL_ERR_UNSUPPORTED, "Q8_1 weights");
+    if (ggml_type != ANVIL_TYPE_Q8_0 && ggml_type != ANVIL_TYPE_Q4_K && ggml_type != ANVIL_TYPE_Q5_K &&
+        ggml_type != ANVIL_TYPE_Q6_K)
+        return fail(ANVIL_ERR_UNSUPPORTED, "the persistent chain takes Q8_0, Q4_K, Q5_K and Q6_K "
+                                           "weights (type %d)", ggml_type);
     PcGroup &g = c->groups.back();
     if (g.K % qk) return fail(ANVIL_ERR_INVALID, "K=%d is not a multiple of the block size %d", g.K, qk);
     if (nrows < 1 || row0 < 0 || nrows_full < row0 + nrows)

@@ -87,9 +87,26 @@ struct MmvqSmem {
 };
 
 __host__ __device__ inline int mmvq_type_bytes(int qt) {
-    return qt == kTypeQ4_K ? 144 : qt == kTypeQ5_K ? 176 : qt == kTypeQ6_K ? 210 : 34;
+    switch (qt) {
+    case kTypeQ4_0: return 18;
+    case kTypeQ4_1: return 20;
+    case kTypeQ5_0: return 22;
+    case kTypeQ5_1: return 24;
+    case kTypeQ4_K: return 144;
+    case kTypeQ5_K: return 176;
+    case kTypeQ6_K: return 210;
+    default: return 34;
+    }
 }
-__host__ __device__ inline int mmvq_type_qk(int qt) { return qt == kTypeQ8_0 ? 32 : 256; }
+__host__ __device__ inline int mmvq_type_qk(int qt) {
+    return qt == kTypeQ4_K || qt == kTypeQ5_K || qt == kTypeQ6_K ? 256 : 32;
+}
+
+// The 32-weight "basic" types (one Q8_1 block per weight block, one unit per block).
+template <int QT>
+constexpr bool kBasic = QT == kTypeQ4_0 || QT == kTypeQ4_1 || QT == kTypeQ5_0 || QT == kTypeQ5_1;
+template <int QT>
+constexpr bool kBlock32 = QT == kTypeQ8_0 || kBasic<QT>;
 
 // Bytes of one column's swizzled activation quants: 2 chunks of 16 B per Q8_1 block,
 // padded to whole 16-chunk groups so the XOR swizzle never leaves the column.
@@ -122,7 +139,7 @@ __host__ __device__ inline MmvqSmem mmvq_smem_layout(int qt, int K, int ncols, i
 // line of each pair of lines is shifted by one slot.
 template <int QT>
 __device__ __forceinline__ int act_chunk(int ci) {
-    if constexpr (QT == kTypeQ8_0) {
+    if constexpr (kBlock32<QT>) {
         return ci ^ ((ci >> 3) & 1);
     } else {
         return ci ^ ((ci >> 4) & 7);
@@ -144,6 +161,26 @@ __device__ __forceinline__ void lds32_a2(const uint8_t *p, uint32_t (&w)[8]) {
         w[k] = __funnelshift_r(prev, nx, sh);
         prev = nx;
     }
+}
+
+// 16 bytes starting at a 2-byte aligned shared-memory address, as 4 little-endian words:
+// five aligned word loads (at most 3 bytes read past the 16) and a funnel shift.
+__device__ __forceinline__ void lds16B_a2(const uint8_t *p, uint32_t (&w)[4]) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    const uint32_t *q = reinterpret_cast<const uint32_t *>(a & ~uintptr_t(3));
+    const uint32_t sh = uint32_t(a & 3) * 8;
+    uint32_t prev = q[0];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const uint32_t nx = q[k + 1];
+        w[k] = __funnelshift_r(prev, nx, sh);
+        prev = nx;
+    }
+}
+
+// Bits 0..3 of h moved to bit 4 of bytes 0..3 (the fifth bit of four 5-bit quants).
+__device__ __forceinline__ uint32_t spread_bit4(uint32_t h) {
+    return ((h & 1u) << 4) | ((h & 2u) << 11) | ((h & 4u) << 18) | ((h & 8u) << 25);
 }
 
 __device__ __forceinline__ uint32_t lds16(const uint8_t *p) {
@@ -186,8 +223,9 @@ __device__ __forceinline__ void load_act(const ActView &v, int kb, ActBlk &a) {
     a.d = v.ad[kb];
     a.ds = 0.f;
     a.slo = a.shi = 0;
-    if constexpr (QT == kTypeQ4_K || QT == kTypeQ5_K) a.ds = v.ads[kb];
-    if constexpr (QT == kTypeQ6_K) {
+    if constexpr (QT == kTypeQ4_K || QT == kTypeQ5_K || QT == kTypeQ4_1 || QT == kTypeQ5_1)
+        a.ds = v.ads[kb];
+    if constexpr (QT == kTypeQ6_K || QT == kTypeQ4_0 || QT == kTypeQ5_0) {
         const int2 s = v.as[kb];
         a.slo = s.x;
         a.shi = s.y;
@@ -208,11 +246,15 @@ struct BlkHdr {
 
 template <int QT> struct Units { static constexpr int n = 4; };
 template <> struct Units<kTypeQ8_0> { static constexpr int n = 1; };
+template <> struct Units<kTypeQ4_0> { static constexpr int n = 1; };
+template <> struct Units<kTypeQ4_1> { static constexpr int n = 1; };
+template <> struct Units<kTypeQ5_0> { static constexpr int n = 1; };
+template <> struct Units<kTypeQ5_1> { static constexpr int n = 1; };
 
 // Q8_1 blocks consumed by unit U of super-block b.
 template <int QT, int U>
 __device__ __forceinline__ void unit_kb(int b, int &kb0, int &kb1) {
-    if constexpr (QT == kTypeQ8_0) {
+    if constexpr (kBlock32<QT>) {
         kb0 = b;
         kb1 = b;
     } else if constexpr (QT == kTypeQ6_K) {
@@ -238,6 +280,9 @@ __device__ __forceinline__ BlkHdr load_hdr(const uint8_t *blk) {
         h.s2 = v.w;
     } else if constexpr (QT == kTypeQ6_K) {
         h.d = h2f(lds16(blk + 208));
+    } else if constexpr (QT == kTypeQ4_1 || QT == kTypeQ5_1) {
+        h.d = h2f(lds16(blk));
+        h.dmin = h2f(lds16(blk + 2));  // m, the block's added minimum
     } else {
         h.d = h2f(lds16(blk));
     }
@@ -305,6 +350,27 @@ __device__ __forceinline__ void load_unit(const uint8_t *blk, WBytes &w) {
             w.q0[k] = (ql[k] & 0x0F0F0F0Fu) | (((qh[k] >> (2 * t)) & 0x03030303u) << 4);
             w.q1[k] = ((ql[k] >> 4) & 0x0F0F0F0Fu) | ((qh[k] >> (2 * t)) & 0x30303030u);
         }
+    } else if constexpr (kBasic<QT>) {
+        // quants in Q8_1 element order: words 0..3 the low nibbles of qs[0..15] (weights
+        // 0..15), words 4..7 the high nibbles (weights 16..31); the 5-bit types add bit e of
+        // qh as bit 4 of weight e (gguf-py quants.py Q4_0..Q5_1 dequantize_blocks)
+        constexpr int qs_off = QT == kTypeQ4_0 ? 2 : QT == kTypeQ4_1 ? 4 : QT == kTypeQ5_0 ? 6 : 8;
+        uint32_t v[4];
+        lds16B_a2(blk + qs_off, v);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            w.q0[k] = v[k] & 0x0F0F0F0Fu;
+            w.q0[4 + k] = (v[k] >> 4) & 0x0F0F0F0Fu;
+        }
+        if constexpr (QT == kTypeQ5_0 || QT == kTypeQ5_1) {
+            constexpr int qh_off = QT == kTypeQ5_0 ? 2 : 4;
+            const uint32_t qh = lds16(blk + qh_off) | (lds16(blk + qh_off + 2) << 16);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                w.q0[k] |= spread_bit4((qh >> (4 * k)) & 15u);
+                w.q0[4 + k] |= spread_bit4((qh >> (16 + 4 * k)) & 15u);
+            }
+        }
     } else {  // Q8_0
         lds32_a2(blk + 2, w.q0);
     }
@@ -361,6 +427,17 @@ __device__ __forceinline__ float dot_unit(const uint8_t *blk, const BlkHdr &h, c
         const int s00 = int(int8_t(sc0 & 0xFF)), s01 = int(int8_t(sc0 >> 8));
         const int s10 = int(int8_t(sc1 & 0xFF)), s11 = int(int8_t(sc1 >> 8));
         return h.d * (a0.d * float(p00 * s00 + p01 * s01) + a1.d * float(p10 * s10 + p11 * s11));
+    } else if constexpr (kBasic<QT>) {
+        // Q4_0 / Q5_0: d * d8 * sum((q - 8 | q - 16) q8), the offset through the block's
+        // sum of q8; Q4_1 / Q5_1: d * d8 * sum(q q8) + m * d8 * sum(q8).
+        int i0 = 0;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) i0 = __dp4a(int(w.q0[k]), int(a0.q[k]), i0);
+        if constexpr (QT == kTypeQ4_0) i0 -= 8 * (a0.slo + a0.shi);
+        if constexpr (QT == kTypeQ5_0) i0 -= 16 * (a0.slo + a0.shi);
+        isum[0] = i0;
+        if constexpr (QT == kTypeQ4_1 || QT == kTypeQ5_1) return h.d * (a0.d * float(i0)) + h.dmin * a0.ds;
+        return h.d * (a0.d * float(i0));
     } else {
         int i0 = 0;
 #pragma unroll
@@ -377,7 +454,7 @@ __device__ __forceinline__ void store_sums(int32_t *srow, int kb0, int kb1, cons
         srow[2 * kb0 + 1] = isum[1];
         srow[2 * kb1] = isum[2];
         srow[2 * kb1 + 1] = isum[3];
-    } else if constexpr (QT == kTypeQ8_0) {
+    } else if constexpr (kBlock32<QT>) {
         srow[kb0] = isum[0];
     } else {
         srow[kb0] = isum[0];
@@ -427,7 +504,7 @@ __device__ __forceinline__ void unit_step(const TileCtx &t, int b, const BlkHdr 
     if constexpr (NCOLS == 1) {
         const ActView v{t.aq, t.ad, t.ads, t.as};
         load_act<QT>(v, kb0, a0);
-        if constexpr (QT != kTypeQ8_0) load_act<QT>(v, kb1, a1);
+        if constexpr (!kBlock32<QT>) load_act<QT>(v, kb1, a1);
     }
     const uint8_t *blk0 = t.lane_row0 + b * TR::bytes;
 #pragma unroll
@@ -441,10 +518,10 @@ __device__ __forceinline__ void unit_step(const TileCtx &t, int b, const BlkHdr 
                 const ActView v{t.aq + c * t.acb, t.ad + c * t.nkb, t.ads + c * t.nkb,
                                 t.as + c * t.nkb};
                 load_act<QT>(v, kb0, a0);
-                if constexpr (QT != kTypeQ8_0) load_act<QT>(v, kb1, a1);
+                if constexpr (!kBlock32<QT>) load_act<QT>(v, kb1, a1);
             }
             int isum[4];
-            acc[sl][c] += dot_unit<QT, U>(blk, hdr[sl], wb, a0, QT == kTypeQ8_0 ? a0 : a1, isum);
+            acc[sl][c] += dot_unit<QT, U>(blk, hdr[sl], wb, a0, kBlock32<QT> ? a0 : a1, isum);
             if constexpr (MODE == kModeSums) {
                 const int i = sl * t.RG + t.grp;
                 if (i < t.rows) {
@@ -803,11 +880,19 @@ MmvqKernelFn mmvq_kernel_q4k(int ncols, int rpb, int lbt, int mode);
 MmvqKernelFn mmvq_kernel_q5k(int ncols, int rpb, int lbt, int mode);
 MmvqKernelFn mmvq_kernel_q6k(int ncols, int rpb, int lbt, int mode);
 MmvqKernelFn mmvq_kernel_q80(int ncols, int rpb, int lbt, int mode);
+MmvqKernelFn mmvq_kernel_q40(int ncols, int rpb, int lbt, int mode);
+MmvqKernelFn mmvq_kernel_q41(int ncols, int rpb, int lbt, int mode);
+MmvqKernelFn mmvq_kernel_q50(int ncols, int rpb, int lbt, int mode);
+MmvqKernelFn mmvq_kernel_q51(int ncols, int rpb, int lbt, int mode);
 // Reads and clears the device status word of that type's translation unit (current device).
 int mmvq_kernel_q4k_take_status();
 int mmvq_kernel_q5k_take_status();
 int mmvq_kernel_q6k_take_status();
 int mmvq_kernel_q80_take_status();
+int mmvq_kernel_q40_take_status();
+int mmvq_kernel_q41_take_status();
+int mmvq_kernel_q50_take_status();
+int mmvq_kernel_q51_take_status();
 
 }  // namespace anvil
 

@@ -51,6 +51,10 @@ class QuantTypeInfo:
 
 
 QUANT_TYPES: dict[str, QuantTypeInfo] = {
+    "Q4_0": QuantTypeInfo("Q4_0", 2, 32, 4, 2, 18),
+    "Q4_1": QuantTypeInfo("Q4_1", 3, 32, 4, 2, 20),
+    "Q5_0": QuantTypeInfo("Q5_0", 6, 32, 4, 2, 22),
+    "Q5_1": QuantTypeInfo("Q5_1", 7, 32, 4, 2, 24),
     "Q8_0": QuantTypeInfo("Q8_0", 8, 32, 8, 2, 34),
     "Q4_K": QuantTypeInfo("Q4_K", 12, 256, 32, 2, 144),
     "Q5_K": QuantTypeInfo("Q5_K", 13, 256, 32, 2, 176),
@@ -113,6 +117,14 @@ def make_weights(qt, nrows: int, K: int, seed: int = 0) -> np.ndarray:
     elif info.name == "Q8_0":
         blocks[:, 0:2] = _fp16_abs_normal(rng, nb, 1e-2)
         blocks[:, 2:34] = rng.integers(-127, 128, size=(nb, 32), dtype=np.int8).view(np.uint8)
+    elif info.name in ("Q4_0", "Q4_1", "Q5_0", "Q5_1"):
+        # d from |N(0,1)| * 1e-2; the _1 types' m (the block minimum) from -|N(0,1)| * 1e-1;
+        # high bits (qh) and nibbles uniform
+        blocks[:, 2:] = rng.integers(0, 256, size=(nb, info.block_size - 2), dtype=np.uint8)
+        blocks[:, 0:2] = _fp16_abs_normal(rng, nb, 1e-2)
+        if info.name.endswith("_1"):
+            m = (-np.abs(rng.standard_normal(nb)) * 1e-1).astype(np.float16)
+            blocks[:, 2:4] = m.view(np.uint8).reshape(nb, 2)
     else:  # pragma: no cover - resolve_type rejects other types
         raise ValueError(info.name)
     return blocks.reshape(nrows, row_bytes)
@@ -151,4 +163,9 @@ def make_weights_device(qt, nrows: int, K: int, seed: int = 0, device="cuda"):
         blocks[:, 0:2] = fp16_abs_normal(1e-2)
         q = torch.randint(-127, 128, (nb, 32), dtype=torch.int8, device=device, generator=g)
         blocks[:, 2:34] = q.view(torch.uint8)
+    elif info.name in ("Q4_0", "Q4_1", "Q5_0", "Q5_1"):
+        blocks[:, 0:2] = fp16_abs_normal(1e-2)
+        if info.name.endswith("_1"):
+            m = (torch.randn(nb, device=device, generator=g).abs_().mul_(-1e-1)).to(torch.float16)
+            blocks[:, 2:4] = m.view(torch.uint8).view(nb, 2)
     return blocks.view(nrows, row_bytes)

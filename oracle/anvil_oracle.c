@@ -4,10 +4,11 @@
  * cpu_baseline leg of bench.py.  Nothing in the product links or calls it.
  *
  * What it restates, and from where:
- *   - GGUF block layouts and per-weight dequantisation of Q4_K, Q5_K, Q6_K and Q8_0:
- *     gguf-py (the reference's declared dependency, kernel-anvil pyproject.toml:19,
- *     gguf 0.19.0) gguf/quants.py:378-401 (Q8_0), 474-523 (Q4_K incl. get_scale_min),
- *     525-549 (Q5_K), 552-572 (Q6_K).  Pinned in tests against gguf.quants.dequantize.
+ *   - GGUF block layouts and per-weight dequantisation of Q4_0, Q4_1, Q5_0, Q5_1, Q4_K,
+ *     Q5_K, Q6_K and Q8_0: gguf-py (the reference's declared dependency, kernel-anvil
+ *     pyproject.toml:19, gguf 0.19.0) gguf/quants.py Q4_0..Q5_1 dequantize_blocks,
+ *     378-401 (Q8_0), 474-523 (Q4_K incl. get_scale_min), 525-549 (Q5_K), 552-572 (Q6_K).
+ *     Pinned in tests against gguf.quants.dequantize (fixtures and live).
  *   - Q8_1 activation quantisation: llama.cpp's CUDA quantize_q8_1 semantics (the
  *     reference's runtime path: kernel_anvil/hip_codegen.py:392-396 layout, 101-102 size;
  *     docs/decode-pipeline-breakdown.md:21): per 32 values d = max|x|/127,
@@ -33,7 +34,7 @@
 #include <omp.h>
 #endif
 
-enum { T_Q8_0 = 8, T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14 };
+enum { T_Q4_0 = 2, T_Q4_1 = 3, T_Q5_0 = 6, T_Q5_1 = 7, T_Q8_0 = 8, T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14 };
 
 /* ---- IEEE binary16 conversions (written from the format definition) ---------- */
 
@@ -172,9 +173,39 @@ static inline int q6k_quant(const uint8_t *blk, int j, int e) {
 }
 
 static int type_bytes(int t) {
-    return t == T_Q4_K ? 144 : t == T_Q5_K ? 176 : t == T_Q6_K ? 210 : t == T_Q8_0 ? 34 : 0;
+    switch (t) {
+    case T_Q4_0: return 18;
+    case T_Q4_1: return 20;
+    case T_Q5_0: return 22;
+    case T_Q5_1: return 24;
+    case T_Q8_0: return 34;
+    case T_Q4_K: return 144;
+    case T_Q5_K: return 176;
+    case T_Q6_K: return 210;
+    default: return 0;
+    }
 }
-static int type_qk(int t) { return t == T_Q8_0 ? 32 : 256; }
+static int is_basic(int t) { return t == T_Q4_0 || t == T_Q4_1 || t == T_Q5_0 || t == T_Q5_1; }
+static int type_qk(int t) { return (t == T_Q8_0 || is_basic(t)) ? 32 : 256; }
+
+/* Q4_0 / Q4_1 / Q5_0 / Q5_1 (gguf-py quants.py Q4_0..Q5_1 dequantize_blocks): 32 weights;
+ * element e < 16 is the low nibble of qs[e], element e >= 16 the high nibble of qs[e - 16];
+ * the _5 types add bit e of the little-endian uint32 qh as bit 4.  Q4_0 subtracts 8, Q5_0
+ * subtracts 16; the _1 types keep the unsigned value and add m. */
+static int basic_qs_off(int t) { return t == T_Q4_0 ? 2 : t == T_Q4_1 ? 4 : t == T_Q5_0 ? 6 : 8; }
+static inline int basic_quant(int t, const uint8_t *blk, int e) {
+    const uint8_t *qs = blk + basic_qs_off(t);
+    int q = e < 16 ? (qs[e] & 15) : (qs[e - 16] >> 4);
+    if (t == T_Q5_0 || t == T_Q5_1) {
+        const uint8_t *h = blk + (t == T_Q5_0 ? 2 : 4);
+        const uint32_t qh = (uint32_t)h[0] | ((uint32_t)h[1] << 8) | ((uint32_t)h[2] << 16) |
+                            ((uint32_t)h[3] << 24);
+        q |= (int)((qh >> e) & 1u) << 4;
+    }
+    if (t == T_Q4_0) q -= 8;
+    if (t == T_Q5_0) q -= 16;
+    return q;
+}
 
 /* ---- dequantisation (gguf-py float32 operation order) -------------------------- */
 
@@ -189,6 +220,14 @@ int oracle_dequant(int type, const uint8_t *W, float *out, int64_t nrows, int64_
         if (type == T_Q8_0) {
             const float d = oracle_half_to_float(rd16(blk));
             for (int e = 0; e < 32; ++e) o[e] = (float)(int8_t)blk[2 + e] * d;
+        } else if (is_basic(type)) {
+            const float d = oracle_half_to_float(rd16(blk));
+            if (type == T_Q4_1 || type == T_Q5_1) {
+                const float m = oracle_half_to_float(rd16(blk + 2));
+                for (int e = 0; e < 32; ++e) o[e] = d * (float)basic_quant(type, blk, e) + m;
+            } else {
+                for (int e = 0; e < 32; ++e) o[e] = d * (float)basic_quant(type, blk, e);
+            }
         } else if (type == T_Q6_K) {
             const float d = oracle_half_to_float(rd16(blk + 208));
             for (int j = 0; j < 8; ++j)
@@ -239,6 +278,13 @@ int oracle_block_sums(int type, const uint8_t *W, const uint8_t *xq, int32_t *su
                     out[b] = s;
                     continue;
                 }
+                if (is_basic(type)) {
+                    const int8_t *a = (const int8_t *)(xc + b * 36 + 4);
+                    int32_t s = 0;
+                    for (int e = 0; e < 32; ++e) s += basic_quant(type, blk, e) * a[e];
+                    out[b] = s;
+                    continue;
+                }
                 for (int j = 0; j < 8; ++j) {
                     const int8_t *a = (const int8_t *)(xc + (8 * b + j) * 36 + 4);
                     if (type == T_Q6_K) {
@@ -280,6 +326,21 @@ int oracle_mmvq(int type, const uint8_t *W, const uint8_t *xq, double *y, int64_
                     for (int e = 0; e < 32; ++e) s += (int32_t)(int8_t)blk[2 + e] * a[e];
                     acc += (double)oracle_half_to_float(rd16(blk)) *
                            (double)oracle_half_to_float(rd16(ab)) * (double)s;
+                    continue;
+                }
+                if (is_basic(type)) {
+                    /* d * d8 * sum(q * q8), plus m * d8 * sum(q8) for the _1 types */
+                    const uint8_t *ab = xc + b * 36;
+                    const int8_t *a = (const int8_t *)(ab + 4);
+                    int32_t s = 0, sq = 0;
+                    for (int e = 0; e < 32; ++e) {
+                        s += basic_quant(type, blk, e) * a[e];
+                        sq += a[e];
+                    }
+                    const double d8 = oracle_half_to_float(rd16(ab));
+                    acc += (double)oracle_half_to_float(rd16(blk)) * d8 * (double)s;
+                    if (type == T_Q4_1 || type == T_Q5_1)
+                        acc += (double)oracle_half_to_float(rd16(blk + 2)) * d8 * (double)sq;
                     continue;
                 }
                 if (type == T_Q6_K) {

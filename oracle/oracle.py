@@ -17,7 +17,7 @@ HERE = Path(__file__).resolve().parent
 LIB = HERE / "_build" / "liboracle.so"
 REF_SMITHY = HERE / "_ref" / "libsmithy_ref.so"
 
-TYPE_IDS = {"Q8_0": 8, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14}
+TYPE_IDS = {"Q4_0": 2, "Q4_1": 3, "Q5_0": 6, "Q5_1": 7, "Q8_0": 8, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14}
 
 _lib = None
 

@@ -20,7 +20,7 @@ from oracle import oracle  # noqa: E402
 
 pytestmark = pytest.mark.gpu
 
-TYPES = ["Q4_K", "Q5_K", "Q6_K", "Q8_0"]
+TYPES = ["Q4_K", "Q5_K", "Q6_K", "Q8_0", "Q4_0", "Q4_1", "Q5_0", "Q5_1"]
 Y_TOL = 1e-3
 
 
@@ -87,6 +87,10 @@ def test_batched_columns(qt, ncols):
     ("Q6_K", 17, 3072), ("Q6_K", 9, 5120),     # 2520 / 4200-byte rows
     ("Q6_K", 1024, 4096), ("Q6_K", 300, 12288),
     ("Q8_0", 1, 32), ("Q8_0", 13, 96),         # 102-byte rows
+    ("Q4_0", 1, 32), ("Q4_0", 7, 96), ("Q4_0", 4096, 4096),   # 18- / 54-byte rows
+    ("Q4_1", 5, 64), ("Q4_1", 2048, 4096),
+    ("Q5_0", 3, 32), ("Q5_0", 11, 160), ("Q5_0", 1024, 14336),  # 22- / 110-byte rows
+    ("Q5_1", 9, 224), ("Q5_1", 1024, 4096),
     ("Q8_0", 7, 1056), ("Q8_0", 3072, 1024), ("Q8_0", 1024, 3072),
 ])
 def test_shapes(qt, nrows, K):

@@ -13,7 +13,7 @@ import pytest
 from kernel_anvil.quants import QUANT_TYPES, make_activation, make_weights
 from oracle import oracle
 
-TYPES = ["Q4_K", "Q5_K", "Q6_K", "Q8_0"]
+TYPES = ["Q4_K", "Q5_K", "Q6_K", "Q8_0", "Q4_0", "Q4_1", "Q5_0", "Q5_1"]
 
 
 @pytest.mark.parametrize("qt", TYPES)
@@ -114,9 +114,12 @@ def test_block_sums_reconstruct_y(qt):
     for r in range(n):
         for b in range(k // info.qk):
             blk = blocks[r, b]
-            if qt == "Q8_0":
+            if qt == "Q8_0" or qt in ("Q4_0", "Q5_0"):
                 d = blk[0:2].copy().view(np.float16).astype(np.float64)[0]
                 y[r] += d * d8[b] * sums[r, b]
+            elif qt in ("Q4_1", "Q5_1"):  # unsigned quants; the min m times d8 * sum(q8)
+                d, m = blk[0:4].copy().view(np.float16).astype(np.float64)
+                y[r] += d * d8[b] * sums[r, b] + m * d8[b] * qsum[b]
             elif qt == "Q6_K":
                 d = blk[208:210].copy().view(np.float16).astype(np.float64)[0]
                 sc = blk[192:208].view(np.int8).astype(np.float64)
