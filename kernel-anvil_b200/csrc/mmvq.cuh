@@ -897,8 +897,8 @@ int mmvq_kernel_q51_take_status();
 }  // namespace anvil
 
 // Builds the [ncols 1..8] x [rpb 1,2,4,8] x [mode] x [lanes per row 16 / 32 / runtime]
-// table for one type.  lbt is 16 or 32 for the compile-time variants, anything else for
-// the runtime-LB kernel.
+// table for one type (compile-time lanes per row for 1, 2, 4 and 8 columns).  lbt is 16 or
+// 32 for the compile-time variants, anything else for the runtime-LB kernel.
 #define ANVIL_MMVQ_TABLE(FN, QT)                                                          \
     namespace anvil {                                                                     \
     template <int NC, int R, int LBT>                                                     \
@@ -912,7 +912,7 @@ int mmvq_kernel_q51_take_status();
     }                                                                                     \
     template <int NC, int R>                                                              \
     static MmvqKernelFn FN##_lb(int lbt, int mode) {                                      \
-        if constexpr (NC == 1) {                                                          \
+        if constexpr (NC == 1 || NC == 2 || NC == 4 || NC == 8) {                         \
             if (lbt == 16) return FN##_mode<NC, R, 16>(mode);                             \
             if (lbt == 32) return FN##_mode<NC, R, 32>(mode);                             \
         }                                                                                 \
