@@ -75,6 +75,9 @@ def parse_args():
     ap.add_argument("--grouped", type=int, default=1,
                     help="graph executor: one launch per run of same-type GEMVs on one input (1) "
                          "quantising in the kernel, or one launch per GEMV (0)")
+    ap.add_argument("--glu", type=int, default=0,
+                    help="grouped graph executor: each layer's ffn_gate/ffn_up pair as one launch "
+                         "with silu(gate) * up in the epilogue (1), or as a grouped GEMV pair (0)")
     ap.add_argument("--multi", choices=["replicas", "rows"], default="replicas",
                     help="N > 1: one full chain per GPU (independent token streams, no collective; "
                          "weak scaling) or every matrix row-sharded across the GPUs with the outputs "
@@ -236,7 +239,8 @@ def dominant_kernel(dc, stream, steps: int, warmup: int) -> dict:
     run of Q4_K GEMVs on one input when grouped) and replayed as their own PDL graph."""
     import torch
 
-    from kernel_anvil.mmvq import Chain
+    from kernel_anvil.chains import is_gate_up
+    from kernel_anvil.mmvq import Chain, q8_1_bytes
     from kernel_anvil.quants import gemv_bytes
 
     ch = Chain()
@@ -250,7 +254,12 @@ def dominant_kernel(dc, stream, steps: int, warmup: int) -> dict:
             while (j < len(gemvs) and j - i < 4 and gemvs[j][0].input == gm.input
                    and gemvs[j][0].qt == gm.qt):
                 j += 1
-        if gm.qt == "Q4_K":
+        if gm.qt == "Q4_K" and dc.glu and is_gate_up([g for g, _, _, _ in gemvs[i:j]]):
+            ch.add_mmvq_glu(gemvs[i][1], gemvs[i + 1][1], gm.qt, dc.xq[gm.input], gemvs[i][2])
+            r = gemvs[i][3][1] - gemvs[i][3][0]
+            nbytes += 2 * gemv_bytes(gm.qt, r, gm.K, 1) - 4 * r - q8_1_bytes(gm.K)
+            n += 1
+        elif gm.qt == "Q4_K":
             run = gemvs[i:j]
             rows = [r1 - r0 for _, _, _, (r0, r1) in run]
             ch.add_mmvq_grouped([w for _, w, _, _ in run], gm.qt, dc.xq[gm.input],
@@ -310,10 +319,13 @@ def run_anvil(args) -> None:
                      seed=0 if shard else rank, fused=args.quantize == "fused",
                      coresident=args.coresident, executor=args.executor,
                      dist=dist if shard else None, nwarps=args.nwarps,
-                     ctas_per_sm=args.ctas_per_sm, grouped=bool(args.grouped) and not persistent)
+                     ctas_per_sm=args.ctas_per_sm, grouped=bool(args.grouped) and not persistent,
+                     glu=bool(args.glu))
     stream = torch.cuda.Stream(device=dev)
     hbm_peak, peak_kind = measured_peaks()
-    total_bytes = spec.algorithmic_bytes() * (1 if shard or world == 1 else world)  # whole job
+    # whole job (gate/up launches write one vector per pair: the chain's own count)
+    total_bytes = ((dc.algorithmic_bytes if dc.glu else spec.algorithmic_bytes())
+                   * (1 if shard or world == 1 else world))
     rank_bytes = dc.algorithmic_bytes       # this rank's shard
 
     graph = None
@@ -451,6 +463,7 @@ def run_anvil(args) -> None:
                                 "CUDA graph of quantize + MMVQ launches, programmatic dependent launch"),
                    "quantize": "in-kernel per group" if persistent else args.quantize,
                    "grouped_launches": bool(args.grouped) and not persistent,
+                   "gate_up_glu": dc.glu,
                    **({"persistent": pinfo} if persistent else
                       {"coresident_kernels_per_sm": args.coresident})},
         "e2e": e2e, "roofline": roofline, "gpu_launches": launches_per_step * args.steps,

@@ -159,6 +159,24 @@ int anvil_mmvq_grouped_f32(int ggml_type, int nseg, const void *const *W, const 
                            void *xq, float *const *y, const int *nrows, int ncols_x, int ncols_dst,
                            int nwarps, int rows_per_block, unsigned flags, anvil_stream_t stream);
 
+/* Gate/up GEMV pair with the SwiGLU product in the epilogue, one activation column:
+ * y[r] = silu(g) * u with g = W_gate[r] . dequant(xq), u = W_up[r] . dequant(xq) and
+ * silu(g) = g / (1 + exp(-g)), r < nrows.  g and u are each what anvil_mmvq computes for
+ * its matrix alone with the same lanes per row; neither is written out.  Replaces the
+ * llama.cpp decode sequence mul_mat_vec_q(gate), mul_mat_vec_q(up), GLU: the
+ * "Q4_K fused (gate+SiLU)" MMVQ variant of docs/decode-pipeline-breakdown.md:40, the fused
+ * gate+up launch of docs/vulkan-vs-rocm-analysis.md:103-106 and its GLU op (:135).  Both matrices have ggml_type and nrows x ncols_x
+ * values; their rows must be a multiple of 16 bytes (Q4_K, Q5_K always; Q8_0, Q4_0 .. Q5_1
+ * when ncols_x % 256 == 0; Q6_K when ncols_x % 2048 == 0), else ANVIL_ERR_ALIGN.
+ * rows_per_block counts gate and up rows together (at least 2).  _f32: fp32 x quantised
+ * into the scratch xq first (two launches, the second under ANVIL_FLAG_PDL). */
+int anvil_mmvq_glu(int ggml_type, const void *W_gate, const void *W_up, const void *xq, float *y,
+                   int nrows, int ncols_x, int nwarps, int rows_per_block, unsigned flags,
+                   anvil_stream_t stream);
+int anvil_mmvq_glu_f32(int ggml_type, const void *W_gate, const void *W_up, const float *x,
+                       void *xq, float *y, int nrows, int ncols_x, int nwarps, int rows_per_block,
+                       unsigned flags, anvil_stream_t stream);
+
 /* Reads and clears the device status words of the current device: the OR of
  * anvil_device_status flags set by kernels whose bounded waits gave up (0 = none),
  * or a negative anvil_status.  Synchronous. */
@@ -207,6 +225,10 @@ int anvil_chain_add_mmvq_grouped(anvil_chain *chain, int ggml_type, int nseg, co
 int anvil_chain_add_mmvq_grouped_f32(anvil_chain *chain, int ggml_type, int nseg, const void *const *W,
                                      const float *x, void *xq, float *const *y, const int *nrows,
                                      int ncols_x, int ncols_dst, int nwarps, int rows_per_block);
+/* Gate/up step: anvil_mmvq_glu's launch as a chain step (reads xq, writes y). */
+int anvil_chain_add_mmvq_glu(anvil_chain *chain, int ggml_type, const void *W_gate,
+                             const void *W_up, const void *xq, float *y, int nrows, int ncols_x,
+                             int nwarps, int rows_per_block);
 /* Sizes every GEMV grid so that `kernels_per_sm` consecutive GEMVs (1..4) fit on each SM
  * together: with programmatic dependent launch the next GEMV's CTAs are then resident
  * while the current one runs and stream their first weight tiles early.  Default 1 (each

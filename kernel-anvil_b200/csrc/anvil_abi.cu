@@ -213,6 +213,8 @@ static int plan_mmvq(int t, int nrows, int K, int ncols, int nwarps, int rpb, in
         return fail(ANVIL_ERR_INVALID, "ncols_x=%d is not a multiple of the block size %d", K, qk);
     if (ncols < 1 || ncols > kMaxCols)
         return fail(ANVIL_ERR_INVALID, "ncols_dst=%d outside 1..%d", ncols, kMaxCols);
+    if (mode == kModeGLU && ncols != 1)
+        return fail(ANVIL_ERR_INVALID, "the gate/up epilogue takes one column, got %d", ncols);
     if (nwarps < 0 || rpb < 0)
         return fail(ANVIL_ERR_INVALID, "nwarps=%d rows_per_block=%d", nwarps, rpb);
     if (nwarps == 0 || rpb == 0) {
@@ -228,6 +230,9 @@ static int plan_mmvq(int t, int nrows, int K, int ncols, int nwarps, int rpb, in
     }
     nwarps = std::min(std::max(nwarps, 1), kMaxWarps);
     rpb = round_rpb(rpb);
+    // gate/up tiles hold rpb/2 rows of each matrix: at least one pair
+    const int min_rpb = mode == kModeGLU ? 2 : 1;
+    if (rpb < min_rpb) rpb = min_rpb;
     int dev;
     if (int s = current_device(&dev)) return s;
     int nsm;
@@ -247,7 +252,7 @@ static int plan_mmvq(int t, int nrows, int K, int ncols, int nwarps, int rpb, in
             p->smem = L.total;
             break;
         }
-        if (rpb > 1) {
+        if (rpb > min_rpb) {
             rpb >>= 1;
         } else if (nwarps > 1) {
             nwarps >>= 1;
@@ -257,7 +262,10 @@ static int plan_mmvq(int t, int nrows, int K, int ncols, int nwarps, int rpb, in
         }
     }
     // Lanes per row: the compile-time variants (16, 32) when the heuristic picks them.
-    const int lbt = host_lanes_per_row(K / qk, rpb);
+    int lbt = host_lanes_per_row(K / qk, rpb);
+    // gate/up pairing: lane group g owns gate row i and up row i, which needs a compile-time
+    // lanes-per-row with rpb/2 a multiple of the 32/lbt row groups (32 lanes always are)
+    if (mode == kModeGLU && !((lbt == 16 || lbt == 32) && (rpb / 2) % (32 / lbt) == 0)) lbt = 32;
     p->fn = kernel_for(t, ncols, rpb, lbt, mode);
     p->mode = mode;
     if (!p->fn) return fail(ANVIL_ERR_UNSUPPORTED, "no kernel for ncols=%d rpb=%d", ncols, rpb);
@@ -266,8 +274,10 @@ static int plan_mmvq(int t, int nrows, int K, int ncols, int nwarps, int rpb, in
     int occ;
     if (int s = prepare_fn(reinterpret_cast<const void *>(p->fn), dev, nwarps * 32, p->smem, &occ))
         return s;
-    // Persistent grid: every warp takes warp-tiles of rpb rows round-robin.
-    const long ntiles = (long(nrows) + rpb - 1) / rpb;
+    // Persistent grid: every warp takes warp-tiles of rpb rows (rpb/2 output rows for the
+    // gate/up epilogue) round-robin.
+    const int trows = mode == kModeGLU ? rpb / 2 : rpb;
+    const long ntiles = (long(nrows) + trows - 1) / trows;
     p->ctas_needed = (ntiles + nwarps - 1) / nwarps;
     p->occ = occ;
     p->nsm = nsm;
@@ -331,6 +341,58 @@ static int launch_mmvq(const Plan &p, const void *W, const void *x, float *y, in
     return launch_mmvq_segs(p, sg, x, sums, K, flags, stream, share);
 }
 
+// Gate/up epilogue: y[r] = silu(W_gate[r] . x) * (W_up[r] . x), one column.  Tiles hold
+// rpb/2 rows of each matrix, both copied whole (rows a multiple of 16 bytes).
+static int launch_glu(const Plan &p, const void *Wg, const void *Wu, const void *xq, float *y,
+                      int nrows, int K, unsigned flags, cudaStream_t stream, int share = 1) {
+    MmvqArgs a = {};
+    a.x = xq;
+    a.sums = nullptr;
+    a.K = K;
+    a.nstages = p.nstages;
+    a.nseg = 1;
+    a.segW[0] = static_cast<const uint8_t *>(Wg);
+    a.segW[1] = static_cast<const uint8_t *>(Wu);
+    a.segY[0] = y;
+    a.segRows[0] = nrows;
+    const int half = p.rpb / 2;
+    const long tiles = (long(nrows) + half - 1) / half;
+    a.segTile[0] = 0;
+    for (int i = 1; i <= kMaxSeg; ++i) a.segTile[i] = int(tiles);
+    Plan q = p;
+    q.ctas_needed = (tiles + p.nwarps - 1) / p.nwarps;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid_for(q, share));
+    cfg.blockDim = dim3(p.nwarps * 32);
+    cfg.dynamicSmemBytes = p.smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    if (flags & ANVIL_FLAG_PDL) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    cudaError_t e = cudaLaunchKernelEx(&cfg, p.fn, a);
+    if (e != cudaSuccess) return cuda_fail(e, "mmvq gate/up launch");
+    return ANVIL_OK;
+}
+
+static int check_glu_args(int t, const void *Wg, const void *Wu, const void *xq, const float *y,
+                          int nrows, int K) {
+    if (!Wg || !Wu || !xq || !y) return fail(ANVIL_ERR_INVALID, "null pointer argument");
+    if (!supported_type(t)) return fail(ANVIL_ERR_UNSUPPORTED, "ggml type %d has no MMVQ kernel", t);
+    if (nrows <= 0 || K <= 0 || K % mmvq_type_qk(t))
+        return fail(ANVIL_ERR_INVALID, "nrows=%d ncols_x=%d", nrows, K);
+    if ((reinterpret_cast<uintptr_t>(Wg) | reinterpret_cast<uintptr_t>(Wu)) & 15)
+        return fail(ANVIL_ERR_ALIGN, "weights must be 16-byte aligned");
+    if ((long(K / mmvq_type_qk(t)) * mmvq_type_bytes(t)) % 16)
+        return fail(ANVIL_ERR_ALIGN, "gate/up rows must be a multiple of 16 bytes (ncols_x=%d)", K);
+    if ((reinterpret_cast<uintptr_t>(xq) | reinterpret_cast<uintptr_t>(y)) & 3)
+        return fail(ANVIL_ERR_ALIGN, "activation and output must be 4-byte aligned");
+    return ANVIL_OK;
+}
+
 static int check_mmvq_ptrs(int t, const void *W, const void *xq, const void *out) {
     if (!W || !xq || !out) return fail(ANVIL_ERR_INVALID, "null pointer argument");
     (void)t;
@@ -384,6 +446,7 @@ struct ChainStep {
     // mmvq
     int type;
     const void *W;
+    const void *W2;  // up matrix of a gate/up step (W is the gate)
     const void *xqin;
     float *y;
     int nrows, ncols_x, ncols_dst, nwarps, rpb;
@@ -555,6 +618,30 @@ int anvil_mmvq_grouped_f32(int ggml_type, int nseg, const void *const *W, const 
         return s;
     if (int s = launch_quantize(x, xq, ncols_x, ncols_dst, flags, st)) return s;
     return launch_mmvq_segs(p, sg, xq, nullptr, ncols_x, ANVIL_FLAG_PDL, st);
+}
+
+int anvil_mmvq_glu(int ggml_type, const void *W_gate, const void *W_up, const void *xq, float *y,
+                   int nrows, int ncols_x, int nwarps, int rows_per_block, unsigned flags,
+                   anvil_stream_t stream) {
+    if (int s = check_glu_args(ggml_type, W_gate, W_up, xq, y, nrows, ncols_x)) return s;
+    Plan p;
+    if (int s = plan_mmvq(ggml_type, nrows, ncols_x, 1, nwarps, rows_per_block, kModeGLU, &p))
+        return s;
+    return launch_glu(p, W_gate, W_up, xq, y, nrows, ncols_x, flags,
+                      reinterpret_cast<cudaStream_t>(stream));
+}
+
+int anvil_mmvq_glu_f32(int ggml_type, const void *W_gate, const void *W_up, const float *x,
+                       void *xq, float *y, int nrows, int ncols_x, int nwarps, int rows_per_block,
+                       unsigned flags, anvil_stream_t stream) {
+    if (!x) return fail(ANVIL_ERR_INVALID, "null pointer argument");
+    if (int s = check_glu_args(ggml_type, W_gate, W_up, xq, y, nrows, ncols_x)) return s;
+    Plan p;
+    if (int s = plan_mmvq(ggml_type, nrows, ncols_x, 1, nwarps, rows_per_block, kModeGLU, &p))
+        return s;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (int s = launch_quantize(x, xq, ncols_x, 1, flags, st)) return s;
+    return launch_glu(p, W_gate, W_up, xq, y, nrows, ncols_x, ANVIL_FLAG_PDL, st);
 }
 
 int anvil_mmvq_block_sums(int ggml_type, const void *W, const void *xq, int32_t *sums,
@@ -742,6 +829,29 @@ int anvil_chain_add_mmvq_grouped_f32(anvil_chain *c, int ggml_type, int nseg, co
     return ANVIL_OK;
 }
 
+int anvil_chain_add_mmvq_glu(anvil_chain *c, int ggml_type, const void *W_gate, const void *W_up,
+                             const void *xq, float *y, int nrows, int ncols_x, int nwarps,
+                             int rows_per_block) {
+    if (!c) return fail(ANVIL_ERR_INVALID, "null chain");
+    if (c->exec) return fail(ANVIL_ERR_INVALID, "chain already instantiated");
+    if (int s = check_glu_args(ggml_type, W_gate, W_up, xq, y, nrows, ncols_x)) return s;
+    ChainStep s = {};
+    s.type = ggml_type;
+    s.W = W_gate;
+    s.W2 = W_up;
+    s.xqin = xq;
+    s.y = y;
+    s.nrows = nrows;
+    s.ncols_x = ncols_x;
+    s.ncols_dst = 1;
+    s.nwarps = nwarps;
+    s.rpb = rows_per_block;
+    if (int st = plan_mmvq(ggml_type, nrows, ncols_x, 1, nwarps, rows_per_block, kModeGLU, &s.plan))
+        return st;
+    c->steps.push_back(s);
+    return ANVIL_OK;
+}
+
 static int run_steps(anvil_chain *c, bool use_pdl, cudaStream_t st) {
     for (size_t i = 0; i < c->steps.size(); ++i) {
         const ChainStep &s = c->steps[i];
@@ -749,6 +859,8 @@ static int run_steps(anvil_chain *c, bool use_pdl, cudaStream_t st) {
         int r;
         if (s.quantize) {
             r = launch_quantize(s.x, s.xq, s.K, s.ncols, flags, st);
+        } else if (s.plan.mode == kModeGLU) {
+            r = launch_glu(s.plan, s.W, s.W2, s.xqin, s.y, s.nrows, s.ncols_x, flags, st, c->share);
         } else if (s.fused && s.plan.mode == kModeF32) {
             r = launch_mmvq_segs(s.plan, s.segs, s.x, nullptr, s.ncols_x, flags, st, c->share);
         } else if (s.fused) {

@@ -45,6 +45,10 @@ constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s bound on any mbarrier w
 constexpr int kModeQ81 = 0;
 constexpr int kModeF32 = 1;
 constexpr int kModeSums = 2;
+// kModeGLU: y = silu(W_gate x) * (W_up x) for one column.  Weights segW[0] (gate) and
+// segW[1] (up); a tile stages RPB/2 rows of each, gate rows first, and the lane that owns
+// gate row i owns up row i, so the epilogue combines them without leaving registers.
+constexpr int kModeGLU = 3;
 
 constexpr int kMaxSeg = 4;  // matrices of one launch (GEMVs sharing the activation)
 
@@ -689,6 +693,20 @@ __global__ void __launch_bounds__(kMaxWarps * 32, NCOLS == 1 ? 2 : 1)
     // interior of the row range goes through the copy engine; a range that does not start
     // or end on 16 bytes leaves at most 15 + 15 bytes for plain loads (below).
     auto issue = [&](int tile, int st) {
+        if constexpr (MODE == kModeGLU) {
+            // rows [r0, r0 + rows) of gate and up, 16-byte aligned rows (checked on the host)
+            constexpr int HALF = RPB / 2;
+            const int r0 = tile * HALF;
+            const int rows = min(HALF, args.segRows[0] - r0);
+            const uint32_t bytes = uint32_t(rows) * uint32_t(row_bytes);
+            uint8_t *dst = ring + st * L.stage;
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            mbar_arrive_expect_tx(&full[st], 2u * bytes);
+            bulk_copy_g2s(dst, args.segW[0] + size_t(r0) * size_t(row_bytes), bytes, &full[st]);
+            bulk_copy_g2s(dst + HALF * row_bytes, args.segW[1] + size_t(r0) * size_t(row_bytes), bytes,
+                          &full[st]);
+            return;
+        }
         const int sg = mmvq_segment(args, tile);
         const int lt = tile - args.segTile[sg];
         const uint8_t *src = args.segW[sg] + size_t(lt) * RPB * size_t(row_bytes);
@@ -768,11 +786,12 @@ __global__ void __launch_bounds__(kMaxWarps * 32, NCOLS == 1 ? 2 : 1)
         const int tile = gwarp + k * wstride;
         const int sg = mmvq_segment(args, tile);
         const int nrows = args.segRows[sg];
-        const int r0 = (tile - args.segTile[sg]) * RPB;
-        const int rows = min(RPB, nrows - r0);
+        constexpr int TROWS = MODE == kModeGLU ? RPB / 2 : RPB;  // output rows per tile
+        const int r0 = (tile - args.segTile[sg]) * TROWS;
+        const int rows = min(TROWS, nrows - r0);
         const uint8_t *src = args.segW[sg] + size_t(r0) * size_t(row_bytes);
-        const uintptr_t s = reinterpret_cast<uintptr_t>(src);
-        const uintptr_t e = s + size_t(rows) * row_bytes;
+        const uintptr_t s = MODE == kModeGLU ? 0 : reinterpret_cast<uintptr_t>(src);
+        const uintptr_t e = MODE == kModeGLU ? 0 : s + size_t(rows) * row_bytes;
         uint8_t *wrow0 = ring + st * L.stage + int(s & 15);
 
         bool have_w = mbar_wait_bounded(&full[st], phase, kWaitLimitNs);
@@ -845,7 +864,21 @@ __global__ void __launch_bounds__(kMaxWarps * 32, NCOLS == 1 ? 2 : 1)
         }
 
         // ---- 4. reduction over the LB lanes sharing a row, then store ------------------
-        if constexpr (MODE != kModeSums) {
+        if constexpr (MODE == kModeGLU) {
+            // slots [0, NS/2) hold gate rows, [NS/2, NS) the up rows of the same lanes
+#pragma unroll
+            for (int sl = 0; sl < NS / 2; ++sl) {
+                float g = acc[sl][0], u = acc[sl + NS / 2][0];
+#pragma unroll
+                for (int o = LBT >> 1; o > 0; o >>= 1) {
+                    g += __shfl_xor_sync(0xffffffffu, g, o);
+                    u += __shfl_xor_sync(0xffffffffu, u, o);
+                }
+                const int i = sl * RG + grp;
+                if (bl == 0 && grp_live && i < rows)
+                    args.segY[0][r0 + i] = g / (1.0f + expf(-g)) * u;
+            }
+        } else if constexpr (MODE != kModeSums) {
 #pragma unroll
             for (int sl = 0; sl < NS; ++sl) {
                 if (LBT > 0 || sl < nslots || sl == 0) {  // uniform across the warp
@@ -902,11 +935,18 @@ int mmvq_kernel_q51_take_status();
 #define ANVIL_MMVQ_TABLE(FN, QT)                                                          \
     namespace anvil {                                                                     \
     template <int NC, int R, int LBT>                                                     \
+    static MmvqKernelFn FN##_glu() {                                                      \
+        if constexpr (NC == 1 && LBT > 0 && R >= 2 && (R / 2) % (32 / (LBT > 0 ? LBT : 32)) == 0) \
+            return mmvq_kernel<QT, NC, R, kModeGLU, LBT>;                                 \
+        return nullptr;                                                                   \
+    }                                                                                     \
+    template <int NC, int R, int LBT>                                                     \
     static MmvqKernelFn FN##_mode(int mode) {                                             \
         switch (mode) {                                                                   \
         case kModeQ81: return mmvq_kernel<QT, NC, R, kModeQ81, LBT>;                      \
         case kModeF32: return mmvq_kernel<QT, NC, R, kModeF32, LBT>;                      \
         case kModeSums: return mmvq_kernel<QT, NC, R, kModeSums, LBT>;                    \
+        case kModeGLU: return FN##_glu<NC, R, LBT>();                                     \
         default: return nullptr;                                                          \
         }                                                                                 \
     }                                                                                     \

@@ -146,6 +146,12 @@ SIGNATURES = {
                                                  c_void_p, c_void_p, c_int, c_int, c_int, c_int]),
     "anvil_chain_add_mmvq_grouped": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p,
                                              c_void_p, c_int, c_int, c_int, c_int]),
+    "anvil_mmvq_glu": (c_int, [c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
+                               c_uint, c_void_p]),
+    "anvil_mmvq_glu_f32": (c_int, [c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,
+                                   c_int, c_int, c_uint, c_void_p]),
+    "anvil_chain_add_mmvq_glu": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
+                                         c_int, c_int, c_int]),
     "anvil_take_device_status": (c_int, []),
     "anvil_mmvq_block_sums": (c_int, [c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
                                       c_int, c_void_p]),

@@ -131,6 +131,13 @@ def get_chain(name: str) -> ChainSpec:
         raise ValueError(f"unknown chain {name!r}; have {sorted(CHAINS)}") from None
 
 
+def is_gate_up(run: list) -> bool:
+    """A run of GEMVs that is one FFN's gate and up projection (same type and shape)."""
+    return (len(run) == 2 and run[0].name.endswith("ffn_gate") and run[1].name.endswith("ffn_up")
+            and (run[0].qt, run[0].nrows, run[0].K) == (run[1].qt, run[1].nrows, run[1].K)
+            and resolve_type(run[0].qt).row_bytes(run[0].K) % 16 == 0)
+
+
 def shard_rows(nrows: int, rank: int, world: int) -> tuple[int, int]:
     """Row range [start, stop) of `rank` when nrows rows are split over `world` ranks.
 
@@ -151,7 +158,9 @@ class DeviceChain:
     programmatic dependent launch); outputs are this rank's slices, (ncols, rows).  With
     grouped=True, consecutive GEMVs of one quant type on the same input (q/k, gate/up) are
     one launch (anvil_mmvq_grouped; with fused=True the launch quantises the fp32 input
-    itself, anvil_mmvq_grouped_f32).
+    itself, anvil_mmvq_grouped_f32).  With glu=True (grouped, one column, separate
+    quantisation) each ffn_gate/ffn_up pair is one gate/up launch (anvil_mmvq_glu) whose
+    silu(gate) * up vector goes to the gate's output; the up output is left unwritten.
     executor="persistent": one persistent kernel per token (pchain.PersistentChain).
     GEMVs sharing an input form a group, and every group waits for the groups before it
     (a decoder layer's data flow).  outputs are full (ncols, nrows) vectors; with world > 1
@@ -161,7 +170,8 @@ class DeviceChain:
     def __init__(self, spec: ChainSpec, ncols: int = 1, seed: int = 0, device="cuda",
                  rank: int = 0, world: int = 1, nwarps: int = 0, rows_per_block: int = 0,
                  configs: dict | None = None, fused: bool = False, coresident: int = 1,
-                 executor: str = "graph", dist=None, ctas_per_sm: int = 0, grouped: bool = False):
+                 executor: str = "graph", dist=None, ctas_per_sm: int = 0, grouped: bool = False,
+                 glu: bool = False):
         import torch
 
         from kernel_anvil.mmvq import Chain, q8_1_bytes
@@ -174,6 +184,7 @@ class DeviceChain:
         self.rank, self.world = rank, world
         self.executor = executor
         self.grouped = grouped and executor == "graph"
+        self.glu = glu and self.grouped and ncols == 1 and not fused
         g = torch.Generator(device=device)
         g.manual_seed(seed + 7919)
         # All fp32 inputs live in one buffer so a step's inputs arrive with one copy.
@@ -216,7 +227,13 @@ class DeviceChain:
                     gm = spec.gemvs[i]
                     nw, rpb = self.launch_cfg[i]
                     rows = [r1 - r0 for r0, r1 in self.rows[i:j]]
-                    if fused:
+                    if self.glu and is_gate_up(spec.gemvs[i:j]):
+                        if gm.input not in quantized:
+                            self.chain.add_quantize(self.x[gm.input], self.xq[gm.input])
+                            quantized.add(gm.input)
+                        self.chain.add_mmvq_glu(self.weights[i], self.weights[i + 1], gm.qt,
+                                                self.xq[gm.input], self.outputs[i])
+                    elif fused:
                         self.chain.add_mmvq_grouped_f32(
                             self.weights[i:j], gm.qt, self.x[gm.input], self.xq[gm.input],
                             self.outputs[i:j], rows, K=gm.K, ncols=ncols, nwarps=nw,

@@ -164,6 +164,61 @@ def mmvq_grouped_f32(Ws: list, qt, x: torch.Tensor, nwarps: int = 0, rows_per_bl
     return outs
 
 
+def _glu_shapes(W_gate: torch.Tensor, W_up: torch.Tensor, info: QuantTypeInfo, K: int) -> int:
+    _require_cuda("W_gate", W_gate, torch.uint8)
+    _require_cuda("W_up", W_up, torch.uint8)
+    nrows = _shape_args(W_gate, info, None, K)[0]
+    if _shape_args(W_up, info, None, K)[0] != nrows:
+        raise AnvilError(_native.ANVIL_ERR_INVALID, "gate and up need the same number of rows")
+    return nrows
+
+
+def mmvq_glu(W_gate: torch.Tensor, W_up: torch.Tensor, qt, xq: torch.Tensor, nwarps: int = 0,
+             rows_per_block: int = 0, out: torch.Tensor | None = None, pdl: bool = False) -> torch.Tensor:
+    """silu(W_gate @ dequant(xq)) * (W_up @ dequant(xq)) for one Q8_1 column, in one launch.
+
+    Each product is what mmvq computes for its matrix; neither is written out.  Rows of
+    W_gate / W_up must be a multiple of 16 bytes."""
+    info = resolve_type(qt)
+    _require_cuda("xq", xq, torch.uint8)
+    K = W_gate.shape[1] // info.block_size * info.qk
+    nrows = _glu_shapes(W_gate, W_up, info, K)
+    if xq.numel() < q8_1_bytes(K):
+        raise AnvilError(_native.ANVIL_ERR_INVALID, "xq is too small")
+    if out is None:
+        out = torch.empty((1, nrows), dtype=torch.float32, device=xq.device)
+    _require_cuda("out", out, torch.float32)
+    if out.numel() < nrows:
+        raise AnvilError(_native.ANVIL_ERR_INVALID, "out is too small")
+    check(_native.lib().anvil_mmvq_glu(info.ggml_type, W_gate.data_ptr(), W_up.data_ptr(), xq.data_ptr(),
+                                       out.data_ptr(), nrows, K, nwarps, rows_per_block,
+                                       ANVIL_FLAG_PDL if pdl else 0, _stream_ptr()))
+    return out
+
+
+def mmvq_glu_f32(W_gate: torch.Tensor, W_up: torch.Tensor, qt, x: torch.Tensor, nwarps: int = 0,
+                 rows_per_block: int = 0, xq_scratch: torch.Tensor | None = None,
+                 out: torch.Tensor | None = None, pdl: bool = False) -> torch.Tensor:
+    """mmvq_glu from fp32 x (K values): quantise to Q8_1, then the gate/up launch."""
+    info = resolve_type(qt)
+    _require_cuda("x", x, torch.float32)
+    K = x.numel()
+    nrows = _glu_shapes(W_gate, W_up, info, K)
+    if xq_scratch is None:
+        xq_scratch = torch.empty(q8_1_bytes(K), dtype=torch.uint8, device=x.device)
+    _require_cuda("xq_scratch", xq_scratch, torch.uint8)
+    if out is None:
+        out = torch.empty((1, nrows), dtype=torch.float32, device=x.device)
+    _require_cuda("out", out, torch.float32)
+    if xq_scratch.numel() < q8_1_bytes(K) or out.numel() < nrows:
+        raise AnvilError(_native.ANVIL_ERR_INVALID, "xq_scratch or out is too small")
+    check(_native.lib().anvil_mmvq_glu_f32(info.ggml_type, W_gate.data_ptr(), W_up.data_ptr(),
+                                           x.contiguous().data_ptr(), xq_scratch.data_ptr(),
+                                           out.data_ptr(), nrows, K, nwarps, rows_per_block,
+                                           ANVIL_FLAG_PDL if pdl else 0, _stream_ptr()))
+    return out
+
+
 def block_sums(W: torch.Tensor, qt, xq: torch.Tensor, nrows: int | None = None, K: int | None = None,
                ncols: int | None = None, nwarps: int = 0, rows_per_block: int = 0) -> torch.Tensor:
     """The production kernel's exact int32 block dots, shape (ncols, nrows, nsub).
@@ -332,6 +387,27 @@ class Chain:
             self.n_mmvq += 1
             self.weight_bytes += n * info.row_bytes(K)
             self.algorithmic_bytes += gemv_bytes(info, n, K, ncols)
+        self.n_launches += 1
+
+    def add_mmvq_glu(self, W_gate: torch.Tensor, W_up: torch.Tensor, qt, xq: torch.Tensor,
+                     y: torch.Tensor, nwarps: int = 0, rows_per_block: int = 0) -> None:
+        """One launch: y = silu(W_gate @ dequant(xq)) * (W_up @ dequant(xq)), one column."""
+        info = resolve_type(qt)
+        _require_cuda("xq", xq, torch.uint8)
+        _require_cuda("y", y, torch.float32)
+        K = W_gate.shape[1] // info.block_size * info.qk
+        nrows = _glu_shapes(W_gate, W_up, info, K)
+        if xq.numel() < q8_1_bytes(K) or y.numel() < nrows:
+            raise AnvilError(_native.ANVIL_ERR_INVALID, "xq or y is too small")
+        check(self._lib.anvil_chain_add_mmvq_glu(self._h, info.ggml_type, W_gate.data_ptr(),
+                                                 W_up.data_ptr(), xq.data_ptr(), y.data_ptr(), nrows,
+                                                 K, nwarps, rows_per_block))
+        self._keep += [W_gate, W_up, xq, y]
+        from kernel_anvil.quants import gemv_bytes
+        self.n_mmvq += 2
+        self.weight_bytes += 2 * nrows * info.row_bytes(K)
+        # both matrices and one read of xq; one output row of 4 bytes per gate/up pair
+        self.algorithmic_bytes += 2 * gemv_bytes(info, nrows, K, 1) - nrows * 4 - q8_1_bytes(K)
         self.n_launches += 1
 
     def set_coresident(self, kernels_per_sm: int) -> None:

@@ -103,6 +103,16 @@ def mmvq(qt, W: np.ndarray, xq: np.ndarray, nrows: int, K: int, ncols: int = 1) 
     return out
 
 
+def mmvq_glu(qt, W_gate: np.ndarray, W_up: np.ndarray, xq: np.ndarray, nrows: int, K: int) -> np.ndarray:
+    """silu(y_gate) * y_up (1, nrows) float64: the SwiGLU product that follows the gate and up
+    GEMVs of a llama.cpp decode step (ggml GLU, silu(g) = g / (1 + exp(-g)): the "GLU | silu +
+    elementwise mul" op of docs/vulkan-vs-rocm-analysis.md:135, fused after the gate GEMV as
+    "Q4_K fused (gate+SiLU)" in docs/decode-pipeline-breakdown.md:40)."""
+    g = mmvq(qt, W_gate, xq, nrows, K)
+    u = mmvq(qt, W_up, xq, nrows, K)
+    return g / (1.0 + np.exp(-g)) * u
+
+
 def float_to_half_bits(v: float) -> int:
     return int(lib().oracle_float_to_half(v))
 

@@ -95,3 +95,17 @@ def test_chain_rows_split_evenly_over_8(name):
     for g in get_chain(name).gemvs:
         for world in (2, 4, 8):
             assert g.nrows % world == 0, (g.name, world)
+
+
+@pytest.mark.parametrize("name,pairs", [("qwen3_8b", 36), ("llama3_70b", 80), ("qwen3_0_6b", 28),
+                                        ("qwen35_27b", 0)])
+def test_gate_up_pairs_found(name, pairs):
+    """Every decoder layer's ffn_gate/ffn_up pair is recognised for the gate/up launch
+    (16-byte rows: Q4_K always, Q8_0 at K = 1024), and nothing else is."""
+    from kernel_anvil.chains import is_gate_up
+
+    g = get_chain(name).gemvs
+    found = [i for i in range(len(g) - 1) if is_gate_up(g[i:i + 2])]
+    assert len(found) == pairs
+    assert all(g[i].name.endswith("ffn_gate") for i in found)
+    assert not is_gate_up(g[:2]) and not is_gate_up(g[:3])
