@@ -2,6 +2,11 @@
 // the sm_100a kernels of libanvil.so.
 //
 // Block layouts are the GGUF/ggml ones (byte offsets within one block):
+//   Q2_K ( 84 B / 256 weights): scales[16] @0 (low nibble scale, high nibble min of each
+//                                16 weights), qs[64] @16 (2-bit), d f16 @80, dmin f16 @82
+//   Q3_K (110 B / 256 weights): hmask[32] @0, qs[64] @32 (2-bit), scales[12] @96 (16 6-bit
+//                                scales, minus 32), d f16 @108; q = low 2 bits - 4 unless
+//                                the weight's hmask bit is set
 //   Q4_K (144 B / 256 weights): d f16 @0, dmin f16 @2, scales[12] @4, qs[128] @16
 //   Q5_K (176 B / 256 weights): d @0, dmin @2, scales[12] @4, qh[32] @16, qs[128] @48
 //   Q6_K (210 B / 256 weights): ql[128] @0, qh[64] @128, scales int8[16] @192, d f16 @208
@@ -12,8 +17,8 @@
 //   Q5_1 ( 24 B /  32 weights): d f16 @0, m f16 @2, qh u32 @4, qs[16] @8 (x = d q + m)
 //   Q8_0 ( 34 B /  32 weights): d f16 @0, qs int8[32] @2
 //   Q8_1 ( 36 B /  32 values ): d f16 @0, s f16 @2, qs int8[32] @4   (GPU layout)
-// (gguf-py quants.py:396-401, 504-523, 527-549, 554-572; kernel_anvil/hip_codegen.py:101-102,
-//  385-396.)
+// (gguf-py quants.py:396-401, 504-523, 527-549, 554-572, Q2_K / Q3_K dequantize_blocks;
+//  kernel_anvil/hip_codegen.py:84-85, 101-102, 385-396.)
 #pragma once
 
 #include <cstdint>
@@ -27,6 +32,8 @@ constexpr int kTypeQ5_0 = 6;
 constexpr int kTypeQ5_1 = 7;
 constexpr int kTypeQ8_0 = 8;
 constexpr int kTypeQ8_1 = 9;
+constexpr int kTypeQ2_K = 10;
+constexpr int kTypeQ3_K = 11;
 constexpr int kTypeQ4_K = 12;
 constexpr int kTypeQ5_K = 13;
 constexpr int kTypeQ6_K = 14;
@@ -47,6 +54,12 @@ template <> struct QTraits<kTypeQ5_K> {
 };
 template <> struct QTraits<kTypeQ6_K> {
     static constexpr int qk = 256, bytes = 210, units = 4, sub = 16;
+};
+template <> struct QTraits<kTypeQ2_K> {
+    static constexpr int qk = 256, bytes = 84, units = 4, sub = 16;
+};
+template <> struct QTraits<kTypeQ3_K> {
+    static constexpr int qk = 256, bytes = 110, units = 4, sub = 16;
 };
 template <> struct QTraits<kTypeQ4_0> {
     static constexpr int qk = 32, bytes = 18, units = 1, sub = 32;

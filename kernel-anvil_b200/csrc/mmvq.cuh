@@ -96,6 +96,8 @@ __host__ __device__ inline int mmvq_type_bytes(int qt) {
     case kTypeQ4_1: return 20;
     case kTypeQ5_0: return 22;
     case kTypeQ5_1: return 24;
+    case kTypeQ2_K: return 84;
+    case kTypeQ3_K: return 110;
     case kTypeQ4_K: return 144;
     case kTypeQ5_K: return 176;
     case kTypeQ6_K: return 210;
@@ -103,7 +105,10 @@ __host__ __device__ inline int mmvq_type_bytes(int qt) {
     }
 }
 __host__ __device__ inline int mmvq_type_qk(int qt) {
-    return qt == kTypeQ4_K || qt == kTypeQ5_K || qt == kTypeQ6_K ? 256 : 32;
+    return qt == kTypeQ4_K || qt == kTypeQ5_K || qt == kTypeQ6_K || qt == kTypeQ2_K ||
+                   qt == kTypeQ3_K
+               ? 256
+               : 32;
 }
 
 // The 32-weight "basic" types (one Q8_1 block per weight block, one unit per block).
@@ -111,6 +116,9 @@ template <int QT>
 constexpr bool kBasic = QT == kTypeQ4_0 || QT == kTypeQ4_1 || QT == kTypeQ5_0 || QT == kTypeQ5_1;
 template <int QT>
 constexpr bool kBlock32 = QT == kTypeQ8_0 || kBasic<QT>;
+// The K-quants with 16-weight scale groups (two per Q8_1 block).
+template <int QT>
+constexpr bool kSub16 = QT == kTypeQ6_K || QT == kTypeQ2_K || QT == kTypeQ3_K;
 
 // Bytes of one column's swizzled activation quants: 2 chunks of 16 B per Q8_1 block,
 // padded to whole 16-chunk groups so the XOR swizzle never leaves the column.
@@ -229,7 +237,7 @@ __device__ __forceinline__ void load_act(const ActView &v, int kb, ActBlk &a) {
     a.slo = a.shi = 0;
     if constexpr (QT == kTypeQ4_K || QT == kTypeQ5_K || QT == kTypeQ4_1 || QT == kTypeQ5_1)
         a.ds = v.ads[kb];
-    if constexpr (QT == kTypeQ6_K || QT == kTypeQ4_0 || QT == kTypeQ5_0) {
+    if constexpr (kSub16<QT> || QT == kTypeQ4_0 || QT == kTypeQ5_0) {
         const int2 s = v.as[kb];
         a.slo = s.x;
         a.shi = s.y;
@@ -241,7 +249,8 @@ __device__ __forceinline__ void load_act(const ActView &v, int kb, ActBlk &a) {
 // A lane handling (row, block) first reads the block header (BlkHdr), then for each unit U
 // (compile time) decodes the unit's weight bytes and dots them with the unit's activation
 // blocks.  Units: Q4_K/Q5_K U = sub-block pair (2U, 2U+1); Q6_K U = (h, t) = (U>>1, U&1),
-// sub-blocks 4h+t and 4h+2+t; Q8_0 one unit, the block itself.
+// sub-blocks 4h+t and 4h+2+t; Q2_K/Q3_K U = weights [64U, 64U+64) (Q8_1 blocks 2U, 2U+1 of
+// the super-block, scale groups 4U..4U+3); Q8_0 one unit, the block itself.
 
 struct BlkHdr {
     float d, dmin;
@@ -284,6 +293,15 @@ __device__ __forceinline__ BlkHdr load_hdr(const uint8_t *blk) {
         h.s2 = v.w;
     } else if constexpr (QT == kTypeQ6_K) {
         h.d = h2f(lds16(blk + 208));
+    } else if constexpr (QT == kTypeQ2_K) {
+        h.d = h2f(lds16(blk + 80));
+        h.dmin = h2f(lds16(blk + 82));
+    } else if constexpr (QT == kTypeQ3_K) {
+        // the 12 scale bytes as three words (2-byte aligned block)
+        h.d = h2f(lds16(blk + 108));
+        h.s0 = lds16(blk + 96) | (lds16(blk + 98) << 16);
+        h.s1 = lds16(blk + 100) | (lds16(blk + 102) << 16);
+        h.s2 = lds16(blk + 104) | (lds16(blk + 106) << 16);
     } else if constexpr (QT == kTypeQ4_1 || QT == kTypeQ5_1) {
         h.d = h2f(lds16(blk));
         h.dmin = h2f(lds16(blk + 2));  // m, the block's added minimum
@@ -354,6 +372,27 @@ __device__ __forceinline__ void load_unit(const uint8_t *blk, WBytes &w) {
             w.q0[k] = (ql[k] & 0x0F0F0F0Fu) | (((qh[k] >> (2 * t)) & 0x03030303u) << 4);
             w.q1[k] = ((ql[k] >> 4) & 0x0F0F0F0Fu) | ((qh[k] >> (2 * t)) & 0x30303030u);
         }
+    } else if constexpr (QT == kTypeQ2_K || QT == kTypeQ3_K) {
+        // weight 64U + 32i + l (i = 0, 1: Q8_1 block kb0, kb1) is bits 2(2(U&1) + i) of qs
+        // byte 32(U>>1) + l; Q3_K adds bit 2U + i of hmask[l] as bit 2 (q + 4 when set)
+        constexpr int qs_off = QT == kTypeQ2_K ? 16 : 32;
+        constexpr int s0 = 4 * (U & 1);
+        uint32_t v[8];
+        lds32_a2(blk + qs_off + 32 * (U >> 1), v);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            w.q0[k] = (v[k] >> s0) & 0x03030303u;
+            w.q1[k] = (v[k] >> (s0 + 2)) & 0x03030303u;
+        }
+        if constexpr (QT == kTypeQ3_K) {
+            uint32_t hm[8];
+            lds32_a2(blk, hm);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                w.q0[k] |= ((hm[k] >> (2 * U)) & 0x01010101u) << 2;
+                w.q1[k] |= ((hm[k] >> (2 * U + 1)) & 0x01010101u) << 2;
+            }
+        }
     } else if constexpr (kBasic<QT>) {
         // quants in Q8_1 element order: words 0..3 the low nibbles of qs[0..15] (weights
         // 0..15), words 4..7 the high nibbles (weights 16..31); the 5-bit types add bit e of
@@ -381,7 +420,7 @@ __device__ __forceinline__ void load_unit(const uint8_t *blk, WBytes &w) {
 }
 
 // Float contribution of one unit against one column; exact int32 block dots to `isum`
-// (K4/K5/Q8_0: isum[0..1], one per 32; Q6_K: isum[0..3], one per 16).
+// (K4/K5/Q8_0: isum[0..1], one per 32; Q2_K, Q3_K, Q6_K: isum[0..3], one per 16).
 template <int QT, int U>
 __device__ __forceinline__ float dot_unit(const uint8_t *blk, const BlkHdr &h, const WBytes &w,
                                           const ActBlk &a0, const ActBlk &a1, int (&isum)[4]) {
@@ -431,6 +470,44 @@ __device__ __forceinline__ float dot_unit(const uint8_t *blk, const BlkHdr &h, c
         const int s00 = int(int8_t(sc0 & 0xFF)), s01 = int(int8_t(sc0 >> 8));
         const int s10 = int(int8_t(sc1 & 0xFF)), s11 = int(int8_t(sc1 >> 8));
         return h.d * (a0.d * float(p00 * s00 + p01 * s01) + a1.d * float(p10 * s10 + p11 * s11));
+    } else if constexpr (QT == kTypeQ2_K || QT == kTypeQ3_K) {
+        int p00 = 0, p01 = 0, p10 = 0, p11 = 0;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            p00 = __dp4a(int(w.q0[k]), int(a0.q[k]), p00);
+            p01 = __dp4a(int(w.q0[k + 4]), int(a0.q[k + 4]), p01);
+            p10 = __dp4a(int(w.q1[k]), int(a1.q[k]), p10);
+            p11 = __dp4a(int(w.q1[k + 4]), int(a1.q[k + 4]), p11);
+        }
+        if constexpr (QT == kTypeQ3_K) {
+            // q - 4 through the activation sums
+            p00 -= 4 * a0.slo;
+            p01 -= 4 * a0.shi;
+            p10 -= 4 * a1.slo;
+            p11 -= 4 * a1.shi;
+        }
+        isum[0] = p00;
+        isum[1] = p01;
+        isum[2] = p10;
+        isum[3] = p11;
+        if constexpr (QT == kTypeQ2_K) {
+            // scale groups 4U..4U+3: low nibble scale, high nibble min
+            // (vec_dot_q2_K_q8_1: d * sum sc * d8 * sumi - dmin * sum m * d8 * sumq)
+            const uint32_t sw = lds16(blk + 4 * U) | (lds16(blk + 4 * U + 2) << 16);
+            const int sc0 = sw & 15, sc1 = (sw >> 8) & 15, sc2 = (sw >> 16) & 15, sc3 = (sw >> 24) & 15;
+            const int m0 = (sw >> 4) & 15, m1 = (sw >> 12) & 15, m2 = (sw >> 20) & 15, m3 = sw >> 28;
+            const float fd = a0.d * float(p00 * sc0 + p01 * sc1) + a1.d * float(p10 * sc2 + p11 * sc3);
+            const float fm = a0.d * float(m0 * a0.slo + m1 * a0.shi) + a1.d * float(m2 * a1.slo + m3 * a1.shi);
+            return h.d * fd - h.dmin * fm;
+        } else {
+            // six-bit scales of groups 4U..4U+3: low nibbles from scales[4(U&1) ..] (high
+            // nibbles for U >= 2), bits 4-5 from bits 2U of scales[8 .. 11]; minus 32
+            const uint32_t lo = ((U & 1 ? h.s1 : h.s0) >> (U >= 2 ? 4 : 0)) & 0x0F0F0F0Fu;
+            const uint32_t sc = lo | (((h.s2 >> (2 * U)) & 0x03030303u) << 4);
+            const int sc0 = int(sc & 0xFF) - 32, sc1 = int((sc >> 8) & 0xFF) - 32;
+            const int sc2 = int((sc >> 16) & 0xFF) - 32, sc3 = int(sc >> 24) - 32;
+            return h.d * (a0.d * float(p00 * sc0 + p01 * sc1) + a1.d * float(p10 * sc2 + p11 * sc3));
+        }
     } else if constexpr (kBasic<QT>) {
         // Q4_0 / Q5_0: d * d8 * sum((q - 8 | q - 16) q8), the offset through the block's
         // sum of q8; Q4_1 / Q5_1: d * d8 * sum(q q8) + m * d8 * sum(q8).
@@ -453,7 +530,7 @@ __device__ __forceinline__ float dot_unit(const uint8_t *blk, const BlkHdr &h, c
 
 template <int QT>
 __device__ __forceinline__ void store_sums(int32_t *srow, int kb0, int kb1, const int (&isum)[4]) {
-    if constexpr (QT == kTypeQ6_K) {
+    if constexpr (kSub16<QT>) {
         srow[2 * kb0] = isum[0];
         srow[2 * kb0 + 1] = isum[1];
         srow[2 * kb1] = isum[2];
@@ -529,7 +606,7 @@ __device__ __forceinline__ void unit_step(const TileCtx &t, int b, const BlkHdr 
             if constexpr (MODE == kModeSums) {
                 const int i = sl * t.RG + t.grp;
                 if (i < t.rows) {
-                    const int nsub = QT == kTypeQ6_K ? t.K / 16 : t.K / 32;
+                    const int nsub = kSub16<QT> ? t.K / 16 : t.K / 32;
                     store_sums<QT>(t.sums + (size_t(c) * t.nrows + t.r0 + i) * nsub, kb0, kb1, isum);
                 }
             }
@@ -917,6 +994,8 @@ MmvqKernelFn mmvq_kernel_q40(int ncols, int rpb, int lbt, int mode);
 MmvqKernelFn mmvq_kernel_q41(int ncols, int rpb, int lbt, int mode);
 MmvqKernelFn mmvq_kernel_q50(int ncols, int rpb, int lbt, int mode);
 MmvqKernelFn mmvq_kernel_q51(int ncols, int rpb, int lbt, int mode);
+MmvqKernelFn mmvq_kernel_q2k(int ncols, int rpb, int lbt, int mode);
+MmvqKernelFn mmvq_kernel_q3k(int ncols, int rpb, int lbt, int mode);
 // Reads and clears the device status word of that type's translation unit (current device).
 int mmvq_kernel_q4k_take_status();
 int mmvq_kernel_q5k_take_status();
@@ -926,6 +1005,8 @@ int mmvq_kernel_q40_take_status();
 int mmvq_kernel_q41_take_status();
 int mmvq_kernel_q50_take_status();
 int mmvq_kernel_q51_take_status();
+int mmvq_kernel_q2k_take_status();
+int mmvq_kernel_q3k_take_status();
 
 }  // namespace anvil
 

@@ -231,7 +231,7 @@ def block_sums(W: torch.Tensor, qt, xq: torch.Tensor, nrows: int | None = None, 
     nrows, K = _shape_args(W, info, nrows, K)
     if ncols is None:
         ncols = xq.numel() // q8_1_bytes(K)
-    nsub = K // 16 if info.name == "Q6_K" else K // 32
+    nsub = K // 16 if info.name in ("Q6_K", "Q2_K", "Q3_K") else K // 32
     out = torch.empty((ncols, nrows, nsub), dtype=torch.int32, device=W.device)
     check(_native.lib().anvil_mmvq_block_sums(info.ggml_type, W.data_ptr(), xq.data_ptr(),
                                               out.data_ptr(), nrows, K, ncols, nwarps,

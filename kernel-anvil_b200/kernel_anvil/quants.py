@@ -56,6 +56,8 @@ QUANT_TYPES: dict[str, QuantTypeInfo] = {
     "Q5_0": QuantTypeInfo("Q5_0", 6, 32, 4, 2, 22),
     "Q5_1": QuantTypeInfo("Q5_1", 7, 32, 4, 2, 24),
     "Q8_0": QuantTypeInfo("Q8_0", 8, 32, 8, 2, 34),
+    "Q2_K": QuantTypeInfo("Q2_K", 10, 256, 16, 1, 84),
+    "Q3_K": QuantTypeInfo("Q3_K", 11, 256, 16, 1, 110),
     "Q4_K": QuantTypeInfo("Q4_K", 12, 256, 32, 2, 144),
     "Q5_K": QuantTypeInfo("Q5_K", 13, 256, 32, 2, 176),
     "Q6_K": QuantTypeInfo("Q6_K", 14, 256, 32, 1, 210),
@@ -117,6 +119,14 @@ def make_weights(qt, nrows: int, K: int, seed: int = 0) -> np.ndarray:
     elif info.name == "Q8_0":
         blocks[:, 0:2] = _fp16_abs_normal(rng, nb, 1e-2)
         blocks[:, 2:34] = rng.integers(-127, 128, size=(nb, 32), dtype=np.int8).view(np.uint8)
+    elif info.name == "Q2_K":
+        # scales/mins nibbles, quants uniform; d, dmin from |N(0,1)| * 1e-2
+        blocks[:, 0:80] = rng.integers(0, 256, size=(nb, 80), dtype=np.uint8)
+        blocks[:, 80:82] = _fp16_abs_normal(rng, nb, 1e-2)
+        blocks[:, 82:84] = _fp16_abs_normal(rng, nb, 1e-2)
+    elif info.name == "Q3_K":
+        blocks[:, 0:108] = rng.integers(0, 256, size=(nb, 108), dtype=np.uint8)
+        blocks[:, 108:110] = _fp16_abs_normal(rng, nb, 1e-2)
     elif info.name in ("Q4_0", "Q4_1", "Q5_0", "Q5_1"):
         # d from |N(0,1)| * 1e-2; the _1 types' m (the block minimum) from -|N(0,1)| * 1e-1;
         # high bits (qh) and nibbles uniform
@@ -163,6 +173,11 @@ def make_weights_device(qt, nrows: int, K: int, seed: int = 0, device="cuda"):
         blocks[:, 0:2] = fp16_abs_normal(1e-2)
         q = torch.randint(-127, 128, (nb, 32), dtype=torch.int8, device=device, generator=g)
         blocks[:, 2:34] = q.view(torch.uint8)
+    elif info.name == "Q2_K":
+        blocks[:, 80:82] = fp16_abs_normal(1e-2)
+        blocks[:, 82:84] = fp16_abs_normal(1e-2)
+    elif info.name == "Q3_K":
+        blocks[:, 108:110] = fp16_abs_normal(1e-2)
     elif info.name in ("Q4_0", "Q4_1", "Q5_0", "Q5_1"):
         blocks[:, 0:2] = fp16_abs_normal(1e-2)
         if info.name.endswith("_1"):

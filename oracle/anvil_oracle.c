@@ -4,10 +4,11 @@
  * cpu_baseline leg of bench.py.  Nothing in the product links or calls it.
  *
  * What it restates, and from where:
- *   - GGUF block layouts and per-weight dequantisation of Q4_0, Q4_1, Q5_0, Q5_1, Q4_K,
- *     Q5_K, Q6_K and Q8_0: gguf-py (the reference's declared dependency, kernel-anvil
- *     pyproject.toml:19, gguf 0.19.0) gguf/quants.py Q4_0..Q5_1 dequantize_blocks,
- *     378-401 (Q8_0), 474-523 (Q4_K incl. get_scale_min), 525-549 (Q5_K), 552-572 (Q6_K).
+ *   - GGUF block layouts and per-weight dequantisation of Q4_0, Q4_1, Q5_0, Q5_1, Q2_K,
+ *     Q3_K, Q4_K, Q5_K, Q6_K and Q8_0: gguf-py (the reference's declared dependency,
+ *     kernel-anvil pyproject.toml:19, gguf 0.19.0) gguf/quants.py Q4_0..Q5_1 and Q2_K, Q3_K
+ *     dequantize_blocks, 378-401 (Q8_0), 474-523 (Q4_K incl. get_scale_min), 525-549
+ *     (Q5_K), 552-572 (Q6_K).
  *     Pinned in tests against gguf.quants.dequantize (fixtures and live).
  *   - Q8_1 activation quantisation: llama.cpp's CUDA quantize_q8_1 semantics (the
  *     reference's runtime path: kernel_anvil/hip_codegen.py:392-396 layout, 101-102 size;
@@ -34,7 +35,8 @@
 #include <omp.h>
 #endif
 
-enum { T_Q4_0 = 2, T_Q4_1 = 3, T_Q5_0 = 6, T_Q5_1 = 7, T_Q8_0 = 8, T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14 };
+enum { T_Q4_0 = 2, T_Q4_1 = 3, T_Q5_0 = 6, T_Q5_1 = 7, T_Q8_0 = 8, T_Q2_K = 10, T_Q3_K = 11,
+       T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14 };
 
 /* ---- IEEE binary16 conversions (written from the format definition) ---------- */
 
@@ -172,8 +174,32 @@ static inline int q6k_quant(const uint8_t *blk, int j, int e) {
     return (lo | (hi << 4)) - 32;
 }
 
+/* Q2_K (84 B: scales[16] @0, qs[64] @16, d @80, dmin @82) and Q3_K (110 B: hmask[32] @0,
+ * qs[64] @32, scales[12] @96, d @108), gguf-py Q2_K / Q3_K dequantize_blocks.  Weight w of
+ * the 256: its 2-bit quant is bits 2s of qs byte 32h + l with h = w / 128, s = (w % 128) / 32,
+ * l = w % 32; Q3_K subtracts 4 unless bit w / 32 of hmask[l] is set.  Sub-block j = w / 16
+ * has Q2_K scale scales[j] & 15 and min scales[j] >> 4, and Q3_K 6-bit scale (low nibble of
+ * scales[j] for j < 8, high nibble of scales[j - 8] above; bits 4-5 from bits 2(j / 4) of
+ * scales[8 + j % 4]) minus 32. */
+static inline int q23_low(const uint8_t *qs, int w) {
+    return (qs[32 * (w >> 7) + (w & 31)] >> (2 * ((w >> 5) & 3))) & 3;
+}
+static inline int q2k_quant(const uint8_t *blk, int w) { return q23_low(blk + 16, w); }
+static inline int q3k_quant(const uint8_t *blk, int w) {
+    const int hbit = (blk[w & 31] >> (w >> 5)) & 1;
+    return q23_low(blk + 32, w) - (hbit ? 0 : 4);
+}
+static inline int q3k_scale(const uint8_t *blk, int j) {
+    const uint8_t *s = blk + 96;
+    const int lo = j < 8 ? (s[j] & 15) : (s[j - 8] >> 4);
+    const int hi = (s[8 + (j & 3)] >> (2 * (j >> 2))) & 3;
+    return (lo | (hi << 4)) - 32;
+}
+
 static int type_bytes(int t) {
     switch (t) {
+    case T_Q2_K: return 84;
+    case T_Q3_K: return 110;
     case T_Q4_0: return 18;
     case T_Q4_1: return 20;
     case T_Q5_0: return 22;
@@ -228,6 +254,20 @@ int oracle_dequant(int type, const uint8_t *W, float *out, int64_t nrows, int64_
             } else {
                 for (int e = 0; e < 32; ++e) o[e] = d * (float)basic_quant(type, blk, e);
             }
+        } else if (type == T_Q2_K) {
+            const float d = oracle_half_to_float(rd16(blk + 80));
+            const float dmin = oracle_half_to_float(rd16(blk + 82));
+            for (int w = 0; w < 256; ++w) {
+                const uint8_t sc = blk[w >> 4];
+                const float dl = d * (float)(sc & 15), ml = dmin * (float)(sc >> 4);
+                o[w] = dl * (float)q2k_quant(blk, w) - ml;
+            }
+        } else if (type == T_Q3_K) {
+            const float d = oracle_half_to_float(rd16(blk + 108));
+            for (int w = 0; w < 256; ++w) {
+                const float dl = d * (float)q3k_scale(blk, w >> 4);
+                o[w] = dl * (float)q3k_quant(blk, w);
+            }
         } else if (type == T_Q6_K) {
             const float d = oracle_half_to_float(rd16(blk + 208));
             for (int j = 0; j < 8; ++j)
@@ -254,15 +294,16 @@ int oracle_dequant(int type, const uint8_t *W, float *out, int64_t nrows, int64_
 
 /* ---- integer block sums and y -------------------------------------------------- */
 
-/* Exact integer dots.  sums[(c*nrows + r)*nsub + s] with nsub = K/16 for Q6_K (one per
- * int8 scale group) and K/32 otherwise (one per Q8_1 block).  Q4_K/Q5_K use the unsigned
- * quant (the min term is separate), Q6_K uses q - 32, Q8_0 the int8 quant. */
+/* Exact integer dots.  sums[(c*nrows + r)*nsub + s] with nsub = K/16 for Q2_K, Q3_K and
+ * Q6_K (one per 16-weight scale group) and K/32 otherwise (one per Q8_1 block).  Q2_K, Q4_K
+ * and Q5_K use the unsigned quant (the min term is separate), Q3_K q with its offset, Q6_K
+ * q - 32, Q8_0 the int8 quant. */
 int oracle_block_sums(int type, const uint8_t *W, const uint8_t *xq, int32_t *sums,
                       int64_t nrows, int64_t K, int64_t ncols) {
     const int bytes = type_bytes(type), qk = type_qk(type);
     if (!bytes || K % qk) return -1;
     const int64_t nblk = K / qk, nkb = K / 32;
-    const int64_t nsub = type == T_Q6_K ? K / 16 : K / 32;
+    const int64_t nsub = (type == T_Q6_K || type == T_Q2_K || type == T_Q3_K) ? K / 16 : K / 32;
 #pragma omp parallel for collapse(2) schedule(static)
     for (int64_t c = 0; c < ncols; ++c)
         for (int64_t r = 0; r < nrows; ++r) {
@@ -283,6 +324,18 @@ int oracle_block_sums(int type, const uint8_t *W, const uint8_t *xq, int32_t *su
                     int32_t s = 0;
                     for (int e = 0; e < 32; ++e) s += basic_quant(type, blk, e) * a[e];
                     out[b] = s;
+                    continue;
+                }
+                if (type == T_Q2_K || type == T_Q3_K) {
+                    for (int j = 0; j < 16; ++j) {
+                        const int8_t *a = (const int8_t *)(xc + (8 * b + (j >> 1)) * 36 + 4) + 16 * (j & 1);
+                        int32_t s = 0;
+                        for (int e = 0; e < 16; ++e) {
+                            const int w = 16 * j + e;
+                            s += (type == T_Q2_K ? q2k_quant(blk, w) : q3k_quant(blk, w)) * a[e];
+                        }
+                        out[16 * b + j] = s;
+                    }
                     continue;
                 }
                 for (int j = 0; j < 8; ++j) {
@@ -341,6 +394,29 @@ int oracle_mmvq(int type, const uint8_t *W, const uint8_t *xq, double *y, int64_
                     acc += (double)oracle_half_to_float(rd16(blk)) * d8 * (double)s;
                     if (type == T_Q4_1 || type == T_Q5_1)
                         acc += (double)oracle_half_to_float(rd16(blk + 2)) * d8 * (double)sq;
+                    continue;
+                }
+                if (type == T_Q2_K || type == T_Q3_K) {
+                    /* per 16-weight group j: d * sc_j * d8 * sum(q q8), and for Q2_K
+                     * - dmin * m_j * d8 * sum(q8) */
+                    const double d = oracle_half_to_float(rd16(blk + (type == T_Q2_K ? 80 : 108)));
+                    const double dmin = type == T_Q2_K ? oracle_half_to_float(rd16(blk + 82)) : 0.0;
+                    double sd = 0.0, sm = 0.0;
+                    for (int j = 0; j < 16; ++j) {
+                        const uint8_t *ab = xc + (8 * b + (j >> 1)) * 36;
+                        const int8_t *a = (const int8_t *)(ab + 4) + 16 * (j & 1);
+                        int32_t si = 0, sq = 0;
+                        for (int e = 0; e < 16; ++e) {
+                            const int w = 16 * j + e;
+                            si += (type == T_Q2_K ? q2k_quant(blk, w) : q3k_quant(blk, w)) * a[e];
+                            sq += a[e];
+                        }
+                        const double d8 = oracle_half_to_float(rd16(ab));
+                        const int sc = type == T_Q2_K ? (blk[j] & 15) : q3k_scale(blk, j);
+                        sd += d8 * (double)sc * (double)si;
+                        if (type == T_Q2_K) sm += d8 * (double)(blk[j] >> 4) * (double)sq;
+                    }
+                    acc += d * sd - dmin * sm;
                     continue;
                 }
                 if (type == T_Q6_K) {

@@ -17,7 +17,8 @@ HERE = Path(__file__).resolve().parent
 LIB = HERE / "_build" / "liboracle.so"
 REF_SMITHY = HERE / "_ref" / "libsmithy_ref.so"
 
-TYPE_IDS = {"Q4_0": 2, "Q4_1": 3, "Q5_0": 6, "Q5_1": 7, "Q8_0": 8, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14}
+TYPE_IDS = {"Q4_0": 2, "Q4_1": 3, "Q5_0": 6, "Q5_1": 7, "Q8_0": 8, "Q2_K": 10, "Q3_K": 11, "Q4_K": 12,
+            "Q5_K": 13, "Q6_K": 14}
 
 _lib = None
 
@@ -84,7 +85,7 @@ def dequantize_q8_1(xq: np.ndarray, K: int) -> np.ndarray:
 
 
 def block_sums(qt, W: np.ndarray, xq: np.ndarray, nrows: int, K: int, ncols: int = 1) -> np.ndarray:
-    nsub = K // 16 if _tid(qt) == 14 else K // 32
+    nsub = K // 16 if _tid(qt) in (10, 11, 14) else K // 32
     out = np.empty((ncols, nrows, nsub), dtype=np.int32)
     W = np.ascontiguousarray(W, dtype=np.uint8)
     xq = np.ascontiguousarray(xq, dtype=np.uint8)

@@ -20,7 +20,7 @@ from oracle import oracle  # noqa: E402
 
 pytestmark = pytest.mark.gpu
 
-TYPES = ["Q4_K", "Q5_K", "Q6_K", "Q8_0", "Q4_0", "Q4_1", "Q5_0", "Q5_1"]
+TYPES = ["Q4_K", "Q5_K", "Q6_K", "Q8_0", "Q4_0", "Q4_1", "Q5_0", "Q5_1", "Q2_K", "Q3_K"]
 Y_TOL = 1e-3
 
 
@@ -201,7 +201,7 @@ def test_argument_errors():
     with pytest.raises(AnvilError, match="CUDA tensor"):
         ops.mmvq(W.cpu(), "Q4_K", xq)
     with pytest.raises(ValueError, match="unsupported quant type"):
-        ops.mmvq(W, "Q2_K", xq)
+        ops.mmvq(W, "IQ2_XXS", xq)
 
 
 def test_no_device_wait_gave_up():

@@ -13,7 +13,7 @@ import pytest
 from kernel_anvil.quants import QUANT_TYPES, make_activation, make_weights
 from oracle import oracle
 
-TYPES = ["Q4_K", "Q5_K", "Q6_K", "Q8_0", "Q4_0", "Q4_1", "Q5_0", "Q5_1"]
+TYPES = ["Q4_K", "Q5_K", "Q6_K", "Q8_0", "Q4_0", "Q4_1", "Q5_0", "Q5_1", "Q2_K", "Q3_K"]
 
 
 @pytest.mark.parametrize("qt", TYPES)
@@ -120,6 +120,21 @@ def test_block_sums_reconstruct_y(qt):
             elif qt in ("Q4_1", "Q5_1"):  # unsigned quants; the min m times d8 * sum(q8)
                 d, m = blk[0:4].copy().view(np.float16).astype(np.float64)
                 y[r] += d * d8[b] * sums[r, b] + m * d8[b] * qsum[b]
+            elif qt in ("Q2_K", "Q3_K"):
+                # 16 groups of 16 weights; Q2_K: nibble scale and min, Q3_K: 6-bit scale - 32
+                xq16 = xb[:, 4:].view(np.int8).astype(np.int64).reshape(-1, 2, 16).sum(axis=2)
+                for g in range(16):
+                    kb = 8 * b + g // 2
+                    if qt == "Q2_K":
+                        d, dmin = blk[80:84].copy().view(np.float16).astype(np.float64)
+                        sc, m = int(blk[g]) & 15, int(blk[g]) >> 4
+                        y[r] += d * sc * d8[kb] * sums[r, 16 * b + g] - dmin * m * d8[kb] * xq16[kb, g % 2]
+                    else:
+                        d = blk[108:110].copy().view(np.float16).astype(np.float64)[0]
+                        s = blk[96:108].astype(int)
+                        lo = s[g] & 15 if g < 8 else s[g - 8] >> 4
+                        sc = (lo | (((s[8 + g % 4] >> (2 * (g // 4))) & 3) << 4)) - 32
+                        y[r] += d * sc * d8[kb] * sums[r, 16 * b + g]
             elif qt == "Q6_K":
                 d = blk[208:210].copy().view(np.float16).astype(np.float64)[0]
                 sc = blk[192:208].view(np.int8).astype(np.float64)
