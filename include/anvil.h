@@ -112,7 +112,9 @@ int anvil_quantize_q8_1_ex(const float *x, void *xq, int K, int ncols, unsigned 
  * nwarps (warps per CTA, 1..32) and rows_per_block (rows per CTA) keep their smithy
  * meaning; 0 selects the smithy table entry for (type, nrows, ncols_x), else the
  * built-in default.  rows_per_block is rounded down to 1, 2, 4 or 8 and reduced
- * further when the tile would not fit in shared memory.
+ * further when the tile would not fit in shared memory.  When ncols_dst columns of
+ * activation do not fit (K = 28672 with 6-8 columns), the call launches the columns in
+ * chunks that do, each chunk reading the weights again.
  * Requirements: K % qk == 0; W 16-byte aligned; xq 4-byte aligned; y 4-byte aligned. */
 int anvil_mmvq(int ggml_type, const void *W, const void *xq, float *y, int nrows, int ncols_x,
                int ncols_dst, int nwarps, int rows_per_block, anvil_stream_t stream);

@@ -8,6 +8,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <memory>
 #include <mutex>
 #include <string>
 #include <unordered_map>
@@ -194,6 +195,11 @@ struct Plan {
     int mode, nwarps, rpb, nstages, grid, smem;
     int occ, nsm;
     long ctas_needed;
+    // Column chunks: when the staged activation of all ncols columns does not fit in shared
+    // memory, the launch runs `chunk` columns at a time (fn and the fields above are the
+    // chunk's plan) and `tail` plans the last ncols % chunk columns.  chunk 0: one launch.
+    int ncols, chunk, type;
+    std::shared_ptr<const Plan> tail;
 };
 
 // Grid of a plan when `share` kernels are meant to be resident on each SM at once (a chain
@@ -206,8 +212,12 @@ static int grid_for(const Plan &p, int share) {
 
 static int round_rpb(int r) { return r >= 8 ? 8 : r >= 4 ? 4 : r >= 2 ? 2 : 1; }
 
-static int plan_mmvq(int t, int nrows, int K, int ncols, int nwarps, int rpb, int mode,
-                     Plan *p) {
+static int plan_one(int t, int nrows, int K, int ncols, int nwarps, int rpb, int mode,
+                    Plan *p) {
+    p->ncols = ncols;
+    p->chunk = 0;
+    p->type = t;
+    p->tail.reset();
     if (!supported_type(t)) return fail(ANVIL_ERR_UNSUPPORTED, "ggml type %d has no MMVQ kernel", t);
     if (nrows <= 0 || K <= 0) return fail(ANVIL_ERR_INVALID, "nrows=%d ncols_x=%d", nrows, K);
     const int qk = mmvq_type_qk(t);
@@ -273,7 +283,7 @@ static int plan_mmvq(int t, int nrows, int K, int ncols, int nwarps, int rpb, in
     if (!p->fn) return fail(ANVIL_ERR_UNSUPPORTED, "no kernel for ncols=%d rpb=%d", ncols, rpb);
     p->nwarps = nwarps;
     p->rpb = rpb;
-    int occ;
+    int occ = 0;
     if (int s = prepare_fn(reinterpret_cast<const void *>(p->fn), dev, nwarps * 32, p->smem, &occ))
         return s;
     // Persistent grid: every warp takes warp-tiles of rpb rows (rpb/2 output rows for the
@@ -287,6 +297,33 @@ static int plan_mmvq(int t, int nrows, int K, int ncols, int nwarps, int rpb, in
     return ANVIL_OK;
 }
 
+// plan_one, or, when ncols columns of activation do not fit in shared memory, the largest
+// column chunk that does (launched once per chunk; the weights are re-read per chunk).
+static int plan_mmvq(int t, int nrows, int K, int ncols, int nwarps, int rpb, int mode,
+                     Plan *p) {
+    const int s = plan_one(t, nrows, K, ncols, nwarps, rpb, mode, p);
+    if (s != ANVIL_ERR_UNSUPPORTED || ncols == 1 ||
+        t_last_error.find("does not fit in shared memory") == std::string::npos)
+        return s;
+    const std::string why = t_last_error;
+    for (int c = ncols - 1; c >= 1; --c) {
+        Plan head;
+        if (plan_one(t, nrows, K, c, nwarps, rpb, mode, &head) != ANVIL_OK) continue;
+        if (ncols % c) {
+            auto tail = std::make_shared<Plan>();
+            if (plan_one(t, nrows, K, ncols % c, nwarps, rpb, mode, tail.get()) != ANVIL_OK) continue;
+            head.tail = tail;
+        }
+        head.ncols = ncols;
+        head.chunk = c;
+        *p = head;
+        t_last_error.clear();
+        return ANVIL_OK;
+    }
+    t_last_error = why;
+    return ANVIL_ERR_UNSUPPORTED;
+}
+
 // Segments of one launch: GEMVs of the plan's type that read the same activation.
 struct Segs {
     int n;
@@ -295,8 +332,8 @@ struct Segs {
     int rows[kMaxSeg];
 };
 
-static int launch_mmvq_segs(const Plan &p, const Segs &sg, const void *x, int32_t *sums, int K,
-                            unsigned flags, cudaStream_t stream, int share = 1) {
+static int launch_segs_one(const Plan &p, const Segs &sg, const void *x, int32_t *sums, int K,
+                           unsigned flags, cudaStream_t stream, int share) {
     MmvqArgs a;
     a.x = x;
     a.sums = sums;
@@ -330,6 +367,28 @@ static int launch_mmvq_segs(const Plan &p, const Segs &sg, const void *x, int32_
     }
     cudaError_t e = cudaLaunchKernelEx(&cfg, p.fn, a);
     if (e != cudaSuccess) return cuda_fail(e, "mmvq launch");
+    return ANVIL_OK;
+}
+
+// One launch, or one per column chunk of the plan (columns are independent: chunk c0 reads
+// activation columns c0.. and writes output columns c0..).
+static int launch_mmvq_segs(const Plan &p, const Segs &sg, const void *x, int32_t *sums, int K,
+                            unsigned flags, cudaStream_t stream, int share = 1) {
+    if (p.chunk == 0) return launch_segs_one(p, sg, x, sums, K, flags, stream, share);
+    const int nkb = K / 32;
+    const bool sub16 = p.type == kTypeQ6_K || p.type == kTypeQ2_K || p.type == kTypeQ3_K;
+    const int nsub = K / (sub16 ? 16 : 32);  // int32 sums per row and column (block-sum mode)
+    for (int c0 = 0; c0 < p.ncols; c0 += p.chunk) {
+        const Plan &q = p.ncols - c0 >= p.chunk ? p : *p.tail;
+        Segs part = sg;
+        for (int i = 0; i < sg.n; ++i) part.y[i] = sg.y[i] ? sg.y[i] + size_t(c0) * sg.rows[i] : nullptr;
+        const void *xc = p.mode == kModeF32
+                             ? static_cast<const void *>(static_cast<const float *>(x) + size_t(c0) * K)
+                             : static_cast<const void *>(static_cast<const uint8_t *>(x) +
+                                                         size_t(c0) * nkb * kQ8_1Bytes);
+        int32_t *sc = sums ? sums + size_t(c0) * sg.rows[0] * nsub : nullptr;
+        if (int s = launch_segs_one(q, part, xc, sc, K, flags, stream, share)) return s;
+    }
     return ANVIL_OK;
 }
 

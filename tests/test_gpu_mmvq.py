@@ -124,6 +124,21 @@ def test_fused_f32_path_matches_two_step(qt):
     assert torch.equal(y1, y2)
 
 
+@pytest.mark.parametrize("qt,ncols", [("Q4_K", 8), ("Q6_K", 7), ("Q8_0", 6), ("Q2_K", 8)])
+def test_long_rows_many_columns_in_chunks(qt, ncols):
+    """K = 28672 with 6-8 columns: the staged activation exceeds shared memory, so the launch
+    runs in column chunks; y and the int32 block sums still meet the bars, and the fp32-input
+    path equals quantise + MMVQ."""
+    K = 28672
+    check_case(qt, 300, K, ncols, seed=ncols)
+    W = dev(make_weights(qt, 64, K, seed=1))
+    x = dev(make_activation(K, ncols=ncols, seed=2))
+    y1 = ops.mmvq(W, qt, ops.quantize_q8_1(x), ncols=ncols)
+    y2 = ops.mmvq_f32(W, qt, x)
+    torch.cuda.synchronize()
+    assert torch.equal(y1, y2)
+
+
 def test_pdl_launch_same_result():
     K = 4096
     W = dev(make_weights("Q4_K", 512, K, seed=4))
