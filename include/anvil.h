@@ -26,7 +26,8 @@
  *     c * (K / 32) * 36 (Q8_1).  Output column c starts at element c * nrows.
  *   - ggml type ids follow ggml.h (kernel_anvil/codegen.py:22-31):
  *     Q4_0 = 2, Q4_1 = 3, Q5_0 = 6, Q5_1 = 7, Q8_0 = 8, Q2_K = 10, Q3_K = 11, Q4_K = 12,
- *     Q5_K = 13, Q6_K = 14 (the persistent chain takes Q8_0, Q4_K, Q5_K and Q6_K).
+ *     Q5_K = 13, Q6_K = 14, IQ4_NL = 20, IQ4_XS = 23 (the persistent chain takes Q8_0,
+ *     Q4_K, Q5_K and Q6_K).
  *   - Thread-safe: the smithy table is guarded by a reader/writer lock; the launch
  *     entry points keep no mutable shared state besides one-time function attributes.
  */
@@ -65,7 +66,9 @@ enum anvil_ggml_type {
     ANVIL_TYPE_Q3_K = 11,
     ANVIL_TYPE_Q4_K = 12,
     ANVIL_TYPE_Q5_K = 13,
-    ANVIL_TYPE_Q6_K = 14
+    ANVIL_TYPE_Q6_K = 14,
+    ANVIL_TYPE_IQ4_NL = 20,
+    ANVIL_TYPE_IQ4_XS = 23
 };
 
 /* Launch flags for anvil_mmvq_ex / anvil_quantize_q8_1_ex. */
@@ -171,8 +174,9 @@ int anvil_mmvq_grouped_f32(int ggml_type, int nseg, const void *const *W, const 
  * "Q4_K fused (gate+SiLU)" MMVQ variant of docs/decode-pipeline-breakdown.md:40, the fused
  * gate+up launch of docs/vulkan-vs-rocm-analysis.md:103-106 and its GLU op (:135).  Both
  * matrices have ggml_type and nrows x ncols_x values; their rows must be a multiple of 16
- * bytes (Q4_K, Q5_K always; Q8_0, Q4_0 .. Q5_1 when ncols_x % 256 == 0; Q2_K when
- * ncols_x % 1024 == 0; Q3_K, Q6_K when ncols_x % 2048 == 0), else ANVIL_ERR_ALIGN.
+ * bytes (Q4_K, Q5_K always; Q8_0, Q4_0 .. Q5_1, IQ4_NL when ncols_x % 256 == 0; IQ4_XS
+ * when ncols_x % 512 == 0; Q2_K when ncols_x % 1024 == 0; Q3_K, Q6_K when
+ * ncols_x % 2048 == 0), else ANVIL_ERR_ALIGN.
  * rows_per_block counts gate and up rows together (at least 2).  _f32: fp32 x quantised
  * into the scratch xq first (two launches, the second under ANVIL_FLAG_PDL). */
 int anvil_mmvq_glu(int ggml_type, const void *W_gate, const void *W_up, const void *xq, float *y,
@@ -191,7 +195,8 @@ int anvil_take_device_status(void);
 /* Parity probe: runs the production MMVQ kernel with its integer block sums written
  * out instead of y.  sums[(c * nrows + r) * nsub + s] is the exact int32 dot of
  * sub-block s of row r with column c, where a sub-block is 32 weights (one Q8_1
- * block) for Q4_K, Q5_K, Q8_0 and Q4_0 .. Q5_1, and 16 weights (one scale group) for Q2_K,
+ * block) for Q4_K, Q5_K, Q8_0, Q4_0 .. Q5_1, IQ4_NL and IQ4_XS (the int8 level times q8),
+ * and 16 weights (one scale group) for Q2_K,
  * Q3_K and Q6_K, so nsub = K/32 or K/16.  For Q2_K/Q4_K/Q5_K and the _1 types the weight
  * operand is the unsigned quant (the min term is separate); for Q3_K it is q with its
  * offset of -4; for Q6_K q - 32; for Q4_0 / Q5_0 q - 8 / q - 16; for Q8_0 the int8 quant. */

@@ -154,7 +154,8 @@ static int prepare_fn(const void *fn, int dev, int threads, int smem, int *occ) 
 // ---------------------------------------------------------------------------------
 static bool supported_type(int t) {
     return t == kTypeQ4_K || t == kTypeQ5_K || t == kTypeQ6_K || t == kTypeQ8_0 || t == kTypeQ4_0 ||
-           t == kTypeQ4_1 || t == kTypeQ5_0 || t == kTypeQ5_1 || t == kTypeQ2_K || t == kTypeQ3_K;
+           t == kTypeQ4_1 || t == kTypeQ5_0 || t == kTypeQ5_1 || t == kTypeQ2_K || t == kTypeQ3_K ||
+           t == kTypeIQ4_NL || t == kTypeIQ4_XS;
 }
 
 static MmvqKernelFn kernel_for(int t, int ncols, int rpb, int lbt, int mode) {
@@ -169,6 +170,8 @@ static MmvqKernelFn kernel_for(int t, int ncols, int rpb, int lbt, int mode) {
     case kTypeQ5_1: return mmvq_kernel_q51(ncols, rpb, lbt, mode);
     case kTypeQ2_K: return mmvq_kernel_q2k(ncols, rpb, lbt, mode);
     case kTypeQ3_K: return mmvq_kernel_q3k(ncols, rpb, lbt, mode);
+    case kTypeIQ4_NL: return mmvq_kernel_iq4nl(ncols, rpb, lbt, mode);
+    case kTypeIQ4_XS: return mmvq_kernel_iq4xs(ncols, rpb, lbt, mode);
     default: return nullptr;
     }
 }
@@ -538,6 +541,8 @@ int anvil_type_geometry(int ggml_type, int *qk, int *block_bytes) {
     case ANVIL_TYPE_Q8_0: q = 32; b = 34; break;
     case ANVIL_TYPE_Q8_1: q = 32; b = 36; break;
     case ANVIL_TYPE_Q2_K: q = 256; b = 84; break;
+    case ANVIL_TYPE_IQ4_NL: q = 32; b = 18; break;
+    case ANVIL_TYPE_IQ4_XS: q = 256; b = 136; break;
     case ANVIL_TYPE_Q3_K: q = 256; b = 110; break;
     case ANVIL_TYPE_Q4_K: q = 256; b = 144; break;
     case ANVIL_TYPE_Q5_K: q = 256; b = 176; break;
@@ -722,12 +727,13 @@ int anvil_mmvq_block_sums(int ggml_type, const void *W, const void *xq, int32_t 
 // flags (0 = no bounded wait gave up) or a negative status.
 int anvil_take_device_status(void) {
     int v = 0;
-    int parts[11] = {take_quantize_status(), mmvq_kernel_q4k_take_status(),
+    int parts[13] = {take_quantize_status(), mmvq_kernel_q4k_take_status(),
                     mmvq_kernel_q5k_take_status(), mmvq_kernel_q6k_take_status(),
                     mmvq_kernel_q80_take_status(), mmvq_kernel_q40_take_status(),
                     mmvq_kernel_q41_take_status(), mmvq_kernel_q50_take_status(),
                     mmvq_kernel_q51_take_status(), mmvq_kernel_q2k_take_status(),
-                    mmvq_kernel_q3k_take_status()};
+                    mmvq_kernel_q3k_take_status(), mmvq_kernel_iq4nl_take_status(),
+                    mmvq_kernel_iq4xs_take_status()};
     for (int x : parts) {
         if (x < 0) return fail(ANVIL_ERR_CUDA, "reading device status failed");
         v |= x;

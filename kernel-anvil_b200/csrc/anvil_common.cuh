@@ -16,8 +16,14 @@
 //   Q5_0 ( 22 B /  32 weights): d f16 @0, qh u32 @2 (bit e = bit 4 of weight e), qs[16] @6; q - 16
 //   Q5_1 ( 24 B /  32 weights): d f16 @0, m f16 @2, qh u32 @4, qs[16] @8 (x = d q + m)
 //   Q8_0 ( 34 B /  32 weights): d f16 @0, qs int8[32] @2
+//   IQ4_NL ( 18 B /  32 weights): d f16 @0, qs[16] @2 (nibbles in Q4_0 order) indexing the
+//                                  16 non-linear int8 levels kIQ4Levels0..3
+//   IQ4_XS (136 B / 256 weights): d f16 @0, scales_h u16 @2, scales_l[4] @4, qs[128] @8;
+//                                  8 groups of 32 (qs bytes 16j..16j+15, low then high
+//                                  nibbles), 6-bit group scale minus 32
 //   Q8_1 ( 36 B /  32 values ): d f16 @0, s f16 @2, qs int8[32] @4   (GPU layout)
-// (gguf-py quants.py:396-401, 504-523, 527-549, 554-572, Q2_K / Q3_K dequantize_blocks;
+// (gguf-py quants.py:396-401, 504-523, 527-549, 554-572, Q2_K / Q3_K / IQ4_NL / IQ4_XS
+//  dequantize_blocks;
 //  kernel_anvil/hip_codegen.py:84-85, 101-102, 385-396.)
 #pragma once
 
@@ -37,6 +43,8 @@ constexpr int kTypeQ3_K = 11;
 constexpr int kTypeQ4_K = 12;
 constexpr int kTypeQ5_K = 13;
 constexpr int kTypeQ6_K = 14;
+constexpr int kTypeIQ4_NL = 20;
+constexpr int kTypeIQ4_XS = 23;
 
 constexpr int kQK_K = 256;
 constexpr int kQK8_1 = 32;
@@ -72,6 +80,12 @@ template <> struct QTraits<kTypeQ5_0> {
 };
 template <> struct QTraits<kTypeQ5_1> {
     static constexpr int qk = 32, bytes = 24, units = 1, sub = 32;
+};
+template <> struct QTraits<kTypeIQ4_NL> {
+    static constexpr int qk = 32, bytes = 18, units = 1, sub = 32;
+};
+template <> struct QTraits<kTypeIQ4_XS> {
+    static constexpr int qk = 256, bytes = 136, units = 4, sub = 32;
 };
 template <> struct QTraits<kTypeQ8_0> {
     static constexpr int qk = 32, bytes = 34, units = 1, sub = 32;

@@ -96,6 +96,8 @@ __host__ __device__ inline int mmvq_type_bytes(int qt) {
     case kTypeQ4_1: return 20;
     case kTypeQ5_0: return 22;
     case kTypeQ5_1: return 24;
+    case kTypeIQ4_NL: return 18;
+    case kTypeIQ4_XS: return 136;
     case kTypeQ2_K: return 84;
     case kTypeQ3_K: return 110;
     case kTypeQ4_K: return 144;
@@ -106,7 +108,7 @@ __host__ __device__ inline int mmvq_type_bytes(int qt) {
 }
 __host__ __device__ inline int mmvq_type_qk(int qt) {
     return qt == kTypeQ4_K || qt == kTypeQ5_K || qt == kTypeQ6_K || qt == kTypeQ2_K ||
-                   qt == kTypeQ3_K
+                   qt == kTypeQ3_K || qt == kTypeIQ4_XS
                ? 256
                : 32;
 }
@@ -115,7 +117,7 @@ __host__ __device__ inline int mmvq_type_qk(int qt) {
 template <int QT>
 constexpr bool kBasic = QT == kTypeQ4_0 || QT == kTypeQ4_1 || QT == kTypeQ5_0 || QT == kTypeQ5_1;
 template <int QT>
-constexpr bool kBlock32 = QT == kTypeQ8_0 || kBasic<QT>;
+constexpr bool kBlock32 = QT == kTypeQ8_0 || kBasic<QT> || QT == kTypeIQ4_NL;
 // The K-quants with 16-weight scale groups (two per Q8_1 block).
 template <int QT>
 constexpr bool kSub16 = QT == kTypeQ6_K || QT == kTypeQ2_K || QT == kTypeQ3_K;
@@ -263,6 +265,29 @@ template <> struct Units<kTypeQ4_0> { static constexpr int n = 1; };
 template <> struct Units<kTypeQ4_1> { static constexpr int n = 1; };
 template <> struct Units<kTypeQ5_0> { static constexpr int n = 1; };
 template <> struct Units<kTypeQ5_1> { static constexpr int n = 1; };
+template <> struct Units<kTypeIQ4_NL> { static constexpr int n = 1; };
+
+// The 16 non-linear int8 levels of IQ4_NL / IQ4_XS (ggml's kvalues_iq4nl, as listed by
+// gguf-py quants.py IQ4_NL.kvalues), four per little-endian word.
+constexpr uint32_t iq4_word(int a, int b, int c, int d) {
+    return uint32_t(uint8_t(a)) | uint32_t(uint8_t(b)) << 8 | uint32_t(uint8_t(c)) << 16 |
+           uint32_t(uint8_t(d)) << 24;
+}
+constexpr uint32_t kIQ4Levels0 = iq4_word(-127, -104, -83, -65);
+constexpr uint32_t kIQ4Levels1 = iq4_word(-49, -35, -22, -10);
+constexpr uint32_t kIQ4Levels2 = iq4_word(1, 13, 25, 38);
+constexpr uint32_t kIQ4Levels3 = iq4_word(53, 69, 89, 113);
+
+// Four 4-bit level indices (one per byte, 0..15) -> their four int8 levels, by two byte
+// permutes over the low and high halves of the table and a per-byte select on bit 3.
+__device__ __forceinline__ uint32_t iq4_levels(uint32_t idx) {
+    const uint32_t sel = (idx & 0x7u) | ((idx >> 4) & 0x70u) | ((idx >> 8) & 0x700u) |
+                         ((idx >> 12) & 0x7000u);
+    const uint32_t lo = __byte_perm(kIQ4Levels0, kIQ4Levels1, sel);
+    const uint32_t hi = __byte_perm(kIQ4Levels2, kIQ4Levels3, sel);
+    const uint32_t m = ((idx >> 3) & 0x01010101u) * 0xFFu;
+    return (hi & m) | (lo & ~m);
+}
 
 // Q8_1 blocks consumed by unit U of super-block b.
 template <int QT, int U>
@@ -293,6 +318,10 @@ __device__ __forceinline__ BlkHdr load_hdr(const uint8_t *blk) {
         h.s2 = v.w;
     } else if constexpr (QT == kTypeQ6_K) {
         h.d = h2f(lds16(blk + 208));
+    } else if constexpr (QT == kTypeIQ4_XS) {
+        h.d = h2f(lds16(blk));
+        h.s0 = lds16(blk + 2);                                 // scales_h
+        h.s1 = lds16(blk + 4) | (lds16(blk + 6) << 16);        // scales_l[4]
     } else if constexpr (QT == kTypeQ2_K) {
         h.d = h2f(lds16(blk + 80));
         h.dmin = h2f(lds16(blk + 82));
@@ -371,6 +400,26 @@ __device__ __forceinline__ void load_unit(const uint8_t *blk, WBytes &w) {
         for (int k = 0; k < 8; ++k) {
             w.q0[k] = (ql[k] & 0x0F0F0F0Fu) | (((qh[k] >> (2 * t)) & 0x03030303u) << 4);
             w.q1[k] = ((ql[k] >> 4) & 0x0F0F0F0Fu) | ((qh[k] >> (2 * t)) & 0x30303030u);
+        }
+    } else if constexpr (QT == kTypeIQ4_XS) {
+        // groups 2U and 2U+1: qs bytes [32U, 32U + 32); within a group byte e holds weight e
+        // (low nibble) and weight 16 + e (high nibble)
+        uint32_t v[8];
+        lds32_a2(blk + 8 + 32 * U, v);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            w.q0[k] = iq4_levels(v[k] & 0x0F0F0F0Fu);
+            w.q0[4 + k] = iq4_levels((v[k] >> 4) & 0x0F0F0F0Fu);
+            w.q1[k] = iq4_levels(v[4 + k] & 0x0F0F0F0Fu);
+            w.q1[4 + k] = iq4_levels((v[4 + k] >> 4) & 0x0F0F0F0Fu);
+        }
+    } else if constexpr (QT == kTypeIQ4_NL) {
+        uint32_t v[4];
+        lds16B_a2(blk + 2, v);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            w.q0[k] = iq4_levels(v[k] & 0x0F0F0F0Fu);
+            w.q0[4 + k] = iq4_levels((v[k] >> 4) & 0x0F0F0F0Fu);
         }
     } else if constexpr (QT == kTypeQ2_K || QT == kTypeQ3_K) {
         // weight 64U + 32i + l (i = 0, 1: Q8_1 block kb0, kb1) is bits 2(2(U&1) + i) of qs
@@ -470,6 +519,26 @@ __device__ __forceinline__ float dot_unit(const uint8_t *blk, const BlkHdr &h, c
         const int s00 = int(int8_t(sc0 & 0xFF)), s01 = int(int8_t(sc0 >> 8));
         const int s10 = int(int8_t(sc1 & 0xFF)), s11 = int(int8_t(sc1 >> 8));
         return h.d * (a0.d * float(p00 * s00 + p01 * s01) + a1.d * float(p10 * s10 + p11 * s11));
+    } else if constexpr (QT == kTypeIQ4_XS) {
+        // d * sum_j d8_j * (ls_j - 32) * sum(level * q8) over groups j = 2U, 2U+1, with
+        // ls_j = scales_l nibble j | (scales_h bits 2j, 2j+1) << 4
+        int i0 = 0, i1 = 0;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            i0 = __dp4a(int(w.q0[k]), int(a0.q[k]), i0);
+            i1 = __dp4a(int(w.q1[k]), int(a1.q[k]), i1);
+        }
+        isum[0] = i0;
+        isum[1] = i1;
+        const int ls0 = int(((h.s1 >> (8 * U)) & 15u) | (((h.s0 >> (4 * U)) & 3u) << 4)) - 32;
+        const int ls1 = int(((h.s1 >> (8 * U + 4)) & 15u) | (((h.s0 >> (4 * U + 2)) & 3u) << 4)) - 32;
+        return h.d * (a0.d * float(i0 * ls0) + a1.d * float(i1 * ls1));
+    } else if constexpr (QT == kTypeIQ4_NL) {
+        int i0 = 0;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) i0 = __dp4a(int(w.q0[k]), int(a0.q[k]), i0);
+        isum[0] = i0;
+        return h.d * (a0.d * float(i0));
     } else if constexpr (QT == kTypeQ2_K || QT == kTypeQ3_K) {
         int p00 = 0, p01 = 0, p10 = 0, p11 = 0;
 #pragma unroll
@@ -996,6 +1065,8 @@ MmvqKernelFn mmvq_kernel_q50(int ncols, int rpb, int lbt, int mode);
 MmvqKernelFn mmvq_kernel_q51(int ncols, int rpb, int lbt, int mode);
 MmvqKernelFn mmvq_kernel_q2k(int ncols, int rpb, int lbt, int mode);
 MmvqKernelFn mmvq_kernel_q3k(int ncols, int rpb, int lbt, int mode);
+MmvqKernelFn mmvq_kernel_iq4nl(int ncols, int rpb, int lbt, int mode);
+MmvqKernelFn mmvq_kernel_iq4xs(int ncols, int rpb, int lbt, int mode);
 // Reads and clears the device status word of that type's translation unit (current device).
 int mmvq_kernel_q4k_take_status();
 int mmvq_kernel_q5k_take_status();
@@ -1007,6 +1078,8 @@ int mmvq_kernel_q50_take_status();
 int mmvq_kernel_q51_take_status();
 int mmvq_kernel_q2k_take_status();
 int mmvq_kernel_q3k_take_status();
+int mmvq_kernel_iq4nl_take_status();
+int mmvq_kernel_iq4xs_take_status();
 
 }  // namespace anvil
 

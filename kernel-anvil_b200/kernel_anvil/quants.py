@@ -61,6 +61,8 @@ QUANT_TYPES: dict[str, QuantTypeInfo] = {
     "Q4_K": QuantTypeInfo("Q4_K", 12, 256, 32, 2, 144),
     "Q5_K": QuantTypeInfo("Q5_K", 13, 256, 32, 2, 176),
     "Q6_K": QuantTypeInfo("Q6_K", 14, 256, 32, 1, 210),
+    "IQ4_NL": QuantTypeInfo("IQ4_NL", 20, 32, 4, 2, 18),
+    "IQ4_XS": QuantTypeInfo("IQ4_XS", 23, 256, 32, 4, 136),
 }
 TYPE_BY_ID = {q.ggml_type: q for q in QUANT_TYPES.values()}
 
@@ -127,6 +129,10 @@ def make_weights(qt, nrows: int, K: int, seed: int = 0) -> np.ndarray:
     elif info.name == "Q3_K":
         blocks[:, 0:108] = rng.integers(0, 256, size=(nb, 108), dtype=np.uint8)
         blocks[:, 108:110] = _fp16_abs_normal(rng, nb, 1e-2)
+    elif info.name in ("IQ4_NL", "IQ4_XS"):
+        # d from |N(0,1)| * 1e-3 (levels reach +-127); scales and level indices uniform
+        blocks[:, 2:] = rng.integers(0, 256, size=(nb, info.block_size - 2), dtype=np.uint8)
+        blocks[:, 0:2] = _fp16_abs_normal(rng, nb, 1e-3)
     elif info.name in ("Q4_0", "Q4_1", "Q5_0", "Q5_1"):
         # d from |N(0,1)| * 1e-2; the _1 types' m (the block minimum) from -|N(0,1)| * 1e-1;
         # high bits (qh) and nibbles uniform
@@ -178,6 +184,8 @@ def make_weights_device(qt, nrows: int, K: int, seed: int = 0, device="cuda"):
         blocks[:, 82:84] = fp16_abs_normal(1e-2)
     elif info.name == "Q3_K":
         blocks[:, 108:110] = fp16_abs_normal(1e-2)
+    elif info.name in ("IQ4_NL", "IQ4_XS"):
+        blocks[:, 0:2] = fp16_abs_normal(1e-3)
     elif info.name in ("Q4_0", "Q4_1", "Q5_0", "Q5_1"):
         blocks[:, 0:2] = fp16_abs_normal(1e-2)
         if info.name.endswith("_1"):

@@ -5,9 +5,9 @@
  *
  * What it restates, and from where:
  *   - GGUF block layouts and per-weight dequantisation of Q4_0, Q4_1, Q5_0, Q5_1, Q2_K,
- *     Q3_K, Q4_K, Q5_K, Q6_K and Q8_0: gguf-py (the reference's declared dependency,
- *     kernel-anvil pyproject.toml:19, gguf 0.19.0) gguf/quants.py Q4_0..Q5_1 and Q2_K, Q3_K
- *     dequantize_blocks, 378-401 (Q8_0), 474-523 (Q4_K incl. get_scale_min), 525-549
+ *     Q3_K, Q4_K, Q5_K, Q6_K, Q8_0, IQ4_NL and IQ4_XS: gguf-py (the reference's declared
+ *     dependency, kernel-anvil pyproject.toml:19, gguf 0.19.0) gguf/quants.py Q4_0..Q5_1,
+ *     Q2_K, Q3_K, IQ4_NL and IQ4_XS dequantize_blocks, 378-401 (Q8_0), 474-523 (Q4_K incl. get_scale_min), 525-549
  *     (Q5_K), 552-572 (Q6_K).
  *     Pinned in tests against gguf.quants.dequantize (fixtures and live).
  *   - Q8_1 activation quantisation: llama.cpp's CUDA quantize_q8_1 semantics (the
@@ -36,7 +36,24 @@
 #endif
 
 enum { T_Q4_0 = 2, T_Q4_1 = 3, T_Q5_0 = 6, T_Q5_1 = 7, T_Q8_0 = 8, T_Q2_K = 10, T_Q3_K = 11,
-       T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14 };
+       T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14, T_IQ4_NL = 20, T_IQ4_XS = 23 };
+
+/* The 16 levels of IQ4_NL / IQ4_XS (gguf-py quants.py IQ4_NL.kvalues). */
+static const int iq4_levels[16] = {-127, -104, -83, -65, -49, -35, -22, -10,
+                                   1,    13,   25,  38,  53,  69,  89,  113};
+
+/* IQ4_NL (18 B: d @0, qs[16] @2): weight e is level qs[e] & 15 (e < 16) or qs[e - 16] >> 4.
+ * IQ4_XS (136 B: d @0, scales_h u16 @2, scales_l[4] @4, qs[128] @8): group j (32 weights)
+ * reads qs[16j + e] low nibble for e < 16 and qs[16j + e - 16] high nibble above; its scale
+ * is (scales_l[j / 2] nibble j % 2 | bits 2j..2j+1 of scales_h << 4) - 32. */
+static inline int iq4nl_level(const uint8_t *qs, int e) {
+    return iq4_levels[e < 16 ? (qs[e] & 15) : (qs[e - 16] >> 4)];
+}
+static inline int iq4xs_scale(const uint8_t *blk, int j) {
+    const int sh = blk[2] | (blk[3] << 8);
+    const int lo = (blk[4 + j / 2] >> (4 * (j & 1))) & 15;
+    return (lo | (((sh >> (2 * j)) & 3) << 4)) - 32;
+}
 
 /* ---- IEEE binary16 conversions (written from the format definition) ---------- */
 
@@ -198,6 +215,8 @@ static inline int q3k_scale(const uint8_t *blk, int j) {
 
 static int type_bytes(int t) {
     switch (t) {
+    case T_IQ4_NL: return 18;
+    case T_IQ4_XS: return 136;
     case T_Q2_K: return 84;
     case T_Q3_K: return 110;
     case T_Q4_0: return 18;
@@ -212,7 +231,7 @@ static int type_bytes(int t) {
     }
 }
 static int is_basic(int t) { return t == T_Q4_0 || t == T_Q4_1 || t == T_Q5_0 || t == T_Q5_1; }
-static int type_qk(int t) { return (t == T_Q8_0 || is_basic(t)) ? 32 : 256; }
+static int type_qk(int t) { return (t == T_Q8_0 || t == T_IQ4_NL || is_basic(t)) ? 32 : 256; }
 
 /* Q4_0 / Q4_1 / Q5_0 / Q5_1 (gguf-py quants.py Q4_0..Q5_1 dequantize_blocks): 32 weights;
  * element e < 16 is the low nibble of qs[e], element e >= 16 the high nibble of qs[e - 16];
@@ -253,6 +272,15 @@ int oracle_dequant(int type, const uint8_t *W, float *out, int64_t nrows, int64_
                 for (int e = 0; e < 32; ++e) o[e] = d * (float)basic_quant(type, blk, e) + m;
             } else {
                 for (int e = 0; e < 32; ++e) o[e] = d * (float)basic_quant(type, blk, e);
+            }
+        } else if (type == T_IQ4_NL) {
+            const float d = oracle_half_to_float(rd16(blk));
+            for (int e = 0; e < 32; ++e) o[e] = d * (float)iq4nl_level(blk + 2, e);
+        } else if (type == T_IQ4_XS) {
+            const float d = oracle_half_to_float(rd16(blk));
+            for (int j = 0; j < 8; ++j) {
+                const float dl = d * (float)iq4xs_scale(blk, j);
+                for (int e = 0; e < 32; ++e) o[32 * j + e] = dl * (float)iq4nl_level(blk + 8 + 16 * j, e);
             }
         } else if (type == T_Q2_K) {
             const float d = oracle_half_to_float(rd16(blk + 80));
@@ -326,6 +354,22 @@ int oracle_block_sums(int type, const uint8_t *W, const uint8_t *xq, int32_t *su
                     out[b] = s;
                     continue;
                 }
+                if (type == T_IQ4_NL) {
+                    const int8_t *a = (const int8_t *)(xc + b * 36 + 4);
+                    int32_t s = 0;
+                    for (int e = 0; e < 32; ++e) s += iq4nl_level(blk + 2, e) * a[e];
+                    out[b] = s;
+                    continue;
+                }
+                if (type == T_IQ4_XS) {
+                    for (int j = 0; j < 8; ++j) {
+                        const int8_t *a = (const int8_t *)(xc + (8 * b + j) * 36 + 4);
+                        int32_t s = 0;
+                        for (int e = 0; e < 32; ++e) s += iq4nl_level(blk + 8 + 16 * j, e) * a[e];
+                        out[8 * b + j] = s;
+                    }
+                    continue;
+                }
                 if (type == T_Q2_K || type == T_Q3_K) {
                     for (int j = 0; j < 16; ++j) {
                         const int8_t *a = (const int8_t *)(xc + (8 * b + (j >> 1)) * 36 + 4) + 16 * (j & 1);
@@ -394,6 +438,28 @@ int oracle_mmvq(int type, const uint8_t *W, const uint8_t *xq, double *y, int64_
                     acc += (double)oracle_half_to_float(rd16(blk)) * d8 * (double)s;
                     if (type == T_Q4_1 || type == T_Q5_1)
                         acc += (double)oracle_half_to_float(rd16(blk + 2)) * d8 * (double)sq;
+                    continue;
+                }
+                if (type == T_IQ4_NL) {
+                    const uint8_t *ab = xc + b * 36;
+                    const int8_t *a = (const int8_t *)(ab + 4);
+                    int32_t s = 0;
+                    for (int e = 0; e < 32; ++e) s += iq4nl_level(blk + 2, e) * a[e];
+                    acc += (double)oracle_half_to_float(rd16(blk)) *
+                           (double)oracle_half_to_float(rd16(ab)) * (double)s;
+                    continue;
+                }
+                if (type == T_IQ4_XS) {
+                    /* d * sum_j d8_j * scale_j * sum(level * q8) */
+                    double sb = 0.0;
+                    for (int j = 0; j < 8; ++j) {
+                        const uint8_t *ab = xc + (8 * b + j) * 36;
+                        const int8_t *a = (const int8_t *)(ab + 4);
+                        int32_t s = 0;
+                        for (int e = 0; e < 32; ++e) s += iq4nl_level(blk + 8 + 16 * j, e) * a[e];
+                        sb += (double)oracle_half_to_float(rd16(ab)) * (double)iq4xs_scale(blk, j) * (double)s;
+                    }
+                    acc += (double)oracle_half_to_float(rd16(blk)) * sb;
                     continue;
                 }
                 if (type == T_Q2_K || type == T_Q3_K) {

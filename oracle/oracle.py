@@ -18,7 +18,7 @@ LIB = HERE / "_build" / "liboracle.so"
 REF_SMITHY = HERE / "_ref" / "libsmithy_ref.so"
 
 TYPE_IDS = {"Q4_0": 2, "Q4_1": 3, "Q5_0": 6, "Q5_1": 7, "Q8_0": 8, "Q2_K": 10, "Q3_K": 11, "Q4_K": 12,
-            "Q5_K": 13, "Q6_K": 14}
+            "Q5_K": 13, "Q6_K": 14, "IQ4_NL": 20, "IQ4_XS": 23}
 
 _lib = None
 

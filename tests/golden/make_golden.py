@@ -39,7 +39,7 @@ from kernel_anvil.quants import make_activation, make_weights  # noqa: E402
 
 DEQUANT_CASES = {"Q4_K": (8, 512), "Q5_K": (8, 512), "Q6_K": (8, 512), "Q8_0": (8, 256),
                  "Q4_0": (8, 256), "Q4_1": (8, 256), "Q5_0": (8, 256), "Q5_1": (8, 256),
-                 "Q2_K": (8, 512), "Q3_K": (8, 512)}
+                 "Q2_K": (8, 512), "Q3_K": (8, 512), "IQ4_NL": (8, 256), "IQ4_XS": (8, 512)}
 
 # Inputs for the reference's codegen.  Keys are (quant, n, k) -> {nwarps, rows_per_block}.
 CODEGEN_CASES = [

@@ -16,7 +16,8 @@ from oracle import oracle  # noqa: E402
 
 pytestmark = pytest.mark.gpu
 
-TYPES = ["Q4_K", "Q5_K", "Q6_K", "Q8_0", "Q4_0", "Q4_1", "Q5_0", "Q5_1", "Q2_K", "Q3_K"]
+TYPES = ["Q4_K", "Q5_K", "Q6_K", "Q8_0", "Q4_0", "Q4_1", "Q5_0", "Q5_1", "Q2_K", "Q3_K", "IQ4_NL",
+         "IQ4_XS"]
 Y_TOL = 1e-3
 
 

@@ -39,7 +39,8 @@ def test_cpu_safe_entry_points():
     assert lib.anvil_abi_version() == 1
     qk, nb = ctypes.c_int(), ctypes.c_int()
     expect = {2: (32, 18), 3: (32, 20), 6: (32, 22), 7: (32, 24), 8: (32, 34), 9: (32, 36),
-              10: (256, 84), 11: (256, 110), 12: (256, 144), 13: (256, 176), 14: (256, 210)}
+              10: (256, 84), 11: (256, 110), 12: (256, 144), 13: (256, 176), 14: (256, 210),
+              20: (32, 18), 23: (256, 136)}
     for t, (q, b) in expect.items():
         assert lib.anvil_type_geometry(t, ctypes.byref(qk), ctypes.byref(nb)) == 0
         assert (qk.value, nb.value) == (q, b)

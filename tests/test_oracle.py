@@ -13,7 +13,8 @@ import pytest
 from kernel_anvil.quants import QUANT_TYPES, make_activation, make_weights
 from oracle import oracle
 
-TYPES = ["Q4_K", "Q5_K", "Q6_K", "Q8_0", "Q4_0", "Q4_1", "Q5_0", "Q5_1", "Q2_K", "Q3_K"]
+TYPES = ["Q4_K", "Q5_K", "Q6_K", "Q8_0", "Q4_0", "Q4_1", "Q5_0", "Q5_1", "Q2_K", "Q3_K", "IQ4_NL",
+         "IQ4_XS"]
 
 
 @pytest.mark.parametrize("qt", TYPES)
@@ -120,6 +121,15 @@ def test_block_sums_reconstruct_y(qt):
             elif qt in ("Q4_1", "Q5_1"):  # unsigned quants; the min m times d8 * sum(q8)
                 d, m = blk[0:4].copy().view(np.float16).astype(np.float64)
                 y[r] += d * d8[b] * sums[r, b] + m * d8[b] * qsum[b]
+            elif qt == "IQ4_NL":
+                d = blk[0:2].copy().view(np.float16).astype(np.float64)[0]
+                y[r] += d * d8[b] * sums[r, b]
+            elif qt == "IQ4_XS":
+                d = blk[0:2].copy().view(np.float16).astype(np.float64)[0]
+                sh = int(blk[2]) | (int(blk[3]) << 8)
+                for j in range(8):
+                    ls = ((int(blk[4 + j // 2]) >> (4 * (j % 2))) & 15) | (((sh >> (2 * j)) & 3) << 4)
+                    y[r] += d * (ls - 32) * d8[8 * b + j] * sums[r, 8 * b + j]
             elif qt in ("Q2_K", "Q3_K"):
                 # 16 groups of 16 weights; Q2_K: nibble scale and min, Q3_K: 6-bit scale - 32
                 xq16 = xb[:, 4:].view(np.int8).astype(np.int64).reshape(-1, 2, 16).sum(axis=2)
