@@ -278,15 +278,22 @@ constexpr uint32_t kIQ4Levels1 = iq4_word(-49, -35, -22, -10);
 constexpr uint32_t kIQ4Levels2 = iq4_word(1, 13, 25, 38);
 constexpr uint32_t kIQ4Levels3 = iq4_word(53, 69, 89, 113);
 
-// Four 4-bit level indices (one per byte, 0..15) -> their four int8 levels, by two byte
-// permutes over the low and high halves of the table and a per-byte select on bit 3.
-__device__ __forceinline__ uint32_t iq4_levels(uint32_t idx) {
-    const uint32_t sel = (idx & 0x7u) | ((idx >> 4) & 0x70u) | ((idx >> 8) & 0x700u) |
-                         ((idx >> 12) & 0x7000u);
-    const uint32_t lo = __byte_perm(kIQ4Levels0, kIQ4Levels1, sel);
-    const uint32_t hi = __byte_perm(kIQ4Levels2, kIQ4Levels3, sel);
-    const uint32_t m = ((idx >> 3) & 0x01010101u) * 0xFFu;
-    return (hi & m) | (lo & ~m);
+// Levels of four 4-bit indices held as the four nibbles of s (bits 0..15): two byte permutes
+// look each index up in the low and high halves of the table (selector bits 0-2), a third
+// takes byte n from the high-half result where bit 3 of nibble n is set.
+__device__ __forceinline__ uint32_t iq4_levels4(uint32_t s) {
+    const uint32_t lo = __byte_perm(kIQ4Levels0, kIQ4Levels1, s & 0x7777u);
+    const uint32_t hi = __byte_perm(kIQ4Levels2, kIQ4Levels3, s & 0x7777u);
+    return __byte_perm(lo, hi, 0x3210u | ((s & 0x8888u) >> 1));
+}
+
+// The eight level indices packed in one word of quants (byte i: low nibble and high nibble)
+// -> lo: the levels of the four low nibbles, hi: those of the four high nibbles, byte i each.
+__device__ __forceinline__ void iq4_levels8(uint32_t v, uint32_t &lo, uint32_t &hi) {
+    const uint32_t a = iq4_levels4(v & 0xFFFFu);  // bytes 0, 1: (lo, hi, lo, hi)
+    const uint32_t b = iq4_levels4(v >> 16);      // bytes 2, 3
+    lo = __byte_perm(a, b, 0x6420u);
+    hi = __byte_perm(a, b, 0x7531u);
 }
 
 // Q8_1 blocks consumed by unit U of super-block b.
@@ -408,19 +415,14 @@ __device__ __forceinline__ void load_unit(const uint8_t *blk, WBytes &w) {
         lds32_a2(blk + 8 + 32 * U, v);
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-            w.q0[k] = iq4_levels(v[k] & 0x0F0F0F0Fu);
-            w.q0[4 + k] = iq4_levels((v[k] >> 4) & 0x0F0F0F0Fu);
-            w.q1[k] = iq4_levels(v[4 + k] & 0x0F0F0F0Fu);
-            w.q1[4 + k] = iq4_levels((v[4 + k] >> 4) & 0x0F0F0F0Fu);
+            iq4_levels8(v[k], w.q0[k], w.q0[4 + k]);
+            iq4_levels8(v[4 + k], w.q1[k], w.q1[4 + k]);
         }
     } else if constexpr (QT == kTypeIQ4_NL) {
         uint32_t v[4];
         lds16B_a2(blk + 2, v);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            w.q0[k] = iq4_levels(v[k] & 0x0F0F0F0Fu);
-            w.q0[4 + k] = iq4_levels((v[k] >> 4) & 0x0F0F0F0Fu);
-        }
+        for (int k = 0; k < 4; ++k) iq4_levels8(v[k], w.q0[k], w.q0[4 + k]);
     } else if constexpr (QT == kTypeQ2_K || QT == kTypeQ3_K) {
         // weight 64U + 32i + l (i = 0, 1: Q8_1 block kb0, kb1) is bits 2(2(U&1) + i) of qs
         // byte 32(U>>1) + l; Q3_K adds bit 2U + i of hmask[l] as bit 2 (q + 4 when set)
