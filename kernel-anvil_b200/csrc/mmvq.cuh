@@ -192,9 +192,11 @@ __device__ __forceinline__ void lds16B_a2(const uint8_t *p, uint32_t (&w)[4]) {
     }
 }
 
-// Bits 0..3 of h moved to bit 4 of bytes 0..3 (the fifth bit of four 5-bit quants).
+// Bits 0..3 of h moved to bit 4 of bytes 0..3 (the fifth bit of four 5-bit quants): one
+// multiply places copies of h at bits 4, 11, 18 and 25 (they do not overlap, so nothing
+// carries) and the mask keeps bit i of copy i.
 __device__ __forceinline__ uint32_t spread_bit4(uint32_t h) {
-    return ((h & 1u) << 4) | ((h & 2u) << 11) | ((h & 4u) << 18) | ((h & 8u) << 25);
+    return ((h & 0xFu) * 0x02040810u) & 0x10101010u;
 }
 
 __device__ __forceinline__ uint32_t lds16(const uint8_t *p) {
