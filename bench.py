@@ -174,9 +174,18 @@ def cpu_step(gemvs, W, x):
         oracle.mmvq(g.qt, w, xq[g.input], g.nrows, g.K)
 
 
+def use_all_host_threads() -> None:
+    """The oracle's OpenMP team = every core this process may run on.  torchrun sets
+    OMP_NUM_THREADS=1 in its workers, which would otherwise time the CPU leg on one core."""
+    from oracle import oracle
+
+    oracle.set_num_threads(len(os.sched_getaffinity(0)))
+
+
 def cpu_baseline(workload: str, seconds: float) -> dict:
     from oracle import oracle
 
+    use_all_host_threads()
     gemvs, W, x, nbytes, desc = cpu_sample(workload)
     cpu_step(gemvs, W, x)  # warm
     reps, t0 = 0, time.perf_counter()
@@ -196,6 +205,7 @@ def run_reference(args) -> None:
         return
     from oracle import oracle
 
+    use_all_host_threads()
     gemvs, W, x, nbytes, desc = cpu_sample(args.workload)
     for _ in range(args.warmup):
         cpu_step(gemvs, W, x)
