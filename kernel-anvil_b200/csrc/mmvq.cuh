@@ -192,6 +192,21 @@ __device__ __forceinline__ void lds16B_a2(const uint8_t *p, uint32_t (&w)[4]) {
     }
 }
 
+// 32 / 16 bytes at a 4-byte aligned shared-memory address as little-endian words.  Used
+// where the block size keeps the quants word aligned: weights start 16-byte aligned (checked
+// on the host) and every row is a whole number of 84-, 20-, 24- or 136-byte blocks (Q2_K,
+// Q4_1, Q5_1, IQ4_XS), so row, block and quant offsets are multiples of 4.
+__device__ __forceinline__ void lds32_a4(const uint8_t *p, uint32_t (&w)[8]) {
+    const uint32_t *q = reinterpret_cast<const uint32_t *>(p);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) w[k] = q[k];
+}
+__device__ __forceinline__ void lds16B_a4(const uint8_t *p, uint32_t (&w)[4]) {
+    const uint32_t *q = reinterpret_cast<const uint32_t *>(p);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) w[k] = q[k];
+}
+
 // Bits 0..3 of h moved to bit 4 of bytes 0..3 (the fifth bit of four 5-bit quants): one
 // multiply places copies of h at bits 4, 11, 18 and 25 (they do not overlap, so nothing
 // carries) and the mask keeps bit i of copy i.
@@ -414,7 +429,7 @@ __device__ __forceinline__ void load_unit(const uint8_t *blk, WBytes &w) {
         // groups 2U and 2U+1: qs bytes [32U, 32U + 32); within a group byte e holds weight e
         // (low nibble) and weight 16 + e (high nibble)
         uint32_t v[8];
-        lds32_a2(blk + 8 + 32 * U, v);
+        lds32_a4(blk + 8 + 32 * U, v);
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
             iq4_levels8(v[k], w.q0[k], w.q0[4 + k]);
@@ -431,7 +446,11 @@ __device__ __forceinline__ void load_unit(const uint8_t *blk, WBytes &w) {
         constexpr int qs_off = QT == kTypeQ2_K ? 16 : 32;
         constexpr int s0 = 4 * (U & 1);
         uint32_t v[8];
-        lds32_a2(blk + qs_off + 32 * (U >> 1), v);
+        if constexpr (QT == kTypeQ2_K) {
+            lds32_a4(blk + qs_off + 32 * (U >> 1), v);
+        } else {
+            lds32_a2(blk + qs_off + 32 * (U >> 1), v);  // 110-byte blocks: 2-byte aligned
+        }
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
             w.q0[k] = (v[k] >> s0) & 0x03030303u;
@@ -452,7 +471,11 @@ __device__ __forceinline__ void load_unit(const uint8_t *blk, WBytes &w) {
         // qh as bit 4 of weight e (gguf-py quants.py Q4_0..Q5_1 dequantize_blocks)
         constexpr int qs_off = QT == kTypeQ4_0 ? 2 : QT == kTypeQ4_1 ? 4 : QT == kTypeQ5_0 ? 6 : 8;
         uint32_t v[4];
-        lds16B_a2(blk + qs_off, v);
+        if constexpr (QT == kTypeQ4_1 || QT == kTypeQ5_1) {
+            lds16B_a4(blk + qs_off, v);
+        } else {
+            lds16B_a2(blk + qs_off, v);  // 18- and 22-byte blocks: 2-byte aligned
+        }
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
             w.q0[k] = v[k] & 0x0F0F0F0Fu;
