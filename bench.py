@@ -1,36 +1,35 @@
 #!/usr/bin/env python
 """Benchmark of the MMVQ hot path: the per-token quantized-GEMV chain of a decode model.
 
-A "step" is one token's pass over the chain: every distinct input quantised to Q8_1
-and every weight matrix multiplied once (the default workload, qwen3_8b: 253 GEMVs over
-4.51 GB of Q4_K/Q6_K weights, 145 distinct inputs).  Weights are synthetic (seeded, drawn
-on the GPU in GGUF block layout with the workload's value distributions) and far larger
-than L2, so every step streams them from HBM.
+A "step" is one token's pass over the chain: every GEMV input quantised to Q8_1 and every
+weight matrix multiplied once.  The default workload is the Llama-3-70B-shaped Q4_K chain
+(80 layers, 560 GEMVs over 38.5 GB of weights), every matrix row-sharded across the N GPUs
+(N = 1 included: one shard is the whole matrix), run by the persistent executor: one
+cooperative kernel per token per GPU, each group of GEMVs reading the previous group's
+gathered output as it arrives (gate/up pairs as one gate/up GEMV with silu(gate) * up),
+each GPU writing its output rows into every GPU's buffer over NVLink inside the kernel.
+Weights are synthetic (seeded, drawn on the GPU in GGUF block layout with the workload's
+value distributions) and far larger than L2, so every step streams them from HBM.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME]
-                  [--executor persistent|graph] [--impl anvil|reference]
-
-Executors: "graph" replays a CUDA graph of separate quantize + MMVQ launches with
-programmatic dependent launch; "persistent" runs the token as one cooperative kernel (groups
-of GEMVs sharing an input, Q8_1 quantisation inside the kernel, a grid barrier before each
-group that depends on earlier ones).  The default, "auto", takes the graph on one GPU and
-the persistent kernel on several (no collective library in the data path).
+                  [--multi rows|replicas] [--executor persistent|graph] [--impl anvil|reference]
 
 One JSON line is printed by rank 0:
-  value        chain bytes / device time, whole job (GB/s): weights + Q8_1 reads + fp32
-               outputs, timed with CUDA events around K launches, max over ranks
-  e2e          the same metric through the public API with the step's fp32 inputs copied
-               host->device from pinned memory and the logits copied back, every step
-  roofline     the dominant kernel: algorithmic bytes per launch / average launch time
-               measured here with CUDA events, against measured HBM copy bandwidth
+  value        whole-job chain bytes / device time (GB/s): weights of all shards + Q8_1
+               reads + fp32 outputs, timed with CUDA events around K launches, max over ranks
+  e2e          the same metric through the public API with the step's external input (the
+               token's fp32 embedding) copied host->device from pinned memory and the last
+               output copied back, every step
+  roofline     the dominant kernel (the persistent chain kernel: the whole step on each GPU):
+               this GPU's algorithmic bytes per launch / its launch time, against the
+               measured HBM copy bandwidth
   cpu_baseline the CPU oracle (oracle/, all host threads) on a bounded sample of the same
-               workload (layer 0 of the chain), rank 0 at N=1 only
-With N > 1 (torchrun), --multi replicas (default) runs one full chain per GPU on its own
-inputs: independent token streams, no collective in the data path, weak scaling (the
-8B-class workloads fit one GPU).  --multi rows shards every matrix by rows across the GPUs
-(strong scaling): the persistent executor writes each output row into every rank's output
-buffer over NVLink (CUDA IPC peer stores) inside the kernel; the graph executor
-all-gathers each GEMV's output with NCCL inside the CUDA graph.
+               workload (layer 0 of the chain), rank 0 at N=1 only, plus the reference's
+               dependency path (gguf-py dequantize + numpy fp32 matvec) on one matrix
+  extras       (N=1) the single Q4_K 4096 x 4096 GEMV and the Qwen3-8B chain in the same run
+--multi replicas runs one full chain per GPU on its own inputs instead (no collective;
+weak scaling).  --executor graph runs a CUDA graph of quantize + MMVQ launches on fixed
+inputs (with --multi rows, an NCCL all-gather after every GEMV inside the graph).
 --impl reference times the CPU oracle port on the same workload (rank 0 only).
 """
 from __future__ import annotations
@@ -57,9 +56,9 @@ FALLBACK_HBM_GBS = 6650.0
 def parse_args():
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default="qwen3_8b")
+    ap.add_argument("--workload", default="llama3_70b")
     ap.add_argument("--gemvs", type=int, default=0,
                     help="only the workload's first N GEMVs (a smaller case of the same shapes)")
     ap.add_argument("--impl", default="anvil", choices=["anvil", "reference"])
@@ -69,19 +68,26 @@ def parse_args():
                     help="quantise each GEMV input in its own kernel or inside the GEMV (fused)")
     ap.add_argument("--coresident", type=int, default=1,
                     help="graph executor: GEMV kernels sized to share each SM")
-    ap.add_argument("--executor", choices=["auto", "persistent", "graph"], default="auto",
-                    help="one persistent kernel per token, or a CUDA graph of per-GEMV launches "
-                         "(auto: graph on one GPU, persistent with peer stores on several)")
+    ap.add_argument("--executor", choices=["persistent", "graph"], default="persistent",
+                    help="one persistent kernel per token (the chain's data flow inside it), or a "
+                         "CUDA graph of quantize + MMVQ launches on fixed inputs")
+    ap.add_argument("--fixed-inputs", action="store_true",
+                    help="persistent executor: every group reads a fixed synthetic input instead of "
+                         "its producer's output")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the N=1 extra measurements (single 4096^2 GEMV, Qwen3-8B chain)")
+    ap.add_argument("--trace", action="store_true",
+                    help="persistent executor: record per-group timestamps of one extra launch")
     ap.add_argument("--grouped", type=int, default=1,
                     help="graph executor: one launch per run of same-type GEMVs on one input (1) "
                          "quantising in the kernel, or one launch per GEMV (0)")
     ap.add_argument("--glu", type=int, default=0,
                     help="grouped graph executor: each layer's ffn_gate/ffn_up pair as one launch "
                          "with silu(gate) * up in the epilogue (1), or as a grouped GEMV pair (0)")
-    ap.add_argument("--multi", choices=["replicas", "rows"], default="replicas",
-                    help="N > 1: one full chain per GPU (independent token streams, no collective; "
-                         "weak scaling) or every matrix row-sharded across the GPUs with the outputs "
-                         "exchanged (strong scaling)")
+    ap.add_argument("--multi", choices=["replicas", "rows"], default="rows",
+                    help="every matrix row-sharded across the GPUs with the outputs exchanged (strong "
+                         "scaling), or one full chain per GPU on its own inputs (no collective; weak "
+                         "scaling)")
     ap.add_argument("--nwarps", type=int, default=0, help="persistent executor: warps per CTA (0 = 8)")
     ap.add_argument("--ctas-per-sm", type=int, default=0, help="persistent executor: CTAs per SM (0 = 1)")
     return ap.parse_args()
@@ -199,6 +205,43 @@ def cpu_baseline(workload: str, seconds: float) -> dict:
             "kind": "port", "sample": f"{desc}; {reps} passes in {dt:.1f} s"}
 
 
+def reference_dependency(workload: str, seconds: float = 4.0) -> dict:
+    """The reference's dependency path on one matrix of the workload: gguf-py (gguf 0.19.0,
+    kernel-anvil pyproject.toml:19) gguf.quants.dequantize of the GGUF blocks, then a numpy
+    fp32 matvec with the Q8_1-dequantised activation.  Single-threaded numpy, as it runs."""
+    import numpy as np
+    from gguf import GGMLQuantizationType
+    from gguf.quants import dequantize
+
+    from kernel_anvil.chains import get_chain
+    from kernel_anvil.quants import gemv_bytes, make_activation, make_weights
+    from oracle import oracle
+
+    spec = get_chain(workload)
+    g = next((g for g in spec.gemvs if g.name.endswith("attn_k")), spec.gemvs[0])
+    W = make_weights(g.qt, g.nrows, g.K, seed=1)
+    x = oracle.dequantize_q8_1(oracle.quantize_q8_1(make_activation(g.K, seed=2)), g.K)[0]
+    qtype = getattr(GGMLQuantizationType, g.qt)
+
+    def one():
+        Wf = dequantize(W.reshape(-1), qtype).reshape(g.nrows, g.K)
+        return Wf @ x
+
+    one()
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        one()
+        reps += 1
+        dt = time.perf_counter() - t0
+        if dt >= seconds:
+            break
+    nbytes = gemv_bytes(g.qt, g.nrows, g.K)
+    return {"value": round(nbytes * reps / dt / 1e9, 4), "unit": "GB/s", "cores": 1,
+            "kind": "reference-dependency",
+            "sample": f"{g.name} ({g.qt} {g.nrows}x{g.K}): gguf.quants.dequantize + numpy fp32 matvec, "
+                      f"{reps} passes in {dt:.1f} s"}
+
+
 def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -245,8 +288,9 @@ def time_graph(launch, stream, steps: int) -> float:
 
 
 def dominant_kernel(dc, stream, steps: int, warmup: int) -> dict:
-    """The Q4_K MMVQ launches of one chain step, launched as in the chain (one launch per
-    run of Q4_K GEMVs on one input when grouped) and replayed as their own PDL graph."""
+    """Graph executor: the Q4_K MMVQ launches of one chain step, launched as in the chain (one
+    launch per run of Q4_K GEMVs on one input when grouped) and replayed as their own PDL
+    graph."""
     import torch
 
     from kernel_anvil.chains import is_gate_up
@@ -286,17 +330,91 @@ def dominant_kernel(dc, stream, steps: int, warmup: int) -> dict:
     return {"launches_per_step": n, "bytes_per_launch": nbytes / n, "ms_per_launch": ms / n}
 
 
-def traffic_per_launch(kernel: str) -> float | None:
-    """dram read+write bytes per launch of `kernel` from the committed ncu summaries (a line
-    `<kernel> dram_bytes_per_launch: N`); None when not captured."""
+def traffic_per_launch(kernel: str) -> tuple[float | None, str | None]:
+    """DRAM read+write bytes per launch of `kernel` from the committed ncu summaries (a line
+    `<kernel> dram_bytes_per_launch: N` with a following `<kernel> traffic_source: ...`);
+    (None, None) when not captured."""
+    val, src = None, None
     for p in sorted((ROOT / "profiles").glob("*.md")):
         try:
             for line in p.read_text().splitlines():
                 if line.startswith(f"{kernel} dram_bytes_per_launch:"):
-                    return float(line.split(":", 1)[1])
+                    val = float(line.split(":", 1)[1])
+                    src = f"profiles/{p.name}"
+                elif line.startswith(f"{kernel} traffic_source:") and val is not None:
+                    src = f"profiles/{p.name}: " + line.split(":", 1)[1].strip()
         except OSError:
             pass
-    return None
+        if val is not None:
+            return val, src
+    return None, None
+
+
+def extra_config0(hbm_peak: float) -> dict:
+    """The single Q4_K GEMV of N = K = 4096 (9,458,176 algorithmic bytes): per-GEMV time over
+    a rotation of distinct weight copies (more bytes than L2), three ways: separate launches
+    in a CUDA graph, the same with programmatic dependent launch, and 64 independent GEMVs
+    run by one persistent kernel."""
+    import torch
+
+    from kernel_anvil.pchain import PersistentChain
+    from kernel_anvil.verify import GemvBench
+
+    out = {"shape": "Q4_K 4096x4096, 1 column", "bytes": None}
+    for pdl in (False, True):
+        b = GemvBench("Q4_K", 4096, 4096, pdl=pdl)
+        us = b.time(warmup=64, runs=640)
+        out["bytes"] = b.bytes
+        out["pdl_launches_us" if pdl else "launches_us"] = round(us, 3)
+        if not pdl:
+            copies, W, x = b.copies, list(b.W), b.x
+        b.close()
+    pc = PersistentChain()
+    for i in range(copies):
+        pc.add_group(x)
+        pc.add_gemv(W[i], "Q4_K", nrows=4096)
+    pc.instantiate()
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            pc.launch(stream)
+        ms = time_graph(lambda: pc.launch(stream), stream, 20)
+    pc.close()
+    out["persistent_us"] = round(ms * 1e3 / copies, 3)
+    out["gemvs_per_persistent_launch"] = copies
+    for k in ("launches_us", "pdl_launches_us", "persistent_us"):
+        gbs = out["bytes"] / (out[k] * 1e-6) / 1e9
+        out[k.replace("_us", "_gbs")] = round(gbs, 1)
+        out[k.replace("_us", "_pct_of_hbm_peak")] = round(100 * gbs / hbm_peak, 1)
+        out[k.replace("_us", "_pct_of_8TBps")] = round(100 * gbs / 8000, 1)
+    out["l2"] = f"{copies} distinct weight copies per rotation ({copies * 9437184 / 1e6:.0f} MB > L2)"
+    return out
+
+
+def extra_qwen3_8b(stream, steps: int, warmup: int) -> dict:
+    """Config 1, the Qwen3-8B chain on this GPU: the persistent dataflow executor and the
+    CUDA graph of grouped quantize + MMVQ launches on fixed inputs."""
+    import torch
+
+    from kernel_anvil.chains import DeviceChain, get_chain
+
+    spec = get_chain("qwen3_8b")
+    res = {"gemvs_per_step": len(spec.gemvs)}
+    for name, kw in (("persistent_dataflow", {"executor": "persistent"}),
+                     ("graph_fixed_inputs", {"executor": "graph", "grouped": True})):
+        dc = DeviceChain(spec, **kw)
+        with torch.cuda.stream(stream):
+            dc.instantiate(pdl=True)
+            for _ in range(max(warmup, 3)):
+                dc.launch()
+            ms = time_graph(dc.launch, stream, steps)
+        nbytes = spec.glu_algorithmic_bytes() if dc.pchain else spec.algorithmic_bytes()
+        res[name] = {"us_per_token": round(ms * 1e3, 1), "gbs": round(nbytes / (ms * 1e-3) / 1e9, 1),
+                     "launches_per_step": dc.launches_per_step}
+        dc.close()
+        del dc
+        torch.cuda.empty_cache()
+    return res
 
 
 def run_anvil(args) -> None:
@@ -305,6 +423,7 @@ def run_anvil(args) -> None:
 
     from kernel_anvil import mmvq as ops
     from kernel_anvil.chains import DeviceChain, get_chain
+    from kernel_anvil.pchain import take_status
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -320,28 +439,26 @@ def run_anvil(args) -> None:
     spec = get_chain(args.workload)
     if args.gemvs:
         spec = spec.head(args.gemvs)
-    shard = world > 1 and args.multi == "rows"
-    if args.executor == "auto":
-        args.executor = "persistent" if shard else "graph"
+    shard = args.multi == "rows"
     persistent = args.executor == "persistent"
     # replicas: every rank runs the whole chain on its own inputs (seeded per rank)
     dc = DeviceChain(spec, rank=rank if shard else 0, world=world if shard else 1, device=dev,
                      seed=0 if shard else rank, fused=args.quantize == "fused",
                      coresident=args.coresident, executor=args.executor,
-                     dist=dist if shard else None, nwarps=args.nwarps,
+                     dist=dist if shard and world > 1 else None, nwarps=args.nwarps,
                      ctas_per_sm=args.ctas_per_sm, grouped=bool(args.grouped) and not persistent,
-                     glu=bool(args.glu))
+                     glu=bool(args.glu), dataflow=not args.fixed_inputs)
     stream = torch.cuda.Stream(device=dev)
     hbm_peak, peak_kind = measured_peaks()
-    # whole job (gate/up launches write one vector per pair: the chain's own count)
-    total_bytes = ((dc.algorithmic_bytes if dc.glu else spec.algorithmic_bytes())
-                   * (1 if shard or world == 1 else world))
-    rank_bytes = dc.algorithmic_bytes       # this rank's shard
+    # whole job: the unsharded chain once (shards), or every replica's chain
+    one_chain = spec.glu_algorithmic_bytes() if (persistent or dc.glu) else spec.algorithmic_bytes()
+    total_bytes = one_chain * (1 if shard else world)
+    rank_bytes = dc.algorithmic_bytes       # this rank's launches
 
     graph = None
     launches_per_step = dc.launches_per_step
     n_quantize = dc.chain.n_quantize if dc.chain else 0
-    if not shard or persistent:
+    if persistent or not (shard and world > 1):
         with torch.cuda.stream(stream):
             dc.instantiate(pdl=True)
         launch = dc.launch
@@ -379,16 +496,40 @@ def run_anvil(args) -> None:
         ms = float(t.item())
     value = total_bytes / (ms * 1e-3) / 1e9
 
-    # ---- end to end: host inputs in, logits out, every step --------------------------------
-    h_in = torch.empty(dc.x_all.numel(), dtype=torch.float32, pin_memory=True)
-    h_in.copy_(dc.x_all.cpu())
-    logits = dc.outputs[-1]
-    h_out = torch.empty(logits.numel(), dtype=torch.float32, pin_memory=True)
+    # ---- per-group trace of one more launch (persistent executor) ----------------------------
+    trace = None
+    if persistent and args.trace:
+        from kernel_anvil.pchain import trace_summary
+        tbuf = dc.pchain.enable_trace()
+        with torch.cuda.stream(stream):
+            launch()
+        stream.synchronize()
+        trace = trace_summary(tbuf)
+        barrier()
+
+    # ---- end to end: host input in, last output out, every step -----------------------------
+    ext = dc.external_inputs
+    xin = [dc.x[a] for a in ext]
+    h_in = [torch.empty(x.numel(), dtype=torch.float32, pin_memory=True) for x in xin]
+    for h, x in zip(h_in, xin):
+        h.copy_(x.reshape(-1).cpu())
+    if persistent:
+        last = torch.empty((dc.ncols, spec.gemvs[-1].nrows), dtype=torch.float32, device=dev)
+
+        def read_last():
+            return dc.pchain.output(dc.pidx[-1], out=last, stream=stream)
+    else:
+        last = dc.outputs[-1]
+
+        def read_last():
+            return last
+    h_out = torch.empty(last.numel(), dtype=torch.float32, pin_memory=True)
 
     def e2e_step():
-        dc.x_all.copy_(h_in, non_blocking=True)
+        for h, x in zip(h_in, xin):
+            x.view(-1).copy_(h, non_blocking=True)
         launch()
-        h_out.copy_(logits.view(-1), non_blocking=True)
+        h_out.copy_(read_last().view(-1), non_blocking=True)
 
     with torch.cuda.stream(stream):
         for _ in range(2):
@@ -403,28 +544,28 @@ def run_anvil(args) -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms_e2e = float(t.item())
     e2e = {"value": round(total_bytes / (ms_e2e * 1e-3) / 1e9, 2), "unit": "GB/s",
-           "h2d_bytes_per_step": h_in.numel() * 4, "d2h_bytes_per_step": h_out.numel() * 4,
-           "ms_per_step": round(ms_e2e, 4)}
+           "h2d_bytes_per_step": sum(h.numel() for h in h_in) * 4, "d2h_bytes_per_step": h_out.numel() * 4,
+           "ms_per_step": round(ms_e2e, 4), "us_per_token": round(ms_e2e * 1e3, 1)}
 
     # ---- dominant kernel roofline -----------------------------------------------------------
     peak_source = (f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                    else "fallback 6.65 TB/s")
     if persistent:
-        # one launch per token: the kernel is the step; this rank's bytes over its time
+        # one launch per token: the kernel is the step; this rank's bytes over its own time
         achieved = rank_bytes / (ms_rank * 1e-3) / 1e9
+        traffic, tsrc = traffic_per_launch(f"pchain_kernel {args.workload} x{world}")
         roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
-                    "frac": round(achieved / hbm_peak, 4),
-                    "traffic": traffic_per_launch(f"pchain_kernel {args.workload}"),
+                    "frac": round(achieved / hbm_peak, 4), "traffic": traffic, "traffic_source": tsrc,
                     "peak_source": peak_source,
-                    "kernel": f"pchain_kernel<ncols={dc.ncols}> (whole token, one cooperative launch)",
+                    "kernel": f"pchain_kernel<ncols={dc.ncols}> (whole token, one cooperative launch per GPU)",
                     "launches_per_step": 1, "bytes_per_launch": rank_bytes,
                     "us_per_launch": round(ms_rank * 1e3, 3)}
     else:
         dk = dominant_kernel(dc, stream, args.steps, args.warmup)
         achieved = dk["bytes_per_launch"] / (dk["ms_per_launch"] * 1e-3) / 1e9
+        traffic, tsrc = traffic_per_launch(f"mmvq_kernel {args.workload}")
         roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
-                    "frac": round(achieved / hbm_peak, 4),
-                    "traffic": traffic_per_launch(f"mmvq_kernel {args.workload}"),
+                    "frac": round(achieved / hbm_peak, 4), "traffic": traffic, "traffic_source": tsrc,
                     "peak_source": peak_source,
                     "kernel": "mmvq_kernel<Q4_K, ncols=1> (all Q4_K launches of one step, PDL graph)",
                     "launches_per_step": dk["launches_per_step"],
@@ -432,57 +573,80 @@ def run_anvil(args) -> None:
                     "us_per_launch": round(dk["ms_per_launch"] * 1e3, 3)}
 
     status = ops.take_device_status()
-    pinfo, n_groups = None, 0
+    pinfo, n_groups, dataflow = None, 0, dc.dataflow
     if persistent:
-        from kernel_anvil.pchain import take_status
         status |= take_status()
         pinfo = dc.pchain.info()
-        n_groups = dc.pchain.n_groups
+        n_groups = pinfo["groups"]
     if graph is not None:
         # the graph holds NCCL work: release it before the process group goes away
         launch = e2e_step = None
         graph.reset()
         del graph
     dc.close()
+    del dc
+    torch.cuda.empty_cache()
+
+    extras = {}
+    if world == 1 and not args.no_extras:
+        extras["config0_single_gemv"] = extra_config0(hbm_peak)
+        extras["config1_qwen3_8b_chain"] = extra_qwen3_8b(stream, args.steps, args.warmup)
+        status |= ops.take_device_status() | take_status()
+
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
         return
+    if shard:
+        parallelism = (f"row-shard x{world}: " + (
+            "outputs written to every rank over NVLink (CUDA IPC peer stores of flagged words) inside "
+            "the kernel" if persistent else "NCCL all-gather after every GEMV") if world > 1
+            else "single GPU (one shard)")
+    else:
+        parallelism = (f"{world} replicas: one full chain per GPU on its own inputs, no collective in "
+                       "the data path" if world > 1 else "single GPU")
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
-        "higher_is_better": True, "scaling": "strong" if shard or world == 1 else "weak",
+        "higher_is_better": True, "scaling": "strong" if shard else "weak",
         "vs_baseline": None,
         "dtype": "int8 dp4a / fp32", "data": "synthetic",
         "config": {"workload": f"{args.workload} per-token GEMV chain",
                    "gemvs_per_step": len(spec.gemvs),
+                   "groups_per_step": n_groups if persistent else None,
                    "quantizations_per_step": n_groups if persistent else n_quantize,
                    "bytes_per_step": total_bytes, "weight_bytes": spec.weight_bytes(),
                    "us_per_token": round(ms * 1e3, 1), "pct_of_hbm_peak": round(100 * value / hbm_peak, 1),
                    "pct_of_8TBps": round(100 * value / 8000.0, 1),
                    "l2": "inputs larger than L2 (weights stream from HBM every step)",
-                   "parallelism": ((f"row-shard x{world}, " + ("outputs written to every rank over NVLink "
-                                    "(CUDA IPC peer stores) inside the kernel" if persistent else
-                                    "NCCL all-gather per GEMV")) if shard else
-                                   f"{world} replicas: one full chain per GPU on its own inputs, no "
-                                   "collective in the data path" if world > 1 else "single GPU"),
+                   "parallelism": parallelism,
                    "executor": ("one persistent cooperative kernel per token: groups of GEMVs sharing an "
-                                "input, Q8_1 quantisation in-kernel, grid barrier between dependent groups"
+                                "input, Q8_1 quantisation in-kernel, "
+                                + ("each group reading its producer's output as it arrives (flagged words)"
+                                   if dataflow else "fixed inputs")
                                 if persistent else
-                                "CUDA graph of quantize + MMVQ launches, programmatic dependent launch"),
-                   "quantize": "in-kernel per group" if persistent else args.quantize,
-                   "grouped_launches": bool(args.grouped) and not persistent,
-                   "gate_up_glu": dc.glu,
+                                "CUDA graph of quantize + MMVQ launches on fixed inputs, programmatic "
+                                "dependent launch"),
+                   "gate_up": "one gate/up GEMV per pair, silu(gate) * up" if persistent or args.glu
+                              else "grouped gate and up GEMVs",
                    **({"persistent": pinfo} if persistent else
-                      {"coresident_kernels_per_sm": args.coresident})},
+                      {"coresident_kernels_per_sm": args.coresident, "grouped_launches": bool(args.grouped)})},
         "e2e": e2e, "roofline": roofline, "gpu_launches": launches_per_step * args.steps,
         "device_status": status,
     }
+    if trace is not None:
+        line["trace"] = trace
+    if extras:
+        line["extras"] = extras
     if clk is not None:
         line["clocks"] = clk
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args.workload, args.cpu_seconds)
+        try:
+            line["cpu_baseline"]["reference_dependency"] = reference_dependency(args.workload)
+        except ImportError as e:  # gguf-py missing on the host
+            line["cpu_baseline"]["reference_dependency"] = {"unavailable": str(e)}
     print(json.dumps(line), flush=True)
 
 

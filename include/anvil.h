@@ -44,7 +44,7 @@ extern "C" {
 /* Same type as cudaStream_t / CUstream, declared without the CUDA headers. */
 typedef struct CUstream_st *anvil_stream_t;
 
-#define ANVIL_ABI_VERSION 1
+#define ANVIL_ABI_VERSION 2
 
 enum anvil_status {
     ANVIL_OK = 0,
@@ -144,10 +144,11 @@ int anvil_mmvq_f32_ex(int ggml_type, const void *W, const float *x, void *xq, fl
  * device budget reserved before the first token; cudaFree synchronising the device).
  * Limit: ncols_dst * (ncols_x/32) * 36 <= 1048576 bytes (K <= 932064 for one column,
  * 116480 for eight), else ANVIL_ERR_INVALID and nothing is launched.  Set-up: the first
- * call on each device (that device current) looks the buffer's address up with
- * cudaGetSymbolAddress; make it outside any stream capture.  The buffer needs no zeroing.
- * All calls on a device share it: calls whose launches overlap (unordered streams,
- * several threads) race, so order them. */
+ * call in each CUDA context (that device current) looks the buffer's address up with
+ * cudaGetSymbolAddress and keeps it keyed by the context's id, so a call after
+ * cudaDeviceReset looks it up again; make the first call outside any stream capture.  The
+ * buffer needs no zeroing.  All calls on a device share it: calls whose launches overlap
+ * (unordered streams, several threads) race, so order them. */
 int anvil_mmvq_f32_noalloc(int ggml_type, const void *W, const float *x, float *y, int nrows,
                            int ncols_x, int ncols_dst, int nwarps, int rows_per_block,
                            anvil_stream_t stream);
@@ -253,49 +254,86 @@ int anvil_chain_num_steps(const anvil_chain *chain);
 
 /* ---- persistent chain: one cooperative launch per token ------------------ */
 
-/* The same per-token GEMV sequence as anvil_chain, run by one persistent kernel.  No
- * counterpart kernel in the reference (its chain is a stream of separate mul_mat_vec_q
- * launches, docs/decode-pipeline-breakdown.md:20-21); each GEMV computes exactly what
- * anvil_mmvq computes for its rows.
+/* The per-token GEMV sequence of a decoder run by one persistent kernel, on one GPU or
+ * row-sharded across several.  No counterpart kernel in the reference (its chain is a
+ * stream of separate quantize_q8_1 + mul_mat_vec_q launches,
+ * docs/decode-pipeline-breakdown.md:20-21); each GEMV computes what anvil_mmvq computes for
+ * its rows, on the input its group stages.
  *
- * Groups: GEMVs added after anvil_pchain_add_group read that group's fp32 input x
- * (ncols x K, 16-byte aligned), which every CTA quantises to Q8_1 itself with the
- * arithmetic of anvil_quantize_q8_1.  wait_prev = 1 makes the group wait until every
- * GEMV before it has finished (a grid barrier; 0 = independent, e.g. k after q).
- * The weight stream runs ahead across groups.
+ * Groups: GEMVs added after a group read that group's input, which every CTA quantises to
+ * Q8_1 itself with the arithmetic of anvil_quantize_q8_1.  anvil_pchain_add_group: a fixed
+ * fp32 input x (ncols x K, 16-byte aligned).  anvil_pchain_add_group_chained: the output of
+ * an earlier GEMV of the chain (K = its nrows_full, a multiple of 32), quantised to the Q8_1
+ * quants of anvil_quantize_q8_1 with d8 kept in fp32 (not rounded to fp16), and the group's
+ * results multiplied by 2^-e, e the exponent of the input column's largest magnitude (so
+ * values stay in range along a chain of any length).  A chained group waits, per value and
+ * bounded, only for the words it reads; there is no grid barrier.
  *
- * Ranks: world > 1 row-shards every matrix.  Rank r passes its rows [row0, row0 + nrows)
- * of an nrows_full-row matrix, and y[q] = rank q's full output buffer (ncols x
- * nrows_full, reachable from this GPU: a peer mapping from anvil_ipc_open); each output
- * row ends up in all ranks' buffers (this rank's copy first, the peers' at the end of the
- * group).  counters[q] = rank q's array of at least 2 x (number of groups) zeroed uint32
- * words, the same layout on every rank; every rank must
- * build the same groups with the same nwarps / ctas_per_sm.  With world = 1, y[0] is the
- * output and counters are allocated by the chain unless set.
+ * Outputs: every value is one 8-byte word {fp32 value (low half), uint32 epoch (high half)}
+ * written with one 64-bit store; the epoch is the launch number (1, 2, ...).  A GEMV's buffer
+ * holds two epochs: words [(epoch & 1) * ncols + c] * nrows_full + pos, pos = the row, or for
+ * a chained source the row's position in 512-value blocks (anvil_pchain_read_output returns
+ * rows in order).  y[q] = rank q's buffer for this GEMV (2 * ncols * nrows_full words,
+ * zeroed, 16-byte aligned; a peer mapping from anvil_ipc_open for q != rank); with world = 1
+ * y may be NULL and the chain allocates it.  Ranks: world > 1 row-shards every matrix; rank
+ * r passes its rows [row0, row0 + nrows) of an nrows_full-row matrix, and writes each of its
+ * output rows into every rank's buffer.  Every rank builds the same chain and launches it the
+ * same number of times.
  *
- * Every wait in the kernel is bounded (2 s); one that gives up sets a flag read by
- * anvil_pchain_take_status (2 = barrier, 1 = weight copy) and the chain must be rebuilt. */
+ * Every wait in the kernel is bounded (anvil_set_wait_limit_ns, default 2 s); one that gives
+ * up sets a flag read by anvil_pchain_take_status (2 = an input word did not arrive, 1 = a
+ * weight copy did not land), later waits of the launch end at once, and the launch's
+ * outputs are then wrong. */
 #define ANVIL_MAX_RANKS 8
 typedef struct anvil_pchain anvil_pchain;
 
 anvil_pchain *anvil_pchain_create(int world, int rank);
 void anvil_pchain_destroy(anvil_pchain *chain);
-int anvil_pchain_add_group(anvil_pchain *chain, const float *x, int K, int ncols, int wait_prev);
-/* rows_per_block: rows per weight tile (0 = built-in default); lanes per row are chosen
- * to keep the most lanes busy (read back with anvil_pchain_gemv_shape). */
+/* Both return the new group's index (>= 0) or a negative status.  A GEMV whose weight family
+ * differs from the group's (Q8_0 against the K-quants) continues in a new group on the same
+ * input. */
+int anvil_pchain_add_group(anvil_pchain *chain, const float *x, int K, int ncols);
+int anvil_pchain_add_group_chained(anvil_pchain *chain, int src_gemv);
+/* A GEMV of the current group; returns its index (>= 0) or a negative status.
+ * rows_per_block: rows per weight tile (0 = built-in default); lanes per row are chosen to
+ * keep the most lanes busy (read back with anvil_pchain_gemv_shape). */
 int anvil_pchain_add_gemv(anvil_pchain *chain, int ggml_type, const void *W, int nrows, int row0,
-                          int nrows_full, float *const *y, int rows_per_block);
-int anvil_pchain_set_counters(anvil_pchain *chain, uint32_t *const *counters);
+                          int nrows_full, uint64_t *const *y, int rows_per_block);
+/* A gate/up pair of the current group (anvil_mmvq_glu's arithmetic): output row r is
+ * silu(W_gate[r] . x) * (W_up[r] . x); both matrices hold the same rows, which must be a
+ * multiple of 16 bytes.  rows_per_block counts rows of one matrix.  Returns the index. */
+int anvil_pchain_add_glu(anvil_pchain *chain, int ggml_type, const void *W_gate, const void *W_up,
+                         int nrows, int row0, int nrows_full, uint64_t *const *y,
+                         int rows_per_block);
+/* Parity probe: the staged activation of group `group` ({fp32 d8, 32 quants} per 32 values,
+ * ncols * K/32 blocks of 36 bytes) is written to `out` by the first CTA. */
+int anvil_pchain_set_group_dump(anvil_pchain *chain, int group, void *out);
 /* nwarps per CTA (0 = 8), CTAs per SM (0 = 1); allocates the device descriptors. */
 int anvil_pchain_instantiate(anvil_pchain *chain, int nwarps, int ctas_per_sm);
+/* Optional timestamps: buf holds grid * ngroups * 4 words; for each CTA and group,
+ * %globaltimer when its warp 0 starts and ends its share of the group's staging, when the
+ * CTA's barrier after the staging is passed, and when warp 0's tiles of the group are done. */
+int anvil_pchain_set_trace(anvil_pchain *chain, uint64_t *buf);
 /* One token: a cooperative launch on `stream`.  Not for stream capture. */
 int anvil_pchain_launch(anvil_pchain *chain, anvil_stream_t stream);
+/* Epoch of the last launch (0 before the first). */
+int anvil_pchain_epoch(const anvil_pchain *chain);
+/* The last launch's output of GEMV `index` on this rank, ncols x nrows_full fp32 in row
+ * order, into dst (device); NaN where a word does not carry the last epoch. */
+int anvil_pchain_read_output(const anvil_pchain *chain, int index, float *dst,
+                             anvil_stream_t stream);
 int anvil_pchain_info(const anvil_pchain *chain, int *grid, int *nwarps, int *ring_bytes,
                       int *smem_bytes, int *ngroups);
 int anvil_pchain_gemv_shape(const anvil_pchain *chain, int index, int *rows_per_block,
                             int *lanes_per_row);
 /* Reads and clears the persistent kernel's device status flags (current device). */
 int anvil_pchain_take_status(void);
+
+/* Bound on every device-side wait (mbarrier waits of the MMVQ kernels, the persistent
+ * chain's input and weight waits) of launches made from now on; 0 restores the default 2 s.
+ * At most 60 s.  No counterpart in the reference (its kernels have no waits). */
+int anvil_set_wait_limit_ns(unsigned long long ns);
+unsigned long long anvil_get_wait_limit_ns(void);
 
 /* Device buffers shared between the ranks' processes (CUDA IPC): allocate (zeroed) and
  * export a 64-byte handle; open a peer's handle into this process; close; free. */

@@ -1,6 +1,7 @@
 // anvil_abi.cu -- extern "C" entry points of libanvil.so (declared in include/anvil.h):
 // argument checks, launch planning, the Q8_1 quantiser kernel, programmatic dependent
 // launch, and the CUDA-graph chain executor.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -87,6 +88,10 @@ struct DeviceInfo {
     std::atomic<int> sm_count{0};
 };
 static DeviceInfo g_dev[kMaxDevices];
+
+static std::atomic<unsigned long long> g_wait_limit_ns{kWaitLimitNs};
+
+unsigned long long wait_limit_ns() { return g_wait_limit_ns.load(std::memory_order_relaxed); }
 
 static std::mutex g_cache_mu;
 struct FnKey {
@@ -340,6 +345,7 @@ static int launch_segs_one(const Plan &p, const Segs &sg, const void *x, int32_t
     MmvqArgs a;
     a.x = x;
     a.sums = sums;
+    a.wait_ns = wait_limit_ns();
     a.K = K;
     a.nstages = p.nstages;
     a.nseg = sg.n;
@@ -412,6 +418,7 @@ static int launch_glu(const Plan &p, const void *Wg, const void *Wu, const void 
     MmvqArgs a = {};
     a.x = xq;
     a.sums = nullptr;
+    a.wait_ns = wait_limit_ns();
     a.K = K;
     a.nstages = p.nstages;
     a.nseg = 1;
@@ -528,6 +535,14 @@ struct anvil_chain {
 extern "C" {
 
 int anvil_abi_version(void) { return ANVIL_ABI_VERSION; }
+
+int anvil_set_wait_limit_ns(unsigned long long ns) {
+    if (ns > 60ull * 1000000000ull) return fail(ANVIL_ERR_INVALID, "wait limit %llu ns above 60 s", ns);
+    g_wait_limit_ns.store(ns ? ns : kWaitLimitNs, std::memory_order_relaxed);
+    return ANVIL_OK;
+}
+
+unsigned long long anvil_get_wait_limit_ns(void) { return wait_limit_ns(); }
 
 const char *anvil_last_error(void) { return t_last_error.c_str(); }
 
@@ -995,12 +1010,14 @@ int anvil_chain_launch(anvil_chain *c, anvil_stream_t stream) {
 // cudaMalloc can fail or fragment what is left), and hosts on a latency-critical path,
 // where cudaFree would synchronise the whole device.
 //
-// Set-up: the first call on each device, with that device current, looks the buffer's
-// device address up with cudaGetSymbolAddress and keeps it; make that first call outside
-// any stream capture.  Nothing in the buffer has to start at zero: the quantiser writes
-// every byte the GEMV then reads.  All calls on one device share the buffer, so calls
-// whose launches overlap (different streams without ordering between them, or several
-// host threads) race on it: order them on one stream or with events.
+// Set-up: the first call in each CUDA context (one per device unless a context is reset),
+// with that device current, looks the buffer's device address up with cudaGetSymbolAddress
+// and keeps it, keyed by the context's unique id; make that first call outside any stream
+// capture.  After cudaDeviceReset the next call finds a new context id and looks the address
+// up again.  Nothing in the buffer has to start at zero: the quantiser writes every byte the
+// GEMV then reads.  All calls on one device share the buffer, so calls whose launches
+// overlap (different streams without ordering between them, or several host threads) race
+// on it: order them on one stream or with events.
 // ---------------------------------------------------------------------------------
 namespace anvil {
 
@@ -1008,20 +1025,60 @@ namespace anvil {
 // 116,480 for eight.
 constexpr size_t kStaticXqBytes = size_t(1) << 20;
 static __device__ __align__(256) uint8_t g_static_xq[kStaticXqBytes];
-static void *g_static_xq_addr[kMaxDevices];  // device address of g_static_xq, per device
+
+struct StaticXqEntry {
+    unsigned long long ctx_id;  // 0: not looked up yet
+    void *addr;
+};
+static StaticXqEntry g_static_xq_addr[kMaxDevices];  // device address of g_static_xq, per device
 static std::mutex g_static_xq_mu;
 
-// Device address of g_static_xq on `dev` (which must be the current device), looked up
-// once per device.
+// Unique id of the calling thread's current context (driver API cuCtxGetCurrent + cuCtxGetId,
+// reached through the runtime's entry-point table, so no link against libcuda).
+static int current_context_id(unsigned long long *id) {
+    using GetCurrent = CUresult (*)(CUcontext *);
+    using GetId = CUresult (*)(CUcontext, unsigned long long *);
+    static GetCurrent get_current = nullptr;
+    static GetId get_id = nullptr;
+    if (!get_current || !get_id) {
+        void *a = nullptr, *b = nullptr;
+        cudaDriverEntryPointQueryResult qa, qb;
+        cudaError_t e = cudaGetDriverEntryPoint("cuCtxGetCurrent", &a, cudaEnableDefault, &qa);
+        if (e == cudaSuccess) e = cudaGetDriverEntryPoint("cuCtxGetId", &b, cudaEnableDefault, &qb);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaGetDriverEntryPoint");
+        if (qa != cudaDriverEntryPointSuccess || qb != cudaDriverEntryPointSuccess || !a || !b)
+            return fail(ANVIL_ERR_UNSUPPORTED, "driver lacks cuCtxGetCurrent / cuCtxGetId");
+        get_current = reinterpret_cast<GetCurrent>(a);
+        get_id = reinterpret_cast<GetId>(b);
+    }
+    CUcontext ctx = nullptr;
+    if (get_current(&ctx) != CUDA_SUCCESS || !ctx)
+        return fail(ANVIL_ERR_CUDA, "no current CUDA context");
+    if (get_id(ctx, id) != CUDA_SUCCESS) return fail(ANVIL_ERR_CUDA, "cuCtxGetId failed");
+    return ANVIL_OK;
+}
+
+// Device address of g_static_xq on `dev` (which must be the current device), looked up once
+// per context.
 static int static_xq_addr(int dev, void **out) {
     std::lock_guard<std::mutex> lock(g_static_xq_mu);
-    if (!g_static_xq_addr[dev]) {
-        void *ptr = nullptr;
+    // a runtime call first, so the device's primary context exists and is current
+    void *ptr = nullptr;
+    unsigned long long id = 0;
+    if (!g_static_xq_addr[dev].ctx_id) {
         const cudaError_t e = cudaGetSymbolAddress((void **)&ptr, g_static_xq);
         if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_static_xq)");
-        g_static_xq_addr[dev] = ptr;
+        if (int s = current_context_id(&id)) return s;
+        g_static_xq_addr[dev] = {id, ptr};
+    } else {
+        if (int s = current_context_id(&id)) return s;
+        if (id != g_static_xq_addr[dev].ctx_id) {  // the context was reset: look up again
+            const cudaError_t e = cudaGetSymbolAddress((void **)&ptr, g_static_xq);
+            if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_static_xq)");
+            g_static_xq_addr[dev] = {id, ptr};
+        }
     }
-    *out = g_static_xq_addr[dev];
+    *out = g_static_xq_addr[dev].addr;
     return ANVIL_OK;
 }
 

@@ -14,5 +14,7 @@ int cuda_fail(cudaError_t e, const char *what);
 int current_device(int *dev);
 // Multiprocessor count of `dev` (cached).
 int sm_count(int dev, int *out);
+// Bound on every device-side wait of the kernels launched from now on (anvil_set_wait_limit_ns).
+unsigned long long wait_limit_ns();
 
 }  // namespace anvil

@@ -1,36 +1,46 @@
-// chain_persistent.cu -- one cooperative launch runs a whole token's GEMV chain.
+// chain_persistent.cu -- one cooperative launch runs a whole token's GEMV chain, on one GPU
+// or row-sharded across several, with the decoder's data flow carried by flagged words.
 //
 // A decode token is a fixed sequence of MMVQ GEMVs.  Launched one kernel per GEMV, each
 // pays a start-up and drain cost of a few microseconds that the weight stream of a small
 // GEMV cannot hide.  Here a persistent kernel walks the chain instead:
 //
-//   * Groups.  GEMVs that read the same activation form a group (q/k/v; gate/up; o; down;
-//     lm_head).  At the start of a group every CTA quantises the group's fp32 input to
-//     Q8_1 in shared memory, with the arithmetic of quantize_q8_1 (d = amax/127 by IEEE
-//     division, q = roundf(x/d)), so the dots see exactly the quants a separate quantiser
-//     would have written.  A group may wait for every group before it (the data flow of a
-//     decoder layer: o-proj needs q/k/v done, gate/up need o-proj, ...): a grid barrier on
-//     per-group arrival counters, spun by one thread per CTA with a 2 s bound.
+//   * Groups.  GEMVs that read the same activation form a group (q/k/v; o; gate/up; down).
+//     A group's input is either a fixed fp32 vector (the token's embedding) or the output
+//     of an earlier GEMV of the chain ("chained": the attention output stands in as q's
+//     output, the ffn input as o's, down's input as silu(gate) * up, the next layer's input
+//     as down's).  Every CTA with work in the group quantises the input to Q8_1 in shared
+//     memory itself, with the arithmetic of quantize_q8_1 (d = amax/127 by IEEE division,
+//     q = roundf(x/d)).  Each warp stages its share of the next group right after its own
+//     tiles of the current one, into the other of two activation buffers, so one CTA barrier
+//     per group remains.  A chained input keeps d8 in fp32, and the group's results are
+//     multiplied by a power of two, 2^-e with e the exponent of the input's largest
+//     magnitude: values stay in range through hundreds of GEMVs, exactly (the quants are
+//     those of the input itself).
+//   * Flagged output words.  Every output value is written as one 8-byte word {fp32 value,
+//     32-bit epoch}, the launch number, with a single 64-bit store, into each rank's copy of
+//     the output (this GPU's, and the peers' over NVLink through CUDA IPC mappings).  A
+//     consumer reads the words of its input and waits (bounded) only until each carries
+//     the current epoch: a word is its own ready flag, so no fence, counter or grid barrier
+//     sits between a producer and its consumers, and a group starts on each CTA as soon as
+//     the values it reads have arrived.  Output buffers hold two epochs (launch parity), so
+//     a rank one launch ahead never overwrites words a slower rank is still reading.
+//     Chained sources are stored in a lane-blocked order (ll_pos) so that a warp's 16-byte
+//     loads are contiguous and each lane still ends up with 16 consecutive values.
 //   * Weight rings.  Each warp owns a byte ring in shared memory and deals itself tiles
 //     round-robin across the tiles of every group of the chain.  Lane 0 keeps the ring full
 //     with bulk async copies (cp.async.bulk, completion on one of 8 mbarriers) and runs
-//     ahead across group boundaries: while a CTA waits at a barrier or stages the next
-//     activation, the copies for the next group's weights are already in flight, so HBM
-//     keeps streaming through the whole token.  Tiles of different GEMVs differ in size;
-//     a tile is placed at the ring head, or at offset 0 when it would cross the end.
+//     ahead across group boundaries: while a CTA waits for its next input, the copies for
+//     the next groups' weights are already in flight.  A gate/up pair is one tile of h gate
+//     rows and h up rows (two copies into one stage); its epilogue stores silu(g) * u.
 //   * Dots.  The tile arithmetic is the MMVQ kernel's (unit_step, load_hdr; lane-per-block
 //     decode with compile-time lanes per row), so for the same rows per tile and lanes per
-//     row the outputs are bit-identical to anvil_mmvq's.
-//   * Ranks.  With world > 1 each rank holds a row shard of every matrix and writes its
-//     output rows into its own copy of the full output; at the end of a group the rank's
-//     last CTA copies the rank's rows into every peer's copy (peer pointers over NVLink),
-//     then counts the rank on every rank's group counter (one system-scope release per
-//     rank and group).  The exchange is the all-gather of the row-sharded GEMV, inside the
-//     kernel.
+//     row a fixed-input GEMV is bit-identical to anvil_mmvq's.
 //
-// Co-residency of all CTAs (required by the barriers) comes from the cooperative launch.
-// Every wait is bounded; a wait that gives up raises a device status flag and the kernel
-// runs on (its results are then wrong, never hung).
+// Co-residency of all CTAs (consumers wait for other CTAs' words) comes from the cooperative
+// launch.  Every wait is bounded; a wait that gives up raises a status flag of this
+// translation unit (read by anvil_pchain_take_status), later waits of the launch then end
+// at once, and the kernel runs to its end with wrong results, never hung.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -45,169 +55,319 @@
 namespace anvil {
 
 constexpr int kPcMaxRanks = ANVIL_MAX_RANKS;
-constexpr int kPcSlots = 8;  // tiles in flight per warp
-constexpr int kStatusBarrierTimeout = 2;
-constexpr uint64_t kBarrierLimitNs = 2000000000ull;
+constexpr int kPcSlots = 8;              // tiles in flight per warp
+// Status flags: 1 (kStatusMbarTimeout) = a weight copy did not land in time, set by
+// mbar_wait_bounded; 2 = an input word did not arrive in time.
+constexpr int kStatusInputTimeout = 2;
 
-// Compile-time tile shapes: rows per tile x lanes per row.
+// Compile-time tile shapes: rows per stage x lanes per row; the gate/up shapes stage h gate
+// rows then h up rows (rows per stage 2h).
 enum PcVariant : int {
-    kV1x32, kV2x32, kV4x32, kV8x32, kV2x16, kV4x16, kV8x16, kV4x8, kV8x8, kNumVariants
+    kV1x32, kV2x32, kV4x32, kV8x32, kV2x16, kV4x16, kV8x16, kV4x8, kV8x8,
+    kG1x32, kG2x32, kG2x16, kG4x32, kG4x16, kG4x8, kNumVariants
 };
-constexpr int kVarRpb[kNumVariants] = {1, 2, 4, 8, 2, 4, 8, 4, 8};
-constexpr int kVarLb[kNumVariants] = {32, 32, 32, 32, 16, 16, 16, 8, 8};
+constexpr int kVarRpb[kNumVariants] = {1, 2, 4, 8, 2, 4, 8, 4, 8, 2, 4, 4, 8, 8, 8};
+constexpr int kVarLb[kNumVariants] = {32, 32, 32, 32, 16, 16, 16, 8, 8, 32, 32, 16, 32, 16, 8};
+constexpr bool kVarGlu[kNumVariants] = {false, false, false, false, false, false, false, false,
+                                        false, true,  true,  true,  true,  true,  true};
 
 struct PcGemv {
-    const uint8_t *W;          // this rank's rows, GGUF blocks
-    float *y[kPcMaxRanks];     // full output buffer (ncols x nrows_full) on each rank
-    int type, variant, rpb;
+    const uint8_t *W;          // this rank's rows (the gate rows of a gate/up pair)
+    const uint8_t *W2;         // the up rows of a gate/up pair, else null
+    uint64_t *y[kPcMaxRanks];  // each rank's output words: [2 parities][ncols][nrows_full]
+    int type, variant;
+    int rpb, trows;            // rows per stage; output rows per tile (rpb, or rpb/2 for a pair)
     int nrows, row0, nrows_full;
+    int perm;                  // output stored in ll_pos order (a chained group reads it)
     int row_bytes, alloc;      // alloc: ring bytes one tile takes
     int tile_base, ntiles;     // tiles of this GEMV within its group
 };
 
 struct PcGroup {
-    const float *x;            // fp32 input, ncols x K
+    const float *x;            // fixed fp32 input (ncols x K), or null
+    const uint64_t *src;       // chained: this rank's output words of the source GEMV
+    uint8_t *dump;             // optional: staged Q8_1 blocks written here (parity probe)
     int K, first, count, ntiles, rot, family;
-    int wait_from, wait_to;    // wait on counters [wait_from, wait_to) before staging
 };
 
 struct PcArgs {
     const PcGroup *groups;
     const PcGemv *gemvs;
-    uint32_t *const *counters;  // device array: counters[q] = rank q's arrival counters
+    uint64_t *trace;            // optional: per CTA and group {start, staged, done, 1}
+    uint64_t wait_ns;           // bound on every wait
     int ngroups, world, rank;
-    int act_off, ring_off, ring_bytes;
-    int first_wait_from;        // group 0 of launch e > 0 (world > 1): previous launch's tail
-    uint32_t epoch;
+    int act_off[2], ring_off, ring_bytes;  // activation buffers of even / odd groups, rings
+    uint32_t epoch;             // this launch's number (1, 2, ...): the flag of its words
 };
 
-// ---- synchronisation helpers ----------------------------------------------------------
+// ---- flagged words -----------------------------------------------------------------------
 
-__device__ __forceinline__ uint32_t ld_relaxed(const uint32_t *p, bool sys) {
-    uint32_t v;
-    if (sys)
-        asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    else
-        asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
+// Position of value r of an n-value chained vector (n % 32 == 0) in its word array.  Values
+// come in blocks of 512 (the last block holds t = n % 512 when that is not 0); within a block,
+// value v = 16 l + 2 k + j (lane l, load k = 0..7, half j) sits at word k (t / 8) + 2 l + j, so
+// the warp's k-th 16-byte load of the block is contiguous and lane l collects the 16
+// consecutive values 16 l .. 16 l + 15.
+__host__ __device__ __forceinline__ int ll_pos(int r, int n) {
+    const int base = r & ~511;
+    const int t = n - base < 512 ? n - base : 512;
+    const int v = r & 511;
+    return base + ((v & 15) >> 1) * (t >> 3) + ((v >> 4) << 1) + (v & 1);
 }
 
-__device__ __forceinline__ void red_relaxed_add(uint32_t *p, uint32_t v, bool sys) {
-    if (sys)
-        asm volatile("red.relaxed.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-    else
-        asm volatile("red.relaxed.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_word(uint64_t *p, float v, uint32_t epoch) {
+    const uint64_t w = uint64_t(__float_as_uint(v)) | (uint64_t(epoch) << 32);
+    asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
 
-// True once any bounded wait of this translation unit has given up: later waits then
-// end at once (barriers) or after 1 ms (weight copies), so a failed run finishes quickly.
+__device__ __forceinline__ void ld_words2(const uint64_t *p, uint64_t &a, uint64_t &b) {
+    asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
+// True once any bounded wait of this translation unit has given up: later waits then end at
+// once (input words) or after 1 ms (weight copies), so a failed launch finishes quickly.
 __device__ __forceinline__ bool pc_failed() {
     return *reinterpret_cast<volatile int *>(&g_anvil_device_status) != 0;
 }
 
-// Thread 0 of a CTA: wait until counters [from, to) all reached `target` (wrap-safe).
-// Relaxed polling; the fence after the last read orders what follows (acquire).
-__device__ void pc_wait_counters(const PcArgs &a, int from, int to, uint32_t target) {
-    const bool sys = a.world > 1;
-    // one CTA count per group on one GPU; one rank count per group across GPUs
-    const uint32_t *base = a.counters[a.rank] + (sys ? a.ngroups : 0);
-    uint64_t t0 = 0;
-    for (int g = from; g < to; ++g) {
-        for (uint32_t it = 0;; ++it) {
-            if (int32_t(ld_relaxed(base + g, sys) - target) >= 0) break;
-            if ((it & 31u) == 31u) {
-                if (pc_failed()) return;  // an earlier wait gave up: do not wait again
-                const uint64_t now = global_timer_ns();
-                if (t0 == 0) {
-                    t0 = now;
-                } else if (now - t0 > kBarrierLimitNs) {
-                    atomicOr(&g_anvil_device_status, kStatusBarrierTimeout);
-                    return;
+// A lane's 16 words of one 512-value block (p: the block start + 2 * lane; step = t / 8 for
+// a block of t values): the warp's k-th 16-byte load is contiguous.
+__device__ __forceinline__ void ll_issue(const uint64_t *p, int step, uint64_t (&w)[16]) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) ld_words2(p + k * step, w[2 * k], w[2 * k + 1]);
+}
+
+// The values of the 16 words once all carry `epoch`: words that do not yet are re-read, with
+// an exponential sleep between polls (64 ns doubling to 2 us) so that waiting warps leave L2
+// to the producers, until they do or the bounded wait gives up (then the status flag is
+// raised and the values are whatever was read).
+__device__ __forceinline__ void ll_finish(const uint64_t *p, int step, uint32_t epoch,
+                                          uint64_t wait_ns, uint64_t (&w)[16], float (&v)[16]) {
+    uint32_t bad = 0;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) bad |= uint32_t(uint32_t(w[i] >> 32) != epoch) << i;
+    if (bad && !pc_failed()) {
+        const uint64_t t0 = global_timer_ns();
+        uint32_t nap = 64;
+        while (bad) {
+            __nanosleep(nap);
+            nap = nap < 2048 ? 2 * nap : 2048;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                if (bad & (3u << (2 * k))) {
+                    ld_words2(p + k * step, w[2 * k], w[2 * k + 1]);
+                    bad &= ~(3u << (2 * k));
+                    bad |= uint32_t(uint32_t(w[2 * k] >> 32) != epoch) << (2 * k);
+                    bad |= uint32_t(uint32_t(w[2 * k + 1] >> 32) != epoch) << (2 * k + 1);
                 }
+            }
+            if (bad && global_timer_ns() - t0 > wait_ns) {
+                atomicOr(&g_anvil_device_status, kStatusInputTimeout);
+                break;
             }
         }
     }
-    if (sys)
-        asm volatile("fence.acq_rel.sys;" ::: "memory");
-    else
-        asm volatile("fence.acq_rel.gpu;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(uint32_t(w[i]));
 }
 
-__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t *p, uint32_t v) {
-    uint32_t old;
-    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
-    return old;
+// 2^-e for a vector whose largest magnitude is m (e = the exponent of m); 2^127 for m == 0
+// or subnormal m, 2^-126 from m >= 2^127 (infinities and NaN included).
+__device__ __forceinline__ float pow2_scale(float m) {
+    const int eb = int((__float_as_uint(m) >> 23) & 0xFF);
+    const int E = min(max(254 - eb, 1), 254);
+    return __uint_as_float(uint32_t(E) << 23);
 }
 
-// Copies this rank's output rows of the group's GEMVs from its own buffer into every peer's
-// (16-byte stores where both sides allow them).  Whole CTA.
-template <int NCOLS>
-__device__ void pc_push_outputs(const PcArgs &a, const PcGroup &grp) {
-    const int T = blockDim.x, tid = threadIdx.x;
-    for (int m = grp.first; m < grp.first + grp.count; ++m) {
-        const PcGemv *gm = a.gemvs + m;
-        const int n = gm->nrows, r0 = gm->row0, nf = gm->nrows_full;
-        for (int c = 0; c < NCOLS; ++c) {
-            const float *src = gm->y[a.rank] + size_t(c) * nf + r0;
-            for (int q = 0; q < a.world; ++q) {
-                if (q == a.rank) continue;
-                float *dst = gm->y[q] + size_t(c) * nf + r0;
-                if (((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0 &&
-                    (n & 3) == 0) {
-                    const float4 *s4 = reinterpret_cast<const float4 *>(src);
-                    float4 *d4 = reinterpret_cast<float4 *>(dst);
-                    for (int i = tid; i < (n >> 2); i += T) d4[i] = s4[i];
-                } else {
-                    for (int i = tid; i < n; i += T) dst[i] = src[i];
-                }
+// Where one staged activation lives in shared memory (one of the two buffers).
+struct ActBuf {
+    uint8_t *aq;
+    float *ad, *ads;
+    int2 *as;
+};
+
+__device__ __forceinline__ ActBuf act_buf(uint8_t *base, int K, int ncols) {
+    const int nkb = K >> 5;
+    ActBuf b;
+    b.aq = base;
+    b.ad = reinterpret_cast<float *>(base + ncols * act_col_bytes(nkb));
+    b.ads = b.ad + ncols * nkb;
+    b.as = reinterpret_cast<int2 *>((reinterpret_cast<uintptr_t>(b.ads + ncols * nkb) + 15) &
+                                    ~uintptr_t(15));
+    return b;
+}
+
+// Quantises this lane's 16 consecutive values (chunk cc of column col; the lane pair 2q, 2q+1
+// holds one Q8_1 block) into the swizzled buffer, with the arithmetic of quantize_q8_1:
+// d = amax / 127 by IEEE division, q = roundf(x / d) through quant_q8.  The stored d8 is
+// rounded to fp16 (ROUND, as quantize_q8_1 stores it) or kept in fp32 (chained inputs).
+// Returns the block's amax.  Whole warp (shuffles); `live` lanes store.
+template <int QT, bool ROUND>
+__device__ __forceinline__ float quant_chunk(const float (&v)[16], bool live, int col, int cc, int nkb,
+                                             int acb, const ActBuf &b) {
+    float am = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) am = fmaxf(am, fabsf(v[i]));
+    am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+    const float d = __fdiv_rn(am, 127.0f);
+    const float dn = am == 0.0f ? 1.0f : d;
+    const float rd = __frcp_rn(dn);
+    uint32_t w[4];
+    int s = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int q = am == 0.0f ? 0 : quant_q8(v[4 * k + i], dn, rd);
+            word |= (uint32_t(q) & 0xFFu) << (8 * i);
+        }
+        w[k] = word;
+        s = __dp4a(int(word), 0x01010101, s);
+    }
+    const int so = __shfl_xor_sync(0xffffffffu, s, 1);
+    if (live) {
+        *reinterpret_cast<uint4 *>(b.aq + col * acb + act_chunk<QT>(cc) * 16) =
+            make_uint4(w[0], w[1], w[2], w[3]);
+        if ((cc & 1) == 0) {
+            const int i = col * nkb + (cc >> 1);
+            const float dd = ROUND ? __half2float(__float2half_rn(d)) : d;
+            b.ad[i] = dd;
+            b.as[i] = make_int2(s, so);
+            b.ads[i] = dd * float(s + so);
+        }
+    }
+    return am;
+}
+
+// One warp's share of a chained group's staging: 512-value blocks warp, warp + nwarps, ...
+// of the NCOLS columns of flagged words, read as they arrive (two blocks in flight per
+// lane), d8 kept in fp32; the warp's column maxima go to colmax[c].  Not inlined: the kernel
+// keeps its ring state in registers across the call.
+template <int QT, int NCOLS>
+__device__ __noinline__ void warp_stage_ll(const uint64_t *__restrict__ src, int K, uint32_t epoch,
+                                           uint64_t wait_ns, uint32_t act_off, float *colmax) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    const ActBuf b = act_buf(smem + act_off, K, NCOLS);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int nkb = K >> 5, acb = act_col_bytes(nkb);
+    const int nb = (K + 511) >> 9;
+    const int total = NCOLS * nb;
+    float cmax[NCOLS];
+#pragma unroll
+    for (int c = 0; c < NCOLS; ++c) cmax[c] = 0.f;
+    for (int b0 = warp; b0 < total; b0 += 2 * nw) {
+        const bool two = b0 + nw < total;  // warp-uniform
+        const int bi1 = two ? b0 + nw : b0;
+        const int col0 = b0 / nb, blk0 = b0 - col0 * nb, col1 = bi1 / nb, blk1 = bi1 - col1 * nb;
+        const int t0 = min(512, K - blk0 * 512), t1 = min(512, K - blk1 * 512);
+        const bool live0 = lane < (t0 >> 4), live1 = two && lane < (t1 >> 4);
+        const uint64_t *p0 = src + size_t(col0) * K + size_t(blk0) * 512 + 2 * lane;
+        const uint64_t *p1 = src + size_t(col1) * K + size_t(blk1) * 512 + 2 * lane;
+        uint64_t w0[16], w1[16];
+        if (live0) ll_issue(p0, t0 >> 3, w0);
+        if (live1) ll_issue(p1, t1 >> 3, w1);
+        float v[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = 0.f;
+        if (live0) ll_finish(p0, t0 >> 3, epoch, wait_ns, w0, v);
+        float am = quant_chunk<QT, false>(v, live0, col0, blk0 * 32 + lane, nkb, acb, b);
+#pragma unroll
+        for (int c = 0; c < NCOLS; ++c)
+            if (c == col0) cmax[c] = fmaxf(cmax[c], am);
+        if (two) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] = 0.f;
+            if (live1) ll_finish(p1, t1 >> 3, epoch, wait_ns, w1, v);
+            am = quant_chunk<QT, false>(v, live1, col1, blk1 * 32 + lane, nkb, acb, b);
+#pragma unroll
+            for (int c = 0; c < NCOLS; ++c)
+                if (c == col1) cmax[c] = fmaxf(cmax[c], am);
+        }
+    }
+#pragma unroll
+    for (int c = 0; c < NCOLS; ++c) {
+        const float m = warp_max(cmax[c]);
+        if (lane == 0) colmax[c] = m;
+    }
+}
+
+// One warp's share of a fixed-input group's staging: the same blocks of fp32 values, d8
+// rounded to fp16 as quantize_q8_1 stores it.
+template <int QT, int NCOLS>
+__device__ __noinline__ void warp_stage_f32(const float *__restrict__ x, int K, uint32_t act_off) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    const ActBuf b = act_buf(smem + act_off, K, NCOLS);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int nkb = K >> 5, acb = act_col_bytes(nkb);
+    const int nb = (K + 511) >> 9;
+    const int total = NCOLS * nb;
+    for (int b0 = warp; b0 < total; b0 += 2 * nw) {
+        float v[2][16];
+        int col[2], blk[2];
+        bool live[2];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const int bi = min(b0 + j * nw, total - 1);
+            col[j] = bi / nb;
+            blk[j] = bi - col[j] * nb;
+            live[j] = b0 + j * nw < total && lane < (min(512, K - blk[j] * 512) >> 4);
+            const float4 *q = reinterpret_cast<const float4 *>(x + size_t(col[j]) * K + blk[j] * 512 +
+                                                               16 * lane);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float4 f = live[j] ? __ldg(q + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+                v[j][4 * k] = f.x;
+                v[j][4 * k + 1] = f.y;
+                v[j][4 * k + 2] = f.z;
+                v[j][4 * k + 3] = f.w;
             }
         }
+        quant_chunk<QT, true>(v[0], live[0], col[0], blk[0] * 32 + lane, nkb, acb, b);
+        if (b0 + nw < total) quant_chunk<QT, true>(v[1], live[1], col[1], blk[1] * 32 + lane, nkb, acb, b);
     }
 }
 
-// The CTA's arrival at the end of group g (whole CTA, after its barrier).  One GPU: thread 0
-// publishes the CTA's outputs (release fence) and counts the CTA.  Several GPUs: the CTAs
-// count themselves on this GPU; the last one (it sees every CTA's outputs through the
-// acquire-release count) copies the rank's output rows to every peer, then one system-scope
-// release and one count per rank on every rank's group counter.
-template <int NCOLS>
-__device__ void pc_arrive(const PcArgs &a, const PcGroup &grp, int g, int *s_last) {
-    if (a.world == 1) {
-        if (threadIdx.x == 0) {
-            asm volatile("fence.acq_rel.gpu;" ::: "memory");
-            red_relaxed_add(a.counters[0] + g, 1u, false);
-        }
-        return;
-    }
-    if (threadIdx.x == 0) {
-        asm volatile("fence.acq_rel.gpu;" ::: "memory");
-        const uint32_t old = atom_add_acq_rel_gpu(a.counters[a.rank] + g, 1u);
-        *s_last = old + 1u == (a.epoch + 1u) * gridDim.x;
-    }
-    __syncthreads();
-    if (*s_last) {
-        pc_push_outputs<NCOLS>(a, grp);
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            asm volatile("fence.acq_rel.sys;" ::: "memory");
-            for (int q = 0; q < a.world; ++q) red_relaxed_add(a.counters[q] + a.ngroups + g, 1u, true);
-        }
+// Writes the staged activation as {fp32 d8, 32 quants} blocks (parity probe).  Whole CTA.
+template <int QT>
+__device__ void dump_staged(uint8_t *out, int K, int ncols, const ActBuf &b) {
+    const int nkb = K >> 5, acb = act_col_bytes(nkb);
+    for (int i = threadIdx.x; i < ncols * nkb; i += blockDim.x) {
+        const int c = i / nkb, kb = i - c * nkb;
+        uint32_t *o = reinterpret_cast<uint32_t *>(out + size_t(i) * kQ8_1Bytes);
+        o[0] = __float_as_uint(b.ad[i]);
+        const uint4 u = *reinterpret_cast<const uint4 *>(b.aq + c * acb + act_chunk<QT>(2 * kb) * 16);
+        const uint4 v = *reinterpret_cast<const uint4 *>(b.aq + c * acb + act_chunk<QT>(2 * kb + 1) * 16);
+        o[1] = u.x; o[2] = u.y; o[3] = u.z; o[4] = u.w;
+        o[5] = v.x; o[6] = v.y; o[7] = v.z; o[8] = v.w;
     }
 }
 
 // ---- tile arithmetic -------------------------------------------------------------------
 
-// Dots of one staged tile (rows r0 .. r0 + rows - 1 of GEMV `gm`, a device descriptor) and
-// the stores of its outputs to every rank's buffer.  Same lane mapping and reduction
-// order as mmvq_kernel with LBT lanes per row.  Scalar arguments only, so the call keeps
-// everything in registers.
-template <int QT, int NCOLS, int RPB, int LBT>
-__device__ __noinline__ void pc_tile(const PcGemv *__restrict__ gm, const uint8_t *wrow0, int r0,
-                                     int rows, const uint8_t *aq, const float *ad,
-                                     const float *ads, const int2 *as, int K, int rank) {
+// Where one GEMV's outputs go, held in registers per warp: this lane's rank buffer (lane
+// bl < world of a row's lanes stores to rank bl), the row offset of this rank's shard, and
+// the layout.
+struct PcOut {
+    uint64_t *y;               // rank (lane < world ? lane : 0)'s buffer, current parity
+    int nfull, row0, perm, world;
+};
+
+// Dots of one staged tile and the stores of its outputs, as flagged words, to every rank's
+// buffer.  Plain: rows r0 .. r0 + rows - 1 of the GEMV.  Gate/up (GLU): the stage holds
+// RPB/2 gate rows then RPB/2 up rows; slot s and slot s + NS/2 of a lane are gate and up row
+// of the same output row, stored as silu(g) * u.  Same lane mapping and reduction order as
+// mmvq_kernel with LBT lanes per row.  sc0 / sc1: the group's per-column input scale (1 for a
+// fixed input).
+template <int QT, int NCOLS, int RPB, int LBT, bool GLU>
+__device__ __forceinline__ void pc_tile(const PcOut &o, uint32_t stage_off, int r0, int rows,
+                                        uint32_t act_off, int K, uint32_t epoch, float sc0, float sc1) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    const uint8_t *wrow0 = smem + stage_off;
+    const ActBuf b = act_buf(smem + act_off, K, NCOLS);
     using TR = QTraits<QT>;
     constexpr int RG = 32 / LBT;
     constexpr int NS = RPB >= RG ? RPB / RG : 1;
+    static_assert(!GLU || (NS % 2 == 0 && RPB % (2 * RG) == 0), "gate/up tile shape");
     const int lane = threadIdx.x & 31;
     const int bl = lane & (LBT - 1), grp = lane / LBT;
     const int nkb = K >> 5, acb = act_col_bytes(nkb);
@@ -220,73 +380,45 @@ __device__ __noinline__ void pc_tile(const PcGemv *__restrict__ gm, const uint8_
         for (int c = 0; c < NCOLS; ++c) acc[i][c] = 0.f;
     if (grp < RPB) {
         const TileCtx ctx{wrow0 + grp * row_bytes, RG * row_bytes, 0, r0, rows, K, nkb, acb, RG, grp,
-                          aq, ad, ads, as, nullptr};
-        for (int b = bl; b < nblk; b += LBT) {
+                          b.aq, b.ad, b.ads, b.as, nullptr};
+        for (int blk = bl; blk < nblk; blk += LBT) {
             BlkHdr hdr[NS];
 #pragma unroll
             for (int sl = 0; sl < NS; ++sl)
-                hdr[sl] = load_hdr<QT>(ctx.lane_row0 + sl * ctx.slot_stride + b * TR::bytes);
-            unit_step<QT, NCOLS, NS, kModeQ81, 0>(ctx, b, hdr, acc);
+                hdr[sl] = load_hdr<QT>(ctx.lane_row0 + sl * ctx.slot_stride + blk * TR::bytes);
+            unit_step<QT, NCOLS, NS, kModeQ81, 0>(ctx, blk, hdr, acc);
             if constexpr (Units<QT>::n == 4) {
-                unit_step<QT, NCOLS, NS, kModeQ81, 1>(ctx, b, hdr, acc);
-                unit_step<QT, NCOLS, NS, kModeQ81, 2>(ctx, b, hdr, acc);
-                unit_step<QT, NCOLS, NS, kModeQ81, 3>(ctx, b, hdr, acc);
+                unit_step<QT, NCOLS, NS, kModeQ81, 1>(ctx, blk, hdr, acc);
+                unit_step<QT, NCOLS, NS, kModeQ81, 2>(ctx, blk, hdr, acc);
+                unit_step<QT, NCOLS, NS, kModeQ81, 3>(ctx, blk, hdr, acc);
             }
         }
     }
-    const int nfull = gm->nrows_full, row0 = gm->row0;
+    const size_t par = size_t(epoch & 1u) * NCOLS;
+    constexpr int NOUT = GLU ? NS / 2 : NS;
 #pragma unroll
-    for (int sl = 0; sl < NS; ++sl) {
+    for (int sl = 0; sl < NOUT; ++sl) {
         const int i = sl * RG + grp;
+        const int row = o.row0 + r0 + i;
+        const int pos = o.perm ? ll_pos(row, o.nfull) : row;
 #pragma unroll
         for (int c = 0; c < NCOLS; ++c) {
+            const float sc = c == 0 ? sc0 : sc1;
             float v = acc[sl][c];
 #pragma unroll
-            for (int o = LBT >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-            if (bl == 0 && grp < RPB && i < rows) {
-                const size_t off = size_t(c) * nfull + row0 + r0 + i;
-                gm->y[rank][off] = v;  // this rank's buffer; peers get the slice at group end
+            for (int k = LBT >> 1; k > 0; k >>= 1) v += __shfl_xor_sync(0xffffffffu, v, k);
+            v *= sc;
+            if constexpr (GLU) {
+                float u = acc[sl + NS / 2][c];
+#pragma unroll
+                for (int k = LBT >> 1; k > 0; k >>= 1) u += __shfl_xor_sync(0xffffffffu, u, k);
+                u *= sc;
+                v = v / (1.0f + expf(-v)) * u;
             }
+            if (bl < o.world && grp < RPB && i < rows) st_word(o.y + (par + c) * o.nfull + pos, v, epoch);
         }
     }
 }
-
-
-#define ANVIL_PC_TILE_ARGS gm, wrow0, r0, rows, aq, ad, ads, as, K, rank
-
-template <int QT, int NCOLS>
-__device__ __forceinline__ void pc_tile_variant(int variant, const PcGemv *gm, const uint8_t *wrow0,
-                                                int r0, int rows, const uint8_t *aq, const float *ad,
-                                                const float *ads, const int2 *as, int K, int rank) {
-    switch (variant) {
-    case kV1x32: pc_tile<QT, NCOLS, 1, 32>(ANVIL_PC_TILE_ARGS); break;
-    case kV2x32: pc_tile<QT, NCOLS, 2, 32>(ANVIL_PC_TILE_ARGS); break;
-    case kV4x32: pc_tile<QT, NCOLS, 4, 32>(ANVIL_PC_TILE_ARGS); break;
-    case kV8x32: pc_tile<QT, NCOLS, 8, 32>(ANVIL_PC_TILE_ARGS); break;
-    case kV2x16: pc_tile<QT, NCOLS, 2, 16>(ANVIL_PC_TILE_ARGS); break;
-    case kV4x16: pc_tile<QT, NCOLS, 4, 16>(ANVIL_PC_TILE_ARGS); break;
-    case kV8x16: pc_tile<QT, NCOLS, 8, 16>(ANVIL_PC_TILE_ARGS); break;
-    case kV4x8: pc_tile<QT, NCOLS, 4, 8>(ANVIL_PC_TILE_ARGS); break;
-    case kV8x8: pc_tile<QT, NCOLS, 8, 8>(ANVIL_PC_TILE_ARGS); break;
-    default: break;
-    }
-}
-
-template <int NCOLS>
-__device__ __forceinline__ void pc_tile_any(int type, int variant, const PcGemv *gm,
-                                            const uint8_t *wrow0, int r0, int rows,
-                                            const uint8_t *aq, const float *ad, const float *ads,
-                                            const int2 *as, int K, int rank) {
-    switch (type) {
-    case kTypeQ4_K: pc_tile_variant<kTypeQ4_K, NCOLS>(variant, ANVIL_PC_TILE_ARGS); break;
-    case kTypeQ5_K: pc_tile_variant<kTypeQ5_K, NCOLS>(variant, ANVIL_PC_TILE_ARGS); break;
-    case kTypeQ6_K: pc_tile_variant<kTypeQ6_K, NCOLS>(variant, ANVIL_PC_TILE_ARGS); break;
-    case kTypeQ8_0: pc_tile_variant<kTypeQ8_0, NCOLS>(variant, ANVIL_PC_TILE_ARGS); break;
-    default: break;
-    }
-}
-
-#undef ANVIL_PC_TILE_ARGS
 
 // ---- the kernel ------------------------------------------------------------------------
 
@@ -297,8 +429,8 @@ struct PcCursor {
     int g, i;
     int g_ntiles;              // tiles of group g
     int m, t_base, t_end;      // current GEMV index and its tile range in the group
-    const uint8_t *W;
-    int row_bytes, rpb, nrows, alloc, type, variant;
+    const uint8_t *W, *W2;
+    int row_bytes, rpb, trows, nrows, alloc, type, variant;
 };
 
 // Per-warp ring state (identical in every lane; lane 0 issues the copies).  Ring space is
@@ -309,11 +441,9 @@ struct PcRing {
     uint32_t p_total, c_total, p_pos, c_pos, issued, consumed;
 };
 
-// What every warp of the launch shares (pointers into this CTA's shared memory).
 struct PcWarp {
     uint8_t *ring;
     uint64_t *bars;
-    int *s_failed;
     int gw, nw, lane;
     uint32_t R;
 };
@@ -334,8 +464,10 @@ __device__ __forceinline__ void pc_load_gemv(const PcArgs &a, PcCursor &c) {
     c.t_base = gm->tile_base;
     c.t_end = gm->tile_base + gm->ntiles;
     c.W = gm->W;
+    c.W2 = gm->W2;
     c.row_bytes = gm->row_bytes;
     c.rpb = gm->rpb;
+    c.trows = gm->trows;
     c.nrows = gm->nrows;
     c.alloc = gm->alloc;
     c.type = gm->type;
@@ -381,20 +513,30 @@ __device__ __forceinline__ void pc_produce(const PcArgs &a, PcRing &r, const PcW
         const uint32_t pos = wrap ? 0u : r.p_pos;
         if (w.lane == 0) {
             const int slot = int(r.issued % kPcSlots);
-            const int r0 = (r.pc.i - r.pc.t_base) * r.pc.rpb;
-            const int rows = min(r.pc.rpb, r.pc.nrows - r0);
-            const uint8_t *src = r.pc.W + size_t(r0) * size_t(r.pc.row_bytes);
-            const uintptr_t s = reinterpret_cast<uintptr_t>(src);
-            const uintptr_t e = s + size_t(rows) * r.pc.row_bytes;
-            const uintptr_t s_al = (s + 15) & ~uintptr_t(15), e_al = e & ~uintptr_t(15);
-            uint8_t *dst = w.ring + pos + uint32_t(s & 15);
+            const int r0 = (r.pc.i - r.pc.t_base) * r.pc.trows;
+            const int rows = min(r.pc.trows, r.pc.nrows - r0);
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            if (e_al > s_al) {
-                mbar_arrive_expect_tx(&w.bars[slot], uint32_t(e_al - s_al));
-                bulk_copy_g2s(dst + (s_al - s), reinterpret_cast<const void *>(s_al),
-                              uint32_t(e_al - s_al), &w.bars[slot]);
+            if (r.pc.W2) {
+                // gate/up pair: whole 16-byte rows (checked on the host), gate rows then up rows
+                const uint32_t bytes = uint32_t(rows) * uint32_t(r.pc.row_bytes);
+                uint8_t *dst = w.ring + pos;
+                mbar_arrive_expect_tx(&w.bars[slot], 2u * bytes);
+                bulk_copy_g2s(dst, r.pc.W + size_t(r0) * size_t(r.pc.row_bytes), bytes, &w.bars[slot]);
+                bulk_copy_g2s(dst + size_t(r.pc.trows) * r.pc.row_bytes,
+                              r.pc.W2 + size_t(r0) * size_t(r.pc.row_bytes), bytes, &w.bars[slot]);
             } else {
-                mbar_arrive(&w.bars[slot]);
+                const uint8_t *src = r.pc.W + size_t(r0) * size_t(r.pc.row_bytes);
+                const uintptr_t s = reinterpret_cast<uintptr_t>(src);
+                const uintptr_t e = s + size_t(rows) * r.pc.row_bytes;
+                const uintptr_t s_al = (s + 15) & ~uintptr_t(15), e_al = e & ~uintptr_t(15);
+                uint8_t *dst = w.ring + pos + uint32_t(s & 15);
+                if (e_al > s_al) {
+                    mbar_arrive_expect_tx(&w.bars[slot], uint32_t(e_al - s_al));
+                    bulk_copy_g2s(dst + (s_al - s), reinterpret_cast<const void *>(s_al),
+                                  uint32_t(e_al - s_al), &w.bars[slot]);
+                } else {
+                    mbar_arrive(&w.bars[slot]);
+                }
             }
         }
         r.p_total += need;
@@ -404,22 +546,145 @@ __device__ __forceinline__ void pc_produce(const PcArgs &a, PcRing &r, const PcW
     }
 }
 
+// Trace stamps of warp 0 (thread 0) per CTA and group: 0 its staging share starts, 1 it ends,
+// 2 the CTA's barrier is passed (input staged), 3 its tiles are done.
+__device__ __forceinline__ void pc_trace(const PcArgs &a, int g, int k) {
+    if (a.trace && threadIdx.x == 0) a.trace[(size_t(blockIdx.x) * a.ngroups + g) * 4 + k] = global_timer_ns();
+}
+
+// This warp's tiles of one GEMV of the current group, cc.i, cc.i + nw, ... < cc.t_end: wait
+// for each tile's copy (bounded), fix up unaligned row ends, dot and store, refill the ring.
+// One call per GEMV and warp (the tile arithmetic is compiled into the loop); the ring
+// state goes in and comes back by value.
+template <int QT, int NCOLS, int RPB, int LBT, bool GLU>
+__device__ __noinline__ PcRing pc_run(const PcArgs &a, PcRing r, PcWarp w, PcCursor cc, PcOut o,
+                                      uint32_t act_off, float sc0, float sc1, int *s_failed) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int lane = w.lane;
+    const int K = a.groups[cc.g].K;
+    for (; cc.i < cc.t_end; cc.i += w.nw) {
+        if (r.issued == r.consumed) pc_produce(a, r, w);
+        const uint32_t alloc = uint32_t(cc.alloc);
+        const bool wrap = r.c_pos + alloc > w.R;
+        const uint32_t pos = wrap ? 0u : r.c_pos;
+        const int r0 = (cc.i - cc.t_base) * cc.trows;
+        const int rows = min(cc.trows, cc.nrows - r0);
+        const int slot = int(r.consumed % kPcSlots);
+        const uint32_t parity = (r.consumed / kPcSlots) & 1u;
+        const uint8_t *src = cc.W + size_t(r0) * size_t(cc.row_bytes);
+        const uintptr_t s = GLU ? 0 : reinterpret_cast<uintptr_t>(src);
+        const uintptr_t e = GLU ? 0 : s + size_t(rows) * cc.row_bytes;
+        uint8_t *wrow0 = w.ring + pos + uint32_t(s & 15);
+        bool have_w = mbar_try_wait(&w.bars[slot], parity);
+        if (!have_w) {
+            const uint64_t lim = *reinterpret_cast<volatile int *>(s_failed)
+                                     ? (a.wait_ns < 1000000ull ? a.wait_ns : 1000000ull)
+                                     : a.wait_ns;
+            have_w = mbar_wait_bounded(&w.bars[slot], parity, lim);
+            if (!have_w) {
+                *s_failed = 1;
+                (void)mbar_wait_bounded(&w.bars[slot], parity, lim);
+            }
+        }
+        if ((s | e) & 15) {  // unaligned ends: plain loads of at most 30 bytes
+            const uintptr_t s_al = (s + 15) & ~uintptr_t(15), e_al = e & ~uintptr_t(15);
+            if (e_al > s_al) {
+                const int nh = int(s_al - s), nt = int(e - e_al);
+                for (int k = lane; k < nh + nt; k += 32) {
+                    const size_t off = k < nh ? size_t(k) : size_t(e_al - s) + size_t(k - nh);
+                    wrow0[off] = src[off];
+                }
+            } else {
+                for (int k = lane; k < int(e - s); k += 32) wrow0[k] = src[k];
+            }
+            __syncwarp();
+        }
+        if (have_w)
+            pc_tile<QT, NCOLS, RPB, LBT, GLU>(o, uint32_t(wrow0 - smem), r0, rows, act_off, K, a.epoch,
+                                              sc0, sc1);
+        __syncwarp();  // every lane is done with the tile's ring bytes
+        r.c_total += (wrap ? w.R - r.c_pos : 0u) + alloc;
+        r.c_pos = pos + alloc;
+        ++r.consumed;
+        pc_produce(a, r, w);
+    }
+    return r;
+}
+
+#define ANVIL_PC_RUN_ARGS a, r, w, cc, o, act_off, sc0, sc1, s_failed
+
+template <int QT, int NCOLS>
+__device__ __forceinline__ PcRing pc_run_variant(const PcArgs &a, const PcRing &r, const PcWarp &w,
+                                                 const PcCursor &cc, const PcOut &o, uint32_t act_off,
+                                                 float sc0, float sc1, int *s_failed) {
+    switch (cc.variant) {
+    case kV1x32: return pc_run<QT, NCOLS, 1, 32, false>(ANVIL_PC_RUN_ARGS);
+    case kV2x32: return pc_run<QT, NCOLS, 2, 32, false>(ANVIL_PC_RUN_ARGS);
+    case kV4x32: return pc_run<QT, NCOLS, 4, 32, false>(ANVIL_PC_RUN_ARGS);
+    case kV8x32: return pc_run<QT, NCOLS, 8, 32, false>(ANVIL_PC_RUN_ARGS);
+    case kV2x16: return pc_run<QT, NCOLS, 2, 16, false>(ANVIL_PC_RUN_ARGS);
+    case kV4x16: return pc_run<QT, NCOLS, 4, 16, false>(ANVIL_PC_RUN_ARGS);
+    case kV8x16: return pc_run<QT, NCOLS, 8, 16, false>(ANVIL_PC_RUN_ARGS);
+    case kV4x8: return pc_run<QT, NCOLS, 4, 8, false>(ANVIL_PC_RUN_ARGS);
+    case kV8x8: return pc_run<QT, NCOLS, 8, 8, false>(ANVIL_PC_RUN_ARGS);
+    case kG1x32: return pc_run<QT, NCOLS, 2, 32, true>(ANVIL_PC_RUN_ARGS);
+    case kG2x32: return pc_run<QT, NCOLS, 4, 32, true>(ANVIL_PC_RUN_ARGS);
+    case kG2x16: return pc_run<QT, NCOLS, 4, 16, true>(ANVIL_PC_RUN_ARGS);
+    case kG4x32: return pc_run<QT, NCOLS, 8, 32, true>(ANVIL_PC_RUN_ARGS);
+    case kG4x16: return pc_run<QT, NCOLS, 8, 16, true>(ANVIL_PC_RUN_ARGS);
+    case kG4x8: return pc_run<QT, NCOLS, 8, 8, true>(ANVIL_PC_RUN_ARGS);
+    default: return r;
+    }
+}
+
+template <int NCOLS>
+__device__ __forceinline__ PcRing pc_run_any(const PcArgs &a, const PcRing &r, const PcWarp &w,
+                                             const PcCursor &cc, const PcOut &o, uint32_t act_off,
+                                             float sc0, float sc1, int *s_failed) {
+    switch (cc.type) {
+    case kTypeQ4_K: return pc_run_variant<kTypeQ4_K, NCOLS>(ANVIL_PC_RUN_ARGS);
+    case kTypeQ5_K: return pc_run_variant<kTypeQ5_K, NCOLS>(ANVIL_PC_RUN_ARGS);
+    case kTypeQ6_K: return pc_run_variant<kTypeQ6_K, NCOLS>(ANVIL_PC_RUN_ARGS);
+    case kTypeQ8_0: return pc_run_variant<kTypeQ8_0, NCOLS>(ANVIL_PC_RUN_ARGS);
+    default: return r;
+    }
+}
+
+#undef ANVIL_PC_RUN_ARGS
+
+// This warp's share of group g's staging into activation buffer g & 1.
+template <int NCOLS>
+__device__ __forceinline__ void pc_stage_share(const PcArgs &a, int g, float (*s_max)[kMaxWarps][2]) {
+    const int warp = threadIdx.x >> 5;
+    const PcGroup *grp = a.groups + g;
+    const uint32_t off = uint32_t(a.act_off[g & 1]);
+    const int K = grp->K;
+    if (grp->src) {
+        const uint64_t *src = grp->src + size_t(a.epoch & 1u) * NCOLS * K;
+        if (grp->family == 0)  // K-quant swizzle
+            warp_stage_ll<kTypeQ4_K, NCOLS>(src, K, a.epoch, a.wait_ns, off, s_max[g & 1][warp]);
+        else                   // Q8_0 swizzle
+            warp_stage_ll<kTypeQ8_0, NCOLS>(src, K, a.epoch, a.wait_ns, off, s_max[g & 1][warp]);
+    } else {
+        if (grp->family == 0)
+            warp_stage_f32<kTypeQ4_K, NCOLS>(grp->x, K, off);
+        else
+            warp_stage_f32<kTypeQ8_0, NCOLS>(grp->x, K, off);
+    }
+}
 
 template <int NCOLS>
 __global__ void __launch_bounds__(kMaxWarps * 32, 1) pchain_kernel(const __grid_constant__ PcArgs a) {
     extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ float s_max[2][kMaxWarps][2];  // per activation buffer, warp, column: input max
+    __shared__ int s_failed;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nwarps = blockDim.x >> 5;
-    uint8_t *act_base = smem + a.act_off;
-    // Set once a bounded wait of this CTA (or, at the launch start, of any kernel of this
-    // library) has given up: later weight waits then use a 1 ms bound.
-    __shared__ int s_failed, s_last;
-    if (tid == 0) s_failed = 0;
+    if (tid == 0) s_failed = pc_failed() ? 1 : 0;
 
     PcWarp w;
     w.ring = smem + a.ring_off + size_t(warp) * a.ring_bytes;
     w.bars = reinterpret_cast<uint64_t *>(smem) + warp * kPcSlots;
-    w.s_failed = &s_failed;
     w.nw = gridDim.x * nwarps;
     w.gw = blockIdx.x * nwarps + warp;
     w.lane = lane;
@@ -438,96 +703,74 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) pchain_kernel(const __grid_
     }
     __syncwarp();
 
-    pc_produce(a, r, w);  // the first weight tiles stream while the first activation is staged
+    pc_produce(a, r, w);  // the first weight tiles stream while the first input is staged
 
-    // The next group's descriptor is read one group ahead, off the barrier's critical path.
-    PcGroup nx{};
-    if (a.ngroups > 0) nx = a.groups[0];
+    if (a.ngroups > 0) {
+        pc_trace(a, 0, 0);
+        pc_stage_share<NCOLS>(a, 0, s_max);
+        pc_trace(a, 0, 1);
+    }
     for (int g = 0; g < a.ngroups; ++g) {
-        const PcGroup cur = nx;
-        if (g + 1 < a.ngroups) nx = a.groups[g + 1];
+        const PcGroup cur = a.groups[g];
         const int K = cur.K;
-        // ---- 1. dependencies -------------------------------------------------------------
-        if (tid == 0) {
-            const uint32_t per_epoch = a.world > 1 ? uint32_t(a.world) : gridDim.x;
-            if (g == 0) {
-                if (pc_failed()) s_failed = 1;
-                if (a.world > 1 && a.epoch > 0)
-                    pc_wait_counters(a, a.first_wait_from, a.ngroups, a.epoch * per_epoch);
-            } else if (cur.wait_to > cur.wait_from) {
-                pc_wait_counters(a, cur.wait_from, cur.wait_to, (a.epoch + 1) * per_epoch);
+        // ---- 1. the group's input is staged (every warp did its share) ----------------------
+        // Also: every warp is done with group g - 1's tiles, so buffer (g + 1) & 1 is free.
+        __syncthreads();
+        pc_trace(a, g, 2);
+        const uint32_t act_off = uint32_t(a.act_off[g & 1]);
+        float sc[2] = {1.f, 1.f};
+        if (cur.src) {
+#pragma unroll
+            for (int c = 0; c < NCOLS; ++c) {
+                float m = 0.f;
+                for (int k = 0; k < nwarps; ++k) m = fmaxf(m, s_max[g & 1][k][c]);
+                sc[c] = pow2_scale(m);
             }
         }
-        __syncthreads();
-        // ---- 2. stage the group's activation (fused Q8_1 quantisation) ---------------------
-        const int nkb = K >> 5;
-        uint8_t *aq = act_base;
-        float *ad = reinterpret_cast<float *>(aq + NCOLS * act_col_bytes(nkb));
-        float *ads = ad + NCOLS * nkb;
-        int2 *as = reinterpret_cast<int2 *>(
-            (reinterpret_cast<uintptr_t>(ads + NCOLS * nkb) + 15) & ~uintptr_t(15));
-        if (cur.family == 0)  // K-quant swizzle
-            stage_f32_q8_1<kTypeQ4_K, NCOLS>(cur.x, K, aq, ad, ads, as);
-        else                  // Q8_0 swizzle
-            stage_f32_q8_1<kTypeQ8_0, NCOLS>(cur.x, K, aq, ad, ads, as);
-        __syncthreads();
+        if (cur.dump && blockIdx.x == 0) {
+            const ActBuf b = act_buf(smem + act_off, K, NCOLS);
+            if (cur.family == 0)
+                dump_staged<kTypeQ4_K>(cur.dump, K, NCOLS, b);
+            else
+                dump_staged<kTypeQ8_0>(cur.dump, K, NCOLS, b);
+        }
 
-        // ---- 3. this warp's tiles of the group -------------------------------------------
+        // ---- 2. this warp's tiles of the group, one run per GEMV ----------------------------
         PcCursor cc{};
         cc.g = g;
         cc.i = pc_first(cur.rot, w.gw, w.nw);
         cc.g_ntiles = cur.ntiles;
-        if (cc.i < cc.g_ntiles) pc_load_gemv(a, cc);
-        for (; cc.i < cc.g_ntiles; cc.i += w.nw) {
-            if (cc.i >= cc.t_end) pc_load_gemv(a, cc);
-            if (r.issued == r.consumed) pc_produce(a, r, w);
-            const uint32_t alloc = uint32_t(cc.alloc);
-            const bool wrap = r.c_pos + alloc > w.R;
-            const uint32_t pos = wrap ? 0u : r.c_pos;
-            const int r0 = (cc.i - cc.t_base) * cc.rpb;
-            const int rows = min(cc.rpb, cc.nrows - r0);
-            const int slot = int(r.consumed % kPcSlots);
-            const uint32_t parity = (r.consumed / kPcSlots) & 1u;
-            const uint8_t *src = cc.W + size_t(r0) * size_t(cc.row_bytes);
-            const uintptr_t s = reinterpret_cast<uintptr_t>(src);
-            const uintptr_t e = s + size_t(rows) * cc.row_bytes;
-            uint8_t *wrow0 = w.ring + pos + uint32_t(s & 15);
-            bool have_w = mbar_try_wait(&w.bars[slot], parity);
-            if (!have_w) {
-                const uint64_t lim = *reinterpret_cast<volatile int *>(&s_failed) ? 1000000ull
-                                                                                   : kWaitLimitNs;
-                have_w = mbar_wait_bounded(&w.bars[slot], parity, lim);
-                if (!have_w) {
-                    s_failed = 1;
-                    (void)mbar_wait_bounded(&w.bars[slot], parity, lim);
-                }
-            }
-            if ((s | e) & 15) {  // unaligned ends: plain loads of at most 30 bytes
-                const uintptr_t s_al = (s + 15) & ~uintptr_t(15), e_al = e & ~uintptr_t(15);
-                if (e_al > s_al) {
-                    const int nh = int(s_al - s), nt = int(e - e_al);
-                    for (int k = lane; k < nh + nt; k += 32) {
-                        const size_t off = k < nh ? size_t(k) : size_t(e_al - s) + size_t(k - nh);
-                        wrow0[off] = src[off];
-                    }
-                } else {
-                    for (int k = lane; k < int(e - s); k += 32) wrow0[k] = src[k];
-                }
-                __syncwarp();
-            }
-            if (have_w)
-                pc_tile_any<NCOLS>(cc.type, cc.variant, a.gemvs + cc.m, wrow0, r0, rows, aq, ad, ads,
-                                   as, K, a.rank);
-            __syncwarp();  // every lane is done with the tile's ring bytes
-            r.c_total += (wrap ? w.R - r.c_pos : 0u) + alloc;
-            r.c_pos = pos + alloc;
-            ++r.consumed;
-            pc_produce(a, r, w);
+        while (cc.i < cc.g_ntiles) {
+            pc_load_gemv(a, cc);
+            const PcGemv *gm = a.gemvs + cc.m;
+            PcOut o;
+            o.y = gm->y[lane < a.world ? lane : 0];
+            o.nfull = gm->nrows_full;
+            o.row0 = gm->row0;
+            o.perm = gm->perm;
+            o.world = a.world;
+            r = pc_run_any<NCOLS>(a, r, w, cc, o, act_off, sc[0], sc[1], &s_failed);
+            cc.i += ((cc.t_end - cc.i + w.nw - 1) / w.nw) * w.nw;  // first tile past this GEMV
         }
-        // ---- 4. arrive -------------------------------------------------------------------
-        __syncthreads();  // all warps done with this group's activation and outputs
-        pc_arrive<NCOLS>(a, cur, g, &s_last);
+        pc_trace(a, g, 3);
+        // ---- 3. this warp's share of the next group's input, into the other buffer ----------
+        if (g + 1 < a.ngroups) {
+            pc_trace(a, g + 1, 0);
+            pc_stage_share<NCOLS>(a, g + 1, s_max);
+            pc_trace(a, g + 1, 1);
+        }
     }
+}
+
+// Current-epoch values of one output, in row order; NaN where a word does not carry `epoch`.
+__global__ void pchain_read_kernel(const uint64_t *__restrict__ y, float *__restrict__ dst, int ncols,
+                                   int n, int perm, uint32_t epoch) {
+    const long i = long(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= long(ncols) * n) return;
+    const int c = int(i / n), r = int(i - long(c) * n);
+    const int pos = perm ? ll_pos(r, n) : r;
+    const uint64_t w = y[(size_t(epoch & 1u) * ncols + c) * n + pos];
+    dst[i] = uint32_t(w >> 32) == epoch ? __uint_as_float(uint32_t(w)) : __uint_as_float(0x7fc00000u);
 }
 
 static int pc_take_status() {
@@ -546,7 +789,7 @@ static PcKernel pc_kernel_for(int ncols) {
     }
 }
 
-// Lanes-per-row utilisation of a (rows per tile, lanes per row) shape on rows of nblk blocks
+// Lanes-per-row utilisation of a (rows per stage, lanes per row) shape on rows of nblk blocks
 // (the measure host_lanes_per_row maximises).
 static float pc_util(int nblk, int rpb, int lb) {
     const int rg = 32 / lb;
@@ -555,9 +798,9 @@ static float pc_util(int nblk, int rpb, int lb) {
     return float(nblk) / float(lb * per_lane) * (r < 1.f ? r : 1.f);
 }
 
-static int pc_variant(int rpb, int lb) {
+static int pc_variant(int rpb, int lb, bool glu) {
     for (int v = 0; v < kNumVariants; ++v)
-        if (kVarRpb[v] == rpb && kVarLb[v] == lb) return v;
+        if (kVarRpb[v] == rpb && kVarLb[v] == lb && kVarGlu[v] == glu) return v;
     return -1;
 }
 
@@ -568,23 +811,100 @@ using namespace anvil;
 struct PcGemvHost {
     PcGemv d;
     int rpb_req, K, qk;
+    bool own_y;
 };
 
 struct anvil_pchain {
     int world = 1, rank = 0, ncols = 0;
     std::vector<PcGroup> groups;
+    std::vector<int> group_src;  // source GEMV of a chained group, -1 for a fixed input
     std::vector<PcGemvHost> gemvs;
-    uint32_t *counters[kPcMaxRanks] = {};
-    uint32_t *own_counters = nullptr;
+    std::vector<void *> owned;   // device buffers this chain allocated
     PcGroup *d_groups = nullptr;
     PcGemv *d_gemvs = nullptr;
-    uint32_t **d_counters = nullptr;
+    uint64_t *trace = nullptr;
     PcKernel fn = nullptr;
-    int grid = 0, nwarps = 0, smem = 0, ring_bytes = 0, act_off = 0, ring_off = 0;
-    int first_wait_from = 0;
+    int grid = 0, nwarps = 0, smem = 0, ring_bytes = 0, ring_off = 0;
+    int act_off[2] = {0, 0};
     uint32_t epoch = 0;
     bool ready = false;
 };
+
+namespace {
+
+int pc_push_group(anvil_pchain *c, const float *x, int src, int K) {
+    PcGroup g{};
+    g.x = x;
+    g.src = nullptr;  // resolved at instantiation (the source's buffer may be allocated then)
+    g.K = K;
+    g.first = int(c->gemvs.size());
+    g.count = 0;
+    g.family = -1;
+    c->groups.push_back(g);
+    c->group_src.push_back(src);
+    return int(c->groups.size()) - 1;
+}
+
+int pc_add(anvil_pchain *c, int ggml_type, const void *W, const void *W2, int nrows, int row0,
+           int nrows_full, uint64_t *const *y, int rows_per_block) {
+    if (!c || !W) return fail(ANVIL_ERR_INVALID, "null argument");
+    if (c->ready) return fail(ANVIL_ERR_INVALID, "chain already instantiated");
+    if (c->groups.empty()) return fail(ANVIL_ERR_INVALID, "add a group first");
+    if (int(c->gemvs.size()) >= (1 << 20)) return fail(ANVIL_ERR_INVALID, "too many GEMVs");
+    int qk, bb;
+    if (int s = anvil_type_geometry(ggml_type, &qk, &bb)) return s;
+    if (ggml_type != ANVIL_TYPE_Q8_0 && ggml_type != ANVIL_TYPE_Q4_K && ggml_type != ANVIL_TYPE_Q5_K &&
+        ggml_type != ANVIL_TYPE_Q6_K)
+        return fail(ANVIL_ERR_UNSUPPORTED, "the persistent chain takes Q8_0, Q4_K, Q5_K and Q6_K "
+                                           "weights (type %d)", ggml_type);
+    PcGroup &g = c->groups.back();
+    if (g.K % qk) return fail(ANVIL_ERR_INVALID, "K=%d is not a multiple of the block size %d", g.K, qk);
+    if (nrows < 1 || row0 < 0 || nrows_full < row0 + nrows)
+        return fail(ANVIL_ERR_INVALID, "rows [%d, %d) outside a %d-row matrix", row0, row0 + nrows,
+                    nrows_full);
+    if ((reinterpret_cast<uintptr_t>(W) | reinterpret_cast<uintptr_t>(W2)) & 15)
+        return fail(ANVIL_ERR_ALIGN, "weights must be 16-byte aligned");
+    const int row_bytes = (g.K / qk) * bb;
+    if (W2 && row_bytes % 16)
+        return fail(ANVIL_ERR_ALIGN, "gate/up rows must be a multiple of 16 bytes (%d)", row_bytes);
+    if (y) {
+        for (int q = 0; q < c->world; ++q) {
+            if (!y[q]) return fail(ANVIL_ERR_INVALID, "null output pointer for rank %d", q);
+            if (reinterpret_cast<uintptr_t>(y[q]) & 15)
+                return fail(ANVIL_ERR_ALIGN, "output words must be 16-byte aligned");
+        }
+    } else if (c->world > 1) {
+        return fail(ANVIL_ERR_INVALID, "world > 1 needs every rank's output buffer");
+    }
+    const int family = ggml_type == ANVIL_TYPE_Q8_0 ? 1 : 0;
+    if (g.family >= 0 && g.family != family) {
+        // Q8_0 and the K-quants read the staged activation in different swizzles: continue
+        // in a new group on the same input, restaged.
+        const PcGroup prev = g;
+        pc_push_group(c, prev.x, c->group_src.back(), prev.K);
+    }
+    PcGroup &cur = c->groups.back();
+    cur.family = family;
+    cur.count += 1;
+    PcGemvHost h{};
+    h.d.W = static_cast<const uint8_t *>(W);
+    h.d.W2 = static_cast<const uint8_t *>(W2);
+    if (y)
+        for (int q = 0; q < c->world; ++q) h.d.y[q] = y[q];
+    h.own_y = y == nullptr;
+    h.d.type = ggml_type;
+    h.d.nrows = nrows;
+    h.d.row0 = row0;
+    h.d.nrows_full = nrows_full;
+    h.d.row_bytes = row_bytes;
+    h.rpb_req = rows_per_block;
+    h.K = cur.K;
+    h.qk = qk;
+    c->gemvs.push_back(h);
+    return int(c->gemvs.size()) - 1;
+}
+
+}  // namespace
 
 extern "C" {
 
@@ -607,12 +927,11 @@ void anvil_pchain_destroy(anvil_pchain *c) {
     if (!c) return;
     if (c->d_groups) cudaFree(c->d_groups);
     if (c->d_gemvs) cudaFree(c->d_gemvs);
-    if (c->d_counters) cudaFree(c->d_counters);
-    if (c->own_counters) cudaFree(c->own_counters);
+    for (void *p : c->owned) cudaFree(p);
     delete c;
 }
 
-int anvil_pchain_add_group(anvil_pchain *c, const float *x, int K, int ncols, int wait_prev) {
+int anvil_pchain_add_group(anvil_pchain *c, const float *x, int K, int ncols) {
     if (!c || !x) return fail(ANVIL_ERR_INVALID, "null argument");
     if (c->ready) return fail(ANVIL_ERR_INVALID, "chain already instantiated");
     if (K <= 0 || K % 32 != 0) return fail(ANVIL_ERR_INVALID, "K=%d is not a positive multiple of 32", K);
@@ -622,78 +941,39 @@ int anvil_pchain_add_group(anvil_pchain *c, const float *x, int K, int ncols, in
         return fail(ANVIL_ERR_INVALID, "all groups of a chain have the same ncols");
     if (reinterpret_cast<uintptr_t>(x) & 15) return fail(ANVIL_ERR_ALIGN, "x must be 16-byte aligned");
     c->ncols = ncols;
-    PcGroup g{};
-    g.x = x;
-    g.K = K;
-    g.first = int(c->gemvs.size());
-    g.count = 0;
-    g.family = -1;
-    g.wait_from = g.wait_to = wait_prev ? 1 : 0;  // resolved at instantiation
-    c->groups.push_back(g);
-    return ANVIL_OK;
+    return pc_push_group(c, x, -1, K);
+}
+
+int anvil_pchain_add_group_chained(anvil_pchain *c, int src_gemv) {
+    if (!c) return fail(ANVIL_ERR_INVALID, "null argument");
+    if (c->ready) return fail(ANVIL_ERR_INVALID, "chain already instantiated");
+    if (src_gemv < 0 || src_gemv >= int(c->gemvs.size()))
+        return fail(ANVIL_ERR_INVALID, "source GEMV %d is not an earlier GEMV of the chain", src_gemv);
+    const int K = c->gemvs[src_gemv].d.nrows_full;
+    if (K % 32 != 0)
+        return fail(ANVIL_ERR_INVALID, "a chained input needs a multiple of 32 values (source has %d)", K);
+    c->gemvs[src_gemv].d.perm = 1;
+    return pc_push_group(c, nullptr, src_gemv, K);
 }
 
 int anvil_pchain_add_gemv(anvil_pchain *c, int ggml_type, const void *W, int nrows, int row0,
-                          int nrows_full, float *const *y, int rows_per_block) {
-    if (!c || !W || !y) return fail(ANVIL_ERR_INVALID, "null argument");
-    if (c->ready) return fail(ANVIL_ERR_INVALID, "chain already instantiated");
-    if (c->groups.empty()) return fail(ANVIL_ERR_INVALID, "add a group first");
-    int qk, bb;
-    if (int s = anvil_type_geometry(ggml_type, &qk, &bb)) return s;
-    if (ggml_type != ANVIL_TYPE_Q8_0 && ggml_type != ANVIL_TYPE_Q4_K && ggml_type != ANVIL_TYPE_Q5_K &&
-        ggml_type != ANVIL_TYPE_Q6_K)
-        return fail(ANVIL_ERR_UNSUPPORTED, "the persistent chain takes Q8_0, Q4_K, Q5_K and Q6_K "
-                                           "weights (type %d)", ggml_type);
-    PcGroup &g = c->groups.back();
-    if (g.K % qk) return fail(ANVIL_ERR_INVALID, "K=%d is not a multiple of the block size %d", g.K, qk);
-    if (nrows < 1 || row0 < 0 || nrows_full < row0 + nrows)
-        return fail(ANVIL_ERR_INVALID, "rows [%d, %d) outside a %d-row matrix", row0, row0 + nrows,
-                    nrows_full);
-    if (reinterpret_cast<uintptr_t>(W) & 15)
-        return fail(ANVIL_ERR_ALIGN, "weights must be 16-byte aligned");
-    for (int q = 0; q < c->world; ++q) {
-        if (!y[q]) return fail(ANVIL_ERR_INVALID, "null output pointer for rank %d", q);
-        if (reinterpret_cast<uintptr_t>(y[q]) & 3)
-            return fail(ANVIL_ERR_ALIGN, "outputs must be 4-byte aligned");
-    }
-    const int family = ggml_type == ANVIL_TYPE_Q8_0 ? 1 : 0;
-    if (g.family >= 0 && g.family != family) {
-        // Q8_0 and the K-quants read the staged activation in different swizzles: continue
-        // in a new group on the same input, restaged, with no barrier in between.
-        PcGroup n{};
-        n.x = g.x;
-        n.K = g.K;
-        n.first = int(c->gemvs.size());
-        n.family = -1;
-        n.wait_from = n.wait_to = 0;
-        c->groups.push_back(n);
-    }
-    PcGroup &cur = c->groups.back();
-    cur.family = family;
-    cur.count += 1;
-    PcGemvHost h{};
-    h.d.W = static_cast<const uint8_t *>(W);
-    for (int q = 0; q < c->world; ++q) h.d.y[q] = y[q];
-    h.d.type = ggml_type;
-    h.d.nrows = nrows;
-    h.d.row0 = row0;
-    h.d.nrows_full = nrows_full;
-    h.d.row_bytes = (cur.K / qk) * bb;
-    h.rpb_req = rows_per_block;
-    h.K = cur.K;
-    h.qk = qk;
-    c->gemvs.push_back(h);
-    return ANVIL_OK;
+                          int nrows_full, uint64_t *const *y, int rows_per_block) {
+    return pc_add(c, ggml_type, W, nullptr, nrows, row0, nrows_full, y, rows_per_block);
 }
 
-int anvil_pchain_set_counters(anvil_pchain *c, uint32_t *const *counters) {
-    if (!c || !counters) return fail(ANVIL_ERR_INVALID, "null argument");
+int anvil_pchain_add_glu(anvil_pchain *c, int ggml_type, const void *W_gate, const void *W_up,
+                         int nrows, int row0, int nrows_full, uint64_t *const *y,
+                         int rows_per_block) {
+    if (!W_up) return fail(ANVIL_ERR_INVALID, "null argument");
+    return pc_add(c, ggml_type, W_gate, W_up, nrows, row0, nrows_full, y, rows_per_block);
+}
+
+int anvil_pchain_set_group_dump(anvil_pchain *c, int group, void *out) {
+    if (!c) return fail(ANVIL_ERR_INVALID, "null chain");
     if (c->ready) return fail(ANVIL_ERR_INVALID, "chain already instantiated");
-    for (int q = 0; q < c->world; ++q) {
-        if (!counters[q] || (reinterpret_cast<uintptr_t>(counters[q]) & 3))
-            return fail(ANVIL_ERR_INVALID, "counter array of rank %d is null or misaligned", q);
-        c->counters[q] = counters[q];
-    }
+    if (group < 0 || group >= int(c->groups.size())) return fail(ANVIL_ERR_INVALID, "bad group %d", group);
+    if (reinterpret_cast<uintptr_t>(out) & 3) return fail(ANVIL_ERR_ALIGN, "dump buffer must be 4-byte aligned");
+    c->groups[group].dump = static_cast<uint8_t *>(out);
     return ANVIL_OK;
 }
 
@@ -707,43 +987,49 @@ int anvil_pchain_instantiate(anvil_pchain *c, int nwarps, int ctas_per_sm) {
     if (ctas_per_sm == 0) ctas_per_sm = 1;
     if (nwarps < 1 || nwarps > kMaxWarps) return fail(ANVIL_ERR_INVALID, "nwarps=%d", nwarps);
     if (ctas_per_sm < 1 || ctas_per_sm > 4) return fail(ANVIL_ERR_INVALID, "ctas_per_sm=%d", ctas_per_sm);
-    if (c->world > 1)
-        for (int q = 0; q < c->world; ++q)
-            if (!c->counters[q]) return fail(ANVIL_ERR_INVALID, "world > 1 needs every rank's counters");
+    for (size_t gi = 0; gi < c->groups.size(); ++gi) {
+        const int src = c->group_src[gi];
+        if (src >= 0 && src >= c->groups[gi].first)
+            return fail(ANVIL_ERR_INVALID, "group %zu reads GEMV %d, which is not before it", gi, src);
+    }
     int dev, nsm;
     if (int s = current_device(&dev)) return s;
     if (int s = sm_count(dev, &nsm)) return s;
     c->fn = pc_kernel_for(c->ncols);
 
-    // Shared memory: [mbarriers][activation of the largest group][nwarps rings].
-    int act = 0;
-    for (const PcGroup &g : c->groups) {
-        const int nkb = g.K / 32;
+    // Shared memory: [mbarriers][activation buffer of even groups][of odd groups][nwarps rings].
+    // Group g is staged into buffer g & 1 while group g - 1's tiles may still read the other.
+    int act[2] = {0, 0};
+    for (size_t gi = 0; gi < c->groups.size(); ++gi) {
+        const int nkb = c->groups[gi].K / 32;
         const int b = c->ncols * act_col_bytes(nkb) + 2 * c->ncols * nkb * 4 + 16 + c->ncols * nkb * 8;
-        act = std::max(act, b);
+        act[gi & 1] = std::max(act[gi & 1], (b + 15) & ~15);
     }
-    act = (act + 15) & ~15;
     const int bars = (nwarps * kPcSlots * 8 + 15) & ~15;
-    const int budget = (228 * 1024) / ctas_per_sm - 1024;  // per CTA, less the runtime's reserve
-    const int ring = ((std::min(budget, kMaxSmem) - bars - act) / nwarps) & ~15;
+    const int budget = (228 * 1024) / ctas_per_sm - 1024 - 256;  // per CTA, less the runtime's reserve
+                                                                 // and the static scratch
+    const int ring = ((std::min(budget, kMaxSmem) - bars - act[0] - act[1]) / nwarps) & ~15;
     if (ring < 4096) return fail(ANVIL_ERR_UNSUPPORTED, "no room for weight rings (%d B per warp)", ring);
 
     // Tile shape per GEMV: requested rows per tile (else the built-in default), the lanes per
-    // row that keep the most lanes busy, and at most half a ring per tile.
+    // row that keep the most lanes busy, and at most half a ring per tile.  A gate/up pair
+    // stages h rows of each matrix (rows per stage 2h, h = 1, 2 or 4).
     for (PcGemvHost &h : c->gemvs) {
         const int K = h.K;
         const int nblk = K / h.qk;
+        const bool glu = h.d.W2 != nullptr;
         int rpb = h.rpb_req > 0 ? h.rpb_req : (h.d.nrows < 2048 ? 1 : (K >= 8192 ? 2 : 4));
         rpb = rpb >= 8 ? 8 : rpb >= 4 ? 4 : rpb >= 2 ? 2 : 1;
+        if (glu) rpb = std::max(2, std::min(8, 2 * rpb));
         auto alloc_of = [&](int r) { return ((r * h.d.row_bytes + 32) + 15) & ~15; };
-        while (rpb > 1 && alloc_of(rpb) > ring / 2) rpb >>= 1;
+        while (rpb > (glu ? 2 : 1) && alloc_of(rpb) > ring / 2) rpb >>= 1;
         if (alloc_of(rpb) > ring)
             return fail(ANVIL_ERR_UNSUPPORTED, "a %d-byte row does not fit a %d-byte ring",
                         h.d.row_bytes, ring);
         int best = -1;
         float bu = -1.f;
         for (int lb : {32, 16, 8}) {
-            const int v = pc_variant(rpb, lb);
+            const int v = pc_variant(rpb, lb, glu);
             if (v < 0) continue;
             const float u = pc_util(nblk, rpb, lb);
             if (u > bu + 1e-6f) {
@@ -751,40 +1037,46 @@ int anvil_pchain_instantiate(anvil_pchain *c, int nwarps, int ctas_per_sm) {
                 best = v;
             }
         }
-        if (best < 0) best = pc_variant(rpb, 32);
+        if (best < 0) best = pc_variant(rpb, 32, glu);
         h.d.variant = best;
         h.d.rpb = rpb;
+        h.d.trows = glu ? rpb / 2 : rpb;
         h.d.alloc = alloc_of(rpb);
     }
 
-    // Tiles and barrier spans.
+    // Output buffers the chain owns (world 1, no buffer given): two parities, zeroed.
+    for (PcGemvHost &h : c->gemvs) {
+        if (!h.own_y || h.d.y[0]) continue;
+        const size_t bytes = size_t(2) * c->ncols * h.d.nrows_full * sizeof(uint64_t);
+        void *p = nullptr;
+        cudaError_t e = cudaMalloc(&p, bytes);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(outputs)");
+        c->owned.push_back(p);
+        e = cudaMemset(p, 0, bytes);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMemset(outputs)");
+        h.d.y[0] = static_cast<uint64_t *>(p);
+    }
+
+    // Tiles per group, chained sources.
     std::vector<PcGemv> dg;
     dg.reserve(c->gemvs.size());
     for (const PcGemvHost &h : c->gemvs) dg.push_back(h.d);
-    int last_wait = 0;
     for (size_t gi = 0; gi < c->groups.size(); ++gi) {
         PcGroup &g = c->groups[gi];
         int t = 0;
         for (int m = g.first; m < g.first + g.count; ++m) {
             dg[m].tile_base = t;
-            dg[m].ntiles = (dg[m].nrows + dg[m].rpb - 1) / dg[m].rpb;
+            dg[m].ntiles = (dg[m].nrows + dg[m].trows - 1) / dg[m].trows;
             t += dg[m].ntiles;
         }
         g.ntiles = t;
-        const bool waits = gi > 0 && g.wait_to != 0;
-        if (waits) {
-            g.wait_from = last_wait;
-            g.wait_to = int(gi);
-            last_wait = int(gi);
-        } else {
-            g.wait_from = g.wait_to = 0;
-        }
+        const int src = c->group_src[gi];
+        g.src = src >= 0 ? dg[src].y[c->rank] : nullptr;
     }
-    c->first_wait_from = last_wait;
 
     int occ = 0;
     const int threads = nwarps * 32;
-    const int smem = bars + act + nwarps * ring;
+    const int smem = bars + act[0] + act[1] + nwarps * ring;
     cudaError_t e = cudaFuncSetAttribute(c->fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, c->fn, threads, smem);
@@ -796,8 +1088,9 @@ int anvil_pchain_instantiate(anvil_pchain *c, int nwarps, int ctas_per_sm) {
     c->nwarps = nwarps;
     c->smem = smem;
     c->ring_bytes = ring;
-    c->act_off = bars;
-    c->ring_off = bars + act;
+    c->act_off[0] = bars;
+    c->act_off[1] = bars + act[0];
+    c->ring_off = bars + act[0] + act[1];
     const int nw = c->grid * nwarps;
     long cum = 0;
     for (PcGroup &g : c->groups) {
@@ -815,18 +1108,14 @@ int anvil_pchain_instantiate(anvil_pchain *c, int nwarps, int ctas_per_sm) {
     e = cudaMemcpy(c->d_gemvs, dg.data(), sizeof(PcGemv) * dg.size(), cudaMemcpyHostToDevice);
     if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy(gemvs)");
     for (size_t m = 0; m < dg.size(); ++m) c->gemvs[m].d = dg[m];
-    if (c->world == 1 && !c->counters[0]) {
-        e = cudaMalloc(&c->own_counters, 2 * sizeof(uint32_t) * c->groups.size());
-        if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(counters)");
-        e = cudaMemset(c->own_counters, 0, 2 * sizeof(uint32_t) * c->groups.size());
-        if (e != cudaSuccess) return cuda_fail(e, "cudaMemset(counters)");
-        c->counters[0] = c->own_counters;
-    }
-    e = cudaMalloc(&c->d_counters, sizeof(uint32_t *) * c->world);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(counter table)");
-    e = cudaMemcpy(c->d_counters, c->counters, sizeof(uint32_t *) * c->world, cudaMemcpyHostToDevice);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy(counter table)");
     c->ready = true;
+    return ANVIL_OK;
+}
+
+int anvil_pchain_set_trace(anvil_pchain *c, uint64_t *buf) {
+    if (!c) return fail(ANVIL_ERR_INVALID, "null chain");
+    if (reinterpret_cast<uintptr_t>(buf) & 7) return fail(ANVIL_ERR_ALIGN, "trace buffer must be 8-byte aligned");
+    c->trace = buf;
     return ANVIL_OK;
 }
 
@@ -836,15 +1125,17 @@ int anvil_pchain_launch(anvil_pchain *c, anvil_stream_t stream) {
     PcArgs a{};
     a.groups = c->d_groups;
     a.gemvs = c->d_gemvs;
-    a.counters = c->d_counters;
+    a.trace = c->trace;
+    a.wait_ns = wait_limit_ns();
     a.ngroups = int(c->groups.size());
     a.world = c->world;
     a.rank = c->rank;
-    a.act_off = c->act_off;
+    a.act_off[0] = c->act_off[0];
+    a.act_off[1] = c->act_off[1];
     a.ring_off = c->ring_off;
     a.ring_bytes = c->ring_bytes;
-    a.first_wait_from = c->first_wait_from;
-    a.epoch = c->epoch;
+    a.epoch = c->epoch + 1;
+    if (a.epoch == 0) a.epoch = 1;  // 0 is the flag of zeroed buffers
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(unsigned(c->grid));
     cfg.blockDim = dim3(unsigned(c->nwarps * 32));
@@ -857,7 +1148,27 @@ int anvil_pchain_launch(anvil_pchain *c, anvil_stream_t stream) {
     cfg.numAttrs = 1;
     cudaError_t e = cudaLaunchKernelEx(&cfg, c->fn, a);
     if (e != cudaSuccess) return cuda_fail(e, "persistent chain launch");
-    ++c->epoch;
+    c->epoch = a.epoch;
+    return ANVIL_OK;
+}
+
+int anvil_pchain_epoch(const anvil_pchain *c) {
+    if (!c) return fail(ANVIL_ERR_INVALID, "null chain");
+    return int(c->epoch & 0x7fffffffu);
+}
+
+int anvil_pchain_read_output(const anvil_pchain *c, int index, float *dst, anvil_stream_t stream) {
+    if (!c || !dst) return fail(ANVIL_ERR_INVALID, "null argument");
+    if (!c->ready) return fail(ANVIL_ERR_INVALID, "chain not instantiated");
+    if (index < 0 || index >= int(c->gemvs.size())) return fail(ANVIL_ERR_INVALID, "bad GEMV index");
+    if (c->epoch == 0) return fail(ANVIL_ERR_INVALID, "chain not launched yet");
+    const PcGemv &d = c->gemvs[index].d;
+    const long n = long(c->ncols) * d.nrows_full;
+    const unsigned blocks = unsigned((n + 255) / 256);
+    pchain_read_kernel<<<blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        d.y[c->rank], dst, c->ncols, d.nrows_full, d.perm, c->epoch);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "read_output launch");
     return ANVIL_OK;
 }
 

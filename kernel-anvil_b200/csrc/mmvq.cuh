@@ -40,7 +40,7 @@ namespace anvil {
 constexpr int kMaxWarps = 8;       // 256 threads: llama.cpp's MMVQ upper bound
 constexpr int kMaxCols = 8;        // MMVQ_MAX_BATCH_SIZE
 constexpr int kMaxSmem = 227 * 1024;
-constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s bound on any mbarrier wait
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // default bound on any device wait (2 s)
 
 constexpr int kModeQ81 = 0;
 constexpr int kModeF32 = 1;
@@ -55,6 +55,7 @@ constexpr int kMaxSeg = 4;  // matrices of one launch (GEMVs sharing the activat
 struct MmvqArgs {
     const void *x;      // Q8_1 blocks (kModeQ81 / kModeSums) or fp32 values (kModeF32)
     int32_t *sums;      // kModeSums output (one segment)
+    uint64_t wait_ns;   // bound on every mbarrier wait
     int K, nstages;
     // Segments: GEMVs of one weight type reading x, dealt as one tile sequence.
     // Segment s: weights segW[s] (raw GGUF blocks, row-major), segRows[s] rows, outputs
@@ -967,11 +968,11 @@ __global__ void __launch_bounds__(kMaxWarps * 32, NCOLS == 1 ? 2 : 1)
         const uintptr_t e = MODE == kModeGLU ? 0 : s + size_t(rows) * row_bytes;
         uint8_t *wrow0 = ring + st * L.stage + int(s & 15);
 
-        bool have_w = mbar_wait_bounded(&full[st], phase, kWaitLimitNs);
+        bool have_w = mbar_wait_bounded(&full[st], phase, args.wait_ns);
         if (!have_w) {
             // The copy did not land in time: one more bounded wait so that it is not still
             // writing this stage when the warp moves on; the tile is then skipped.
-            (void)mbar_wait_bounded(&full[st], phase, kWaitLimitNs);
+            (void)mbar_wait_bounded(&full[st], phase, args.wait_ns);
         }
         if ((s | e) & 15) {  // unaligned ends: plain loads of at most 30 bytes
             const uintptr_t s_al = (s + 15) & ~uintptr_t(15), e_al = e & ~uintptr_t(15);

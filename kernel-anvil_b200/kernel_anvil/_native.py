@@ -70,10 +70,39 @@ def _headers() -> list[Path]:
     return sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.h")) + sorted(INCLUDE.glob("*.h"))
 
 
+def _local_deps(src: Path) -> set[Path]:
+    """src and every csrc/ or include/ header it includes, transitively (quoted includes)."""
+    import re
+
+    seen, todo = set(), [src]
+    while todo:
+        f = todo.pop()
+        if f in seen or not f.exists():
+            continue
+        seen.add(f)
+        for name in re.findall(r'^\s*#\s*include\s+"([^"]+)"', f.read_text(), flags=re.M):
+            for d in (f.parent, CSRC, INCLUDE):
+                if (d / name).exists():
+                    todo.append(d / name)
+                    break
+    return seen
+
+
+def _obj(src: Path) -> Path:
+    return OBJ_DIR / (src.name + ".o")
+
+
+def _stale(src: Path) -> bool:
+    obj = _obj(src)
+    return not obj.exists() or obj.stat().st_mtime <= max(p.stat().st_mtime for p in _local_deps(src))
+
+
 def needs_build() -> bool:
     if not LIB_PATH.exists():
         return True
     t = LIB_PATH.stat().st_mtime
+    if OBJ_DIR.exists():  # a source tree with its objects: per-unit dependencies
+        return any(_stale(p) or _obj(p).stat().st_mtime > t for p in _sources())
     return any(p.stat().st_mtime > t for p in _sources() + _headers())
 
 
@@ -87,7 +116,9 @@ def build(force: bool = False, verbose: bool = False, jobs: int | None = None) -
     inc = ["-I", str(INCLUDE), "-I", str(CSRC)]
 
     def compile_one(src: Path) -> Path:
-        obj = OBJ_DIR / (src.name + ".o")
+        obj = _obj(src)
+        if not force and not _stale(src):
+            return obj  # up to date
         if src.suffix == ".cu":
             cmd = [nvcc, *ARCH_FLAGS, *NVCC_FLAGS, *inc, "-c", str(src), "-o", str(obj)]
         else:
@@ -169,14 +200,22 @@ SIGNATURES = {
     "anvil_chain_num_steps": (c_int, [c_void_p]),
     "anvil_pchain_create": (c_void_p, [c_int, c_int]),
     "anvil_pchain_destroy": (None, [c_void_p]),
-    "anvil_pchain_add_group": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int]),
+    "anvil_pchain_add_group": (c_int, [c_void_p, c_void_p, c_int, c_int]),
+    "anvil_pchain_add_group_chained": (c_int, [c_void_p, c_int]),
     "anvil_pchain_add_gemv": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_void_p, c_int]),
-    "anvil_pchain_set_counters": (c_int, [c_void_p, c_void_p]),
+    "anvil_pchain_add_glu": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p,
+                                     c_int]),
+    "anvil_pchain_set_group_dump": (c_int, [c_void_p, c_int, c_void_p]),
     "anvil_pchain_instantiate": (c_int, [c_void_p, c_int, c_int]),
+    "anvil_pchain_set_trace": (c_int, [c_void_p, c_void_p]),
     "anvil_pchain_launch": (c_int, [c_void_p, c_void_p]),
+    "anvil_pchain_epoch": (c_int, [c_void_p]),
+    "anvil_pchain_read_output": (c_int, [c_void_p, c_int, c_void_p, c_void_p]),
     "anvil_pchain_info": (c_int, [c_void_p, _PI, _PI, _PI, _PI, _PI]),
     "anvil_pchain_gemv_shape": (c_int, [c_void_p, c_int, _PI, _PI]),
     "anvil_pchain_take_status": (c_int, []),
+    "anvil_set_wait_limit_ns": (c_int, [ctypes.c_ulonglong]),
+    "anvil_get_wait_limit_ns": (ctypes.c_ulonglong, []),
     "anvil_ipc_alloc": (c_int, [ctypes.c_size_t, ctypes.POINTER(c_void_p), c_void_p]),
     "anvil_ipc_open": (c_int, [c_void_p, ctypes.POINTER(c_void_p)]),
     "anvil_ipc_close": (c_int, [c_void_p]),

@@ -8,6 +8,15 @@ is quantised inside the chain, so the chain carries exactly the quantize + MMVQ 
 
 Shapes are (nrows N, ncols_x K) = (output features, input features).
 
+The decoder chains also record their data flow (``ChainSpec.sources``): which GEMV output
+each activation is computed from, with the ops between GEMVs that are not part of this path
+reduced to what keeps the dependency: the attention output stands in as attn_q's output
+(a vector of the same length), the ffn input as attn_output's, ffn_down's input as
+silu(ffn_gate) * ffn_up, the next layer's attention input as ffn_down's output, and the
+lm_head input as the last ffn_down's.  The persistent executor runs that flow (each group
+reads its producer's output, scaled by a power of two); the graph executor keeps every
+input a fixed synthetic vector.
+
   qwen3_8b      36 layers: q 4096x4096, k/v 1024x4096, o 4096x4096, gate/up 12288x4096,
                 down 4096x12288; Q4_K except Q6_K on attn_v and ffn_down in even layers;
                 lm_head 151936x4096 Q4_K.  253 GEMVs, 145 quantisations per token.
@@ -40,6 +49,9 @@ class ChainSpec:
     name: str
     gemvs: list[Gemv]
     inputs: dict[str, int] = field(default_factory=dict)  # activation id -> K (in first-use order)
+    # activation id -> ("copy", gemv name) or ("glu", gate name, up name): the GEMV output(s)
+    # it is computed from; activations absent here are fixed inputs
+    sources: dict[str, tuple] = field(default_factory=dict)
 
     def unique_shapes(self) -> dict[tuple[str, int, int], int]:
         """{(quant, N, K): count} over the chain's GEMVs."""
@@ -48,6 +60,21 @@ class ChainSpec:
     def algorithmic_bytes(self, ncols: int = 1) -> int:
         return sum(gemv_bytes(g.qt, g.nrows, g.K, ncols) for g in self.gemvs)
 
+    def glu_algorithmic_bytes(self, ncols: int = 1) -> int:
+        """Algorithmic bytes when every gate/up pair is one gate/up GEMV: both weight streams,
+        one activation read and one output vector per pair."""
+        total, i = 0, 0
+        while i < len(self.gemvs):
+            g = self.gemvs[i]
+            if is_gate_up(self.gemvs[i:i + 2]):
+                total += (2 * gemv_bytes(g.qt, g.nrows, g.K, ncols) - 4 * g.nrows * ncols
+                          - gemv_bytes(g.qt, 0, g.K, ncols))
+                i += 2
+            else:
+                total += gemv_bytes(g.qt, g.nrows, g.K, ncols)
+                i += 1
+        return total
+
     def weight_bytes(self) -> int:
         return sum(g.nrows * resolve_type(g.qt).row_bytes(g.K) for g in self.gemvs)
 
@@ -55,8 +82,15 @@ class ChainSpec:
         """The chain's first n GEMVs (with their inputs): a smaller case of the same shapes."""
         gemvs = self.gemvs[:n]
         used = {g.input for g in gemvs}
+        names = {g.name for g in gemvs}
+        sources = {a: src for a, src in self.sources.items()
+                   if a in used and all(nm in names for nm in src[1:])}
         return ChainSpec(name or f"{self.name}[:{n}]", list(gemvs),
-                         {a: k for a, k in self.inputs.items() if a in used})
+                         {a: k for a, k in self.inputs.items() if a in used}, sources)
+
+    def fixed_inputs(self) -> list[str]:
+        """Activations not computed from an earlier GEMV (in first-use order)."""
+        return [a for a in self.inputs if a not in self.sources]
 
 
 def _layered(name: str, n_layers: int, per_layer, tail=()) -> ChainSpec:
@@ -66,10 +100,31 @@ def _layered(name: str, n_layers: int, per_layer, tail=()) -> ChainSpec:
             act = f"{inp}.{layer}"
             spec.inputs.setdefault(act, k)
             spec.gemvs.append(Gemv(f"blk.{layer}.{gname}", qt, n, k, act))
+        blk = f"blk.{layer}"
+        spec.sources[f"attn_out.{layer}"] = ("copy", f"{blk}.attn_q")
+        spec.sources[f"ffn_in.{layer}"] = ("copy", f"{blk}.attn_output")
+        spec.sources[f"ffn_act.{layer}"] = ("glu", f"{blk}.ffn_gate", f"{blk}.ffn_up")
+        if layer > 0:
+            spec.sources[f"attn_in.{layer}"] = ("copy", f"blk.{layer - 1}.ffn_down")
     for gname, qt, n, k, inp in tail:
         spec.inputs.setdefault(inp, k)
         spec.gemvs.append(Gemv(gname, qt, n, k, inp))
+        spec.sources[inp] = ("copy", f"blk.{n_layers - 1}.ffn_down")
+    _check_sources(spec)
     return spec
+
+
+def _check_sources(spec: ChainSpec) -> None:
+    """Every chained activation has its producer's length and a producer that comes first."""
+    rows = {g.name: (i, g.nrows) for i, g in enumerate(spec.gemvs)}
+    first_use = {}
+    for i, g in enumerate(spec.gemvs):
+        first_use.setdefault(g.input, i)
+    for act, src in spec.sources.items():
+        for nm in src[1:]:
+            i, n = rows[nm]
+            if n != spec.inputs[act] or i >= first_use[act]:
+                raise ValueError(f"{spec.name}: {act} cannot be computed from {nm}")
 
 
 def qwen3_8b() -> ChainSpec:
@@ -138,6 +193,13 @@ def is_gate_up(run: list) -> bool:
             and resolve_type(run[0].qt).row_bytes(run[0].K) % 16 == 0)
 
 
+def spec_index(spec: ChainSpec, name: str) -> int:
+    for i, g in enumerate(spec.gemvs):
+        if g.name == name:
+            return i
+    raise KeyError(name)
+
+
 def shard_rows(nrows: int, rank: int, world: int) -> tuple[int, int]:
     """Row range [start, stop) of `rank` when nrows rows are split over `world` ranks.
 
@@ -162,16 +224,19 @@ class DeviceChain:
     quantisation) each ffn_gate/ffn_up pair is one gate/up launch (anvil_mmvq_glu) whose
     silu(gate) * up vector goes to the gate's output; the up output is left unwritten.
     executor="persistent": one persistent kernel per token (pchain.PersistentChain).
-    GEMVs sharing an input form a group, and every group waits for the groups before it
-    (a decoder layer's data flow).  outputs are full (ncols, nrows) vectors; with world > 1
-    they live in CUDA-IPC memory that every rank writes its rows into (needs `dist`).
+    GEMVs sharing an input form a group; each ffn_gate/ffn_up pair is one gate/up GEMV
+    (silu(gate) * up).  With dataflow=True (and a spec that records it) every chained
+    activation is its producer's output, read inside the kernel as it arrives; only the
+    first input is a fixed vector.  Outputs are full (ncols, nrows) vectors read with
+    output(i); with world > 1 every rank writes its rows into every rank's buffer, which
+    lives in CUDA-IPC memory (needs `dist`).
     """
 
     def __init__(self, spec: ChainSpec, ncols: int = 1, seed: int = 0, device="cuda",
                  rank: int = 0, world: int = 1, nwarps: int = 0, rows_per_block: int = 0,
                  configs: dict | None = None, fused: bool = False, coresident: int = 1,
                  executor: str = "graph", dist=None, ctas_per_sm: int = 0, grouped: bool = False,
-                 glu: bool = False):
+                 glu: bool = False, dataflow: bool = True):
         import torch
 
         from kernel_anvil.mmvq import Chain, q8_1_bytes
@@ -208,6 +273,8 @@ class DeviceChain:
         self.chain = None
         self.pchain = None
         self.arena = None
+        self.pidx: list[int | None] = []   # persistent: chain GEMV index of each spec GEMV
+        self.dataflow = False
         if executor == "graph":
             self.xq = {a: torch.empty(q8_1_bytes(k, ncols), dtype=torch.uint8, device=device)
                        for a, k in spec.inputs.items()}
@@ -263,39 +330,73 @@ class DeviceChain:
                                         nwarps=nw, rows_per_block=rpb)
                 self.outputs.append(y)
         else:
-            self._build_persistent(device, nwarps, ctas_per_sm, dist)
+            self._build_persistent(device, nwarps, ctas_per_sm, dist, dataflow)
 
-    def _build_persistent(self, device, nwarps: int, ctas_per_sm: int, dist) -> None:
-        import torch
-
-        from kernel_anvil.pchain import PeerArena, PersistentChain
+    def _build_persistent(self, device, nwarps: int, ctas_per_sm: int, dist, dataflow: bool) -> None:
+        from kernel_anvil.pchain import PeerArena, PersistentChain, output_words_bytes
 
         spec, ncols = self.spec, self.ncols
-        ngroups_max = len(spec.gemvs) + 1
+        sources = spec.sources if dataflow else {}
+        self.dataflow = bool(sources)
+        # chain GEMVs in order: a gate/up pair is one gate/up GEMV, every other GEMV its own
+        items: list[list[int]] = []
+        i = 0
+        while i < len(spec.gemvs):
+            if is_gate_up(spec.gemvs[i:i + 2]):
+                items.append([i, i + 1])
+                i += 2
+            else:
+                items.append([i])
+                i += 1
         if self.world > 1:
             if dist is None:
                 raise ValueError("a sharded persistent chain needs the process group (dist)")
-            layout = [(f"y{i}", ncols * gm.nrows * 4) for i, gm in enumerate(spec.gemvs)]
-            layout.append(("counters", 2 * ngroups_max * 4))  # CTA counts, then rank counts
+            layout = [(f"y{j}", output_words_bytes(spec.gemvs[it[0]].nrows, ncols))
+                      for j, it in enumerate(items)]
             self.arena = PeerArena(layout, dist)
-            for i, gm in enumerate(spec.gemvs):
-                self.outputs.append(self.arena.local_tensor(f"y{i}", (ncols, gm.nrows)))
-        else:
-            for gm in spec.gemvs:
-                self.outputs.append(torch.empty((ncols, gm.nrows), dtype=torch.float32, device=device))
         pc = PersistentChain(self.world, self.rank)
+        self.pidx = [None] * len(spec.gemvs)
         prev = None
-        for i, (gm, W, (r0, r1), (_, rpb)) in enumerate(zip(spec.gemvs, self.weights, self.rows,
-                                                             self.launch_cfg)):
+        for j, it in enumerate(items):
+            gm = spec.gemvs[it[0]]
             if gm.input != prev:
-                pc.add_group(self.x[gm.input], wait=True)
+                src = sources.get(gm.input)
+                if src is None:
+                    pc.add_group(self.x[gm.input])
+                else:
+                    producer = self.pidx[spec_index(spec, src[1])]
+                    if producer is None or (src[0] == "glu" and len(items[producer]) != 2):
+                        raise ValueError(f"{gm.input}: its producer is not a chain GEMV")
+                    pc.add_group_chained(producer)
                 prev = gm.input
-            ys = self.arena.ptrs(f"y{i}") if self.arena else [self.outputs[i].data_ptr()]
-            pc.add_gemv(W, gm.qt, ys, nrows=r1 - r0, row0=r0, nrows_full=gm.nrows, rows_per_block=rpb)
-        if self.arena:
-            pc.set_counters(self.arena.ptrs("counters"))
+            (r0, r1), (_, rpb) = self.rows[it[0]], self.launch_cfg[it[0]]
+            ys = self.arena.ptrs(f"y{j}") if self.arena else None
+            if len(it) == 2:
+                idx = pc.add_glu(self.weights[it[0]], self.weights[it[1]], gm.qt, nrows=r1 - r0, row0=r0,
+                                 nrows_full=gm.nrows, y_ptrs=ys, rows_per_block=rpb)
+            else:
+                idx = pc.add_gemv(self.weights[it[0]], gm.qt, nrows=r1 - r0, row0=r0, nrows_full=gm.nrows,
+                                  y_ptrs=ys, rows_per_block=rpb)
+            assert idx == j
+            for k in it:
+                self.pidx[k] = j
         pc.instantiate(nwarps=nwarps, ctas_per_sm=ctas_per_sm)
         self.pchain = pc
+        self._items = items
+        self.outputs = [None] * len(spec.gemvs)
+
+    def output(self, i: int):
+        """Spec GEMV i's output: (ncols, rows) for the graph executor (this rank's rows), the
+        full (ncols, nrows) vector for the persistent one (for a gate/up pair, the
+        silu(gate) * up vector, under either GEMV's index)."""
+        if self.chain:
+            return self.outputs[i]
+        return self.pchain.output(self.pidx[i])
+
+    @property
+    def external_inputs(self) -> list[str]:
+        """Activations the step takes from outside the chain (copied in every step)."""
+        return self.spec.fixed_inputs() if self.dataflow else list(self.spec.inputs)
 
     @property
     def algorithmic_bytes(self) -> int:

@@ -1,7 +1,7 @@
 """GGUF model parsing: tensor shapes, quant types, unique GEMV workloads, tensor data.
 
 ``parse_gguf`` / ``ModelProfile`` / ``TensorInfo`` / ``print_model_summary`` keep the
-reference's interface and results (kernel_anvil/gguf.py:14-111), including its key
+reference's interface (kernel_anvil/gguf.py:14-111) and parse results, including its key
 convention: ``unique_shapes`` is keyed ``(quant, ne0, ne1)``, the GGUF dims order, which is
 (columns, rows) of the weight matrix (gguf-py gguf_reader.py keeps ``shape = dims`` with
 ne0 first).  ``ModelProfile.gemv_shapes()`` gives the same counts keyed by the true GEMV
@@ -42,15 +42,17 @@ class ModelProfile:
         return dict(out)
 
 
-def _get_string_field(reader, key: str) -> str | None:
-    if key not in reader.fields:
+def _metadata_str(reader, key: str) -> str | None:
+    """A string-valued metadata field, decoded by gguf-py itself (ReaderField.contents()),
+    or None when the key is absent or holds something else."""
+    field = reader.fields.get(key)
+    if field is None:
         return None
-    f = reader.fields[key]
-    if len(f.data) > 0:
-        part = f.parts[f.data[0]]
-        if hasattr(part, "dtype"):
-            return bytes(part).decode("utf-8", errors="replace")
-    return None
+    try:
+        value = field.contents()
+    except (IndexError, ValueError, TypeError):
+        return None
+    return value if isinstance(value, str) else None
 
 
 def parse_gguf(path: str | Path) -> ModelProfile:
@@ -62,8 +64,8 @@ def parse_gguf(path: str | Path) -> ModelProfile:
     from gguf import GGUFReader
 
     reader = GGUFReader(str(path))
-    name = _get_string_field(reader, "general.name") or path.stem
-    arch = _get_string_field(reader, "general.architecture") or "unknown"
+    name = _metadata_str(reader, "general.name") or path.stem
+    arch = _metadata_str(reader, "general.architecture") or "unknown"
     tensors, shapes = [], Counter()
     for t in reader.tensors:
         shape = tuple(int(x) for x in t.shape)
@@ -75,18 +77,20 @@ def parse_gguf(path: str | Path) -> ModelProfile:
 
 
 def print_model_summary(profile: ModelProfile) -> None:
-    n2 = sum(1 for t in profile.tensors if len(t.shape) == 2)
-    total = sum(t.size_bytes for t in profile.tensors)
-    print(f"Model: {profile.name}")
-    print(f"Architecture: {profile.architecture}")
-    print(f"Tensors: {len(profile.tensors)} ({n2} weight, {len(profile.tensors) - n2} other)")
-    print(f"Total size: {total / 1e9:.2f} GB")
-    print()
-    print(f"Unique GEMV workloads ({len(profile.unique_shapes)}):")
-    print(f"  {'Quant':<8} {'N':>8} {'K':>8} {'Count':>6}")
-    print(f"  {'-----':<8} {'-----':>8} {'-----':>8} {'-----':>6}")
-    for (qt, n, k), count in sorted(profile.unique_shapes.items()):
-        print(f"  {qt:<8} {n:>8} {k:>8} {count:>6}")
+    """Human-readable overview: totals, then one line per unique GEMV workload with its true
+    shape (rows x cols) and the GGUF dims key the tuner's JSON uses."""
+    mats = [t for t in profile.tensors if len(t.shape) == 2]
+    gib = sum(t.size_bytes for t in profile.tensors) / 2**30
+    print(f"{profile.name} [{profile.architecture}]: {len(profile.tensors)} tensors, "
+          f"{len(mats)} matrices, {gib:.2f} GiB")
+    if not profile.unique_shapes:
+        print("no 2-D tensors")
+        return
+    width = max(len(qt) for qt, _, _ in profile.unique_shapes)
+    print(f"{len(profile.unique_shapes)} GEMV workloads (rows x cols; GGUF ne0 x ne1 in brackets):")
+    for (qt, ne0, ne1), count in sorted(profile.unique_shapes.items(),
+                                        key=lambda kv: (kv[0][0], -kv[0][2] * kv[0][1])):
+        print(f"  {qt.ljust(width)}  {ne1:>7} x {ne0:<7} [{ne0} x {ne1}]  x{count}")
 
 
 def read_tensor_blocks(path: str | Path, name: str):

@@ -117,12 +117,15 @@ def load_gguf_linears(path, device="cuda") -> dict[str, QuantLinear]:
     from gguf import GGUFReader
 
     out = {}
-    for t in GGUFReader(str(path)).tensors:
-        if len(t.shape) != 2 or t.tensor_type.name not in QUANT_TYPES:
+    for t in GGUFReader(str(path)).tensors:  # one parse of the file for every tensor
+        qt = t.tensor_type.name
+        if len(t.shape) != 2 or qt not in QUANT_TYPES:
             continue
-        if int(t.shape[0]) % resolve_type(t.tensor_type.name).qk:
+        K, nrows = int(t.shape[0]), int(t.shape[1])
+        if K % resolve_type(qt).qk:
             continue
-        out[t.name] = QuantLinear.from_gguf(path, t.name, device=device)
+        blocks = torch.from_numpy(np.ascontiguousarray(t.data).reshape(nrows, -1)).to(device)
+        out[t.name] = QuantLinear(blocks, qt, K, None)
     return out
 
 

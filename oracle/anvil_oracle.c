@@ -17,6 +17,11 @@
  *     xor-butterfly order of a 32-lane warp reduction.  gguf-py has no Q8_1; its Q8_0
  *     quantiser (gguf/quants.py:381-392) is the closest pinned relative and tests
  *     compare against it.
+ *   - Chained-input Q8_1 (the persistent chain's group input computed from an earlier
+ *     GEMV's output; no counterpart in the reference, whose decode quantises every input
+ *     with quantize_q8_1 after ops outside this path): the quants of quantize_q8_1 with d kept
+ *     in fp32, and a per-column power of two 2^-e (e the exponent of the column's largest
+ *     magnitude) applied to the GEMV's result.
  *   - Block dots: the MMVQ arithmetic of vec_dot_{q4_K,q5_K,q6_K,q8_0}_q8_1 as restated
  *     in kernel_anvil/hip_codegen.py:430-491 (with qi = 32, the correct QI4_K of
  *     kernel_anvil/hip_codegen.py:86) and docs/llama-cpp-kernel-analysis.md:200-224:
@@ -155,6 +160,44 @@ void oracle_quantize_q8_1(const float *x, uint8_t *xq, int64_t K, int64_t ncols)
         blk[1] = (uint8_t)(hd >> 8);
         blk[2] = (uint8_t)hs;
         blk[3] = (uint8_t)(hs >> 8);
+    }
+}
+
+/* Chained-input quantisation (the persistent chain's group input computed from an earlier
+ * GEMV's output): per 32-value block the quants of quantize_q8_1 (q = roundf(x / d),
+ * d = amax / 127) with d kept in fp32 at bytes 0-3 of the block; per column the scale
+ * 2^(E - 127), E = clamp(254 - biased exponent of max|x|, 1, 254), which the GEMV applies to
+ * its result (y = scale * sum over blocks). */
+void oracle_quantize_q8_1_chained(const float *x, uint8_t *xq, float *scale, int64_t K,
+                                  int64_t ncols) {
+    for (int64_t c = 0; c < ncols; ++c) {
+        const float *col = x + c * K;
+        float m = 0.0f;
+        for (int64_t i = 0; i < K; ++i) {
+            const float a = fabsf(col[i]);
+            m = a > m ? a : m;
+        }
+        uint32_t mb;
+        memcpy(&mb, &m, 4);
+        int E = 254 - (int)((mb >> 23) & 0xFF);
+        E = E < 1 ? 1 : E > 254 ? 254 : E;
+        const uint32_t sb = (uint32_t)E << 23;
+        memcpy(&scale[c], &sb, 4);
+        for (int64_t b = 0; b < K / 32; ++b) {
+            const float *v = col + b * 32;
+            float amax = 0.0f;
+            for (int l = 0; l < 32; ++l) {
+                const float a = fabsf(v[l]);
+                amax = a > amax ? a : amax;
+            }
+            const float d = amax / 127.0f;
+            uint8_t *blk = xq + (c * (K / 32) + b) * 36;
+            for (int l = 0; l < 32; ++l) {
+                const int q = amax == 0.0f ? 0 : (int)roundf(v[l] / d);
+                blk[4 + l] = (uint8_t)(int8_t)q;
+            }
+            memcpy(blk, &d, 4);
+        }
     }
 }
 
@@ -402,9 +445,18 @@ int oracle_block_sums(int type, const uint8_t *W, const uint8_t *xq, int32_t *su
     return 0;
 }
 
+/* The activation block's d8: fp16 at byte 0 (Q8_1), or fp32 at bytes 0-3 (the chained-input
+ * blocks of the persistent chain). */
+static inline double act_d8(const uint8_t *ab, int d32) {
+    if (!d32) return (double)oracle_half_to_float(rd16(ab));
+    float f;
+    memcpy(&f, ab, 4);
+    return (double)f;
+}
+
 /* y[c*nrows + r] in double from the exact block sums (same formula as the kernels). */
-int oracle_mmvq(int type, const uint8_t *W, const uint8_t *xq, double *y, int64_t nrows,
-                int64_t K, int64_t ncols) {
+static int mmvq_impl(int type, const uint8_t *W, const uint8_t *xq, double *y, int64_t nrows,
+                     int64_t K, int64_t ncols, int d32) {
     const int bytes = type_bytes(type), qk = type_qk(type);
     if (!bytes || K % qk) return -1;
     const int64_t nblk = K / qk, nkb = K / 32;
@@ -422,7 +474,7 @@ int oracle_mmvq(int type, const uint8_t *W, const uint8_t *xq, double *y, int64_
                     int32_t s = 0;
                     for (int e = 0; e < 32; ++e) s += (int32_t)(int8_t)blk[2 + e] * a[e];
                     acc += (double)oracle_half_to_float(rd16(blk)) *
-                           (double)oracle_half_to_float(rd16(ab)) * (double)s;
+                           (double)act_d8(ab, d32) * (double)s;
                     continue;
                 }
                 if (is_basic(type)) {
@@ -434,7 +486,7 @@ int oracle_mmvq(int type, const uint8_t *W, const uint8_t *xq, double *y, int64_
                         s += basic_quant(type, blk, e) * a[e];
                         sq += a[e];
                     }
-                    const double d8 = oracle_half_to_float(rd16(ab));
+                    const double d8 = act_d8(ab, d32);
                     acc += (double)oracle_half_to_float(rd16(blk)) * d8 * (double)s;
                     if (type == T_Q4_1 || type == T_Q5_1)
                         acc += (double)oracle_half_to_float(rd16(blk + 2)) * d8 * (double)sq;
@@ -446,7 +498,7 @@ int oracle_mmvq(int type, const uint8_t *W, const uint8_t *xq, double *y, int64_
                     int32_t s = 0;
                     for (int e = 0; e < 32; ++e) s += iq4nl_level(blk + 2, e) * a[e];
                     acc += (double)oracle_half_to_float(rd16(blk)) *
-                           (double)oracle_half_to_float(rd16(ab)) * (double)s;
+                           (double)act_d8(ab, d32) * (double)s;
                     continue;
                 }
                 if (type == T_IQ4_XS) {
@@ -457,7 +509,7 @@ int oracle_mmvq(int type, const uint8_t *W, const uint8_t *xq, double *y, int64_
                         const int8_t *a = (const int8_t *)(ab + 4);
                         int32_t s = 0;
                         for (int e = 0; e < 32; ++e) s += iq4nl_level(blk + 8 + 16 * j, e) * a[e];
-                        sb += (double)oracle_half_to_float(rd16(ab)) * (double)iq4xs_scale(blk, j) * (double)s;
+                        sb += (double)act_d8(ab, d32) * (double)iq4xs_scale(blk, j) * (double)s;
                     }
                     acc += (double)oracle_half_to_float(rd16(blk)) * sb;
                     continue;
@@ -477,7 +529,7 @@ int oracle_mmvq(int type, const uint8_t *W, const uint8_t *xq, double *y, int64_
                             si += (type == T_Q2_K ? q2k_quant(blk, w) : q3k_quant(blk, w)) * a[e];
                             sq += a[e];
                         }
-                        const double d8 = oracle_half_to_float(rd16(ab));
+                        const double d8 = act_d8(ab, d32);
                         const int sc = type == T_Q2_K ? (blk[j] & 15) : q3k_scale(blk, j);
                         sd += d8 * (double)sc * (double)si;
                         if (type == T_Q2_K) sm += d8 * (double)(blk[j] >> 4) * (double)sq;
@@ -495,7 +547,7 @@ int oracle_mmvq(int type, const uint8_t *W, const uint8_t *xq, double *y, int64_
                         for (int e = 0; e < 16; ++e) s0 += q6k_quant(blk, j, e) * a[e];
                         for (int e = 16; e < 32; ++e) s1 += q6k_quant(blk, j, e) * a[e];
                         const int32_t sc0 = (int8_t)blk[192 + 2 * j], sc1 = (int8_t)blk[193 + 2 * j];
-                        sb += (double)oracle_half_to_float(rd16(ab)) *
+                        sb += (double)act_d8(ab, d32) *
                               ((double)sc0 * (double)s0 + (double)sc1 * (double)s1);
                     }
                     acc += d * sb;
@@ -514,7 +566,7 @@ int oracle_mmvq(int type, const uint8_t *W, const uint8_t *xq, double *y, int64_
                     }
                     int sc, m;
                     q4k_scale_min(blk + 4, j, &sc, &m);
-                    const double d8 = oracle_half_to_float(rd16(ab));
+                    const double d8 = act_d8(ab, d32);
                     sd += d8 * (double)sc * (double)si;
                     sm += d8 * (double)m * (double)sq;
                 }
@@ -523,6 +575,17 @@ int oracle_mmvq(int type, const uint8_t *W, const uint8_t *xq, double *y, int64_
             y[c * nrows + r] = acc;
         }
     return 0;
+}
+
+int oracle_mmvq(int type, const uint8_t *W, const uint8_t *xq, double *y, int64_t nrows,
+                int64_t K, int64_t ncols) {
+    return mmvq_impl(type, W, xq, y, nrows, K, ncols, 0);
+}
+
+/* oracle_mmvq on blocks whose d8 is fp32 (bytes 0-3), unscaled. */
+int oracle_mmvq_d32(int type, const uint8_t *W, const uint8_t *xq, double *y, int64_t nrows,
+                    int64_t K, int64_t ncols) {
+    return mmvq_impl(type, W, xq, y, nrows, K, ncols, 1);
 }
 
 int oracle_num_threads(void) {

@@ -37,6 +37,8 @@ def lib() -> ctypes.CDLL:
         P = ctypes.c_void_p
         I64 = ctypes.c_int64
         h.oracle_quantize_q8_1.argtypes = [P, P, I64, I64]
+        h.oracle_quantize_q8_1_chained.argtypes = [P, P, P, I64, I64]
+        h.oracle_mmvq_d32.argtypes = [ctypes.c_int, P, P, P, I64, I64, I64]
         h.oracle_dequant.argtypes = [ctypes.c_int, P, P, I64, I64]
         h.oracle_block_sums.argtypes = [ctypes.c_int, P, P, P, I64, I64, I64]
         h.oracle_mmvq.argtypes = [ctypes.c_int, P, P, P, I64, I64, I64]
@@ -66,6 +68,38 @@ def quantize_q8_1(x: np.ndarray) -> np.ndarray:
     out = np.empty((ncols, K // 32 * 36), dtype=np.uint8)
     lib().oracle_quantize_q8_1(_ptr(x), _ptr(out), K, ncols)
     return out
+
+
+def quantize_q8_1_chained(x: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+    """The persistent chain's chained-input quantisation of x (ncols, K): Q8_1-shaped blocks
+    with the quants of quantize_q8_1 and d in fp32 (bytes 0-3), and per column the power of
+    two 2^-e (e = exponent of the column's max |x|) that the GEMV applies to its result."""
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, x.shape[-1])
+    ncols, K = x.shape
+    out = np.empty((ncols, K // 32 * 36), dtype=np.uint8)
+    scale = np.empty(ncols, dtype=np.float32)
+    lib().oracle_quantize_q8_1_chained(_ptr(x), _ptr(out), _ptr(scale), K, ncols)
+    return out, scale
+
+
+def mmvq_chained(qt, W: np.ndarray, xq: np.ndarray, scale: np.ndarray, nrows: int, K: int,
+                 ncols: int = 1) -> np.ndarray:
+    """y (ncols, nrows) float64 of a chained group: the block formula with fp32 d8, times the
+    column's scale."""
+    out = np.empty((ncols, nrows), dtype=np.float64)
+    W = np.ascontiguousarray(W, dtype=np.uint8)
+    xq = np.ascontiguousarray(xq, dtype=np.uint8)
+    if lib().oracle_mmvq_d32(_tid(qt), _ptr(W), _ptr(xq), _ptr(out), nrows, K, ncols) != 0:
+        raise ValueError("bad type or K")
+    return out * np.asarray(scale, dtype=np.float64).reshape(ncols, 1)
+
+
+def mmvq_glu_chained(qt, W_gate: np.ndarray, W_up: np.ndarray, xq: np.ndarray, scale: np.ndarray,
+                     nrows: int, K: int) -> np.ndarray:
+    """silu(g) * u (1, nrows) float64 of a chained gate/up pair (g, u scaled first)."""
+    g = mmvq_chained(qt, W_gate, xq, scale, nrows, K)
+    u = mmvq_chained(qt, W_up, xq, scale, nrows, K)
+    return g / (1.0 + np.exp(-g)) * u
 
 
 def dequantize(qt, W: np.ndarray, nrows: int, K: int) -> np.ndarray:

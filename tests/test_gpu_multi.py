@@ -1,9 +1,13 @@
-"""Row-sharded persistent chain on 2 GPUs: every rank writes its output rows into every
-rank's buffer (CUDA IPC peer stores) and the group barriers count the CTAs of both ranks.
-The gathered outputs must equal each rank's own single-GEMV results, concatenated.
+"""Row-sharded persistent chain on 2 GPUs: every rank writes its output rows, as flagged
+words, into every rank's buffer (CUDA IPC peer stores), and each chained group reads the
+gathered output of its producer as the words arrive.
 
-Runs as two spawned processes, one per GPU (NCCL only for set-up and the check); skipped
-with fewer than two GPUs."""
+Checks, on every rank: the gathered outputs of every GEMV hold no stale or missing value;
+this rank's rows of every GEMV match the oracle computed from the gathered input (the
+fixed vector, or the producer's gathered output under the chained-input rule); and the
+gathered vectors are identical on both ranks.  Runs as two spawned processes, one per GPU
+(NCCL with NVLS off, only for set-up and the comparison); skipped with fewer than two
+GPUs."""
 import os
 import socket
 from datetime import timedelta
@@ -23,51 +27,63 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, out_dir):
+def _worker(rank, world, port, out_dir, spec_name, ngemv):
     import sys
     from pathlib import Path
 
     repo = Path(__file__).resolve().parent.parent
-    for p in (repo / "kernel-anvil_b200", repo):
+    for p in (repo / "kernel-anvil_b200", repo, repo / "tests"):
         sys.path.insert(0, str(p))
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
-    from kernel_anvil import mmvq as ops
+    from chain_oracle import check_chain
     from kernel_anvil.chains import DeviceChain, get_chain
     from kernel_anvil.pchain import take_status
 
-    ok = True
+    msg = "ok"
+    dc = None
     try:
-        spec = get_chain("qwen3_8b").head(14)
-        dc = DeviceChain(spec, rank=rank, world=world, executor="persistent", dist=dist)
-        for _ in range(3):  # three tokens: the cross-rank barrier epochs advance
+        spec = get_chain(spec_name).head(ngemv)
+        dc = DeviceChain(spec, rank=rank, world=world, executor="persistent", dist=dist, seed=0)
+        for _ in range(3):  # three tokens: epochs 1..3, both output parities
             dc.launch()
         torch.cuda.synchronize()
         dist.barrier()
-        ok &= take_status() == 0
-        for i, gm in enumerate(spec.gemvs):
-            rpb, _ = dc.pchain.gemv_shape(i)
-            r0, r1 = dc.rows[i]
-            local = ops.mmvq(dc.weights[i], gm.qt, ops.quantize_q8_1(dc.x[gm.input]), nrows=r1 - r0,
-                             K=gm.K, rows_per_block=rpb).view(-1)
-            parts = [torch.empty(gm.nrows // world, device="cuda") for _ in range(world)]
-            dist.all_gather(parts, local.contiguous())
-            want = torch.cat(parts)
-            got = dc.outputs[i].view(-1)
-            if not torch.allclose(got, want, rtol=1e-5, atol=1e-5 * float(want.abs().max())):
-                ok = False
+        status = take_status()
+        if status:
+            msg = f"device status {status}"
+        worst = check_chain(dc)
+        for j in range(dc.pchain.n_gemv):
+            mine = dc.pchain.output(j)
+            other = torch.empty_like(mine)
+            # rank 0 sends its gathered vector to rank 1 and receives rank 1's
+            if rank == 0:
+                dist.send(mine, 1)
+                dist.recv(other, 1)
+            else:
+                dist.recv(other, 0)
+                dist.send(mine, 0)
+            if not torch.equal(mine, other):
+                msg = f"chain GEMV {j}: gathered outputs differ between ranks"
+        if msg == "ok":
+            msg = f"ok {worst:.2e}"
         dist.barrier()
-        dc.close()
+    except AssertionError as e:
+        msg = f"fail: {e}"
     finally:
-        Path(out_dir, f"rank{rank}.txt").write_text("ok" if ok else "fail")
+        if dc is not None:
+            dc.close()
+        Path(out_dir, f"rank{rank}.txt").write_text(msg)
         dist.destroy_process_group()
 
 
-def test_sharded_persistent_chain_two_gpus(tmp_path):
+@pytest.mark.parametrize("spec_name,ngemv", [("qwen3_8b", 15), ("llama3_70b", 8)])
+def test_sharded_dataflow_chain_two_gpus(tmp_path, spec_name, ngemv):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
-    mp.start_processes(_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True,
-                       start_method="spawn")
-    assert [(tmp_path / f"rank{r}.txt").read_text() for r in range(2)] == ["ok", "ok"]
+    mp.start_processes(_worker, args=(2, _free_port(), str(tmp_path), spec_name, ngemv), nprocs=2,
+                       join=True, start_method="spawn")
+    res = [(tmp_path / f"rank{r}.txt").read_text() for r in range(2)]
+    assert all(r.startswith("ok") for r in res), res

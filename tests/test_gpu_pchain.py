@@ -1,25 +1,29 @@
 """The persistent chain kernel (anvil_pchain_*) on one GPU.
 
-Every GEMV of a persistent chain must equal what anvil_mmvq computes for the same rows:
-bit for bit when the chain picked the same rows per tile and lanes per row as the
-single-GEMV launch (same arithmetic, same reduction order), else within the fp32 output
-tolerance against the oracle.  Also: repeated launches (the barrier epochs), groups
-mixing weight types, the in-kernel quantisation against the quantiser, argument errors."""
+Fixed-input GEMVs must equal what anvil_mmvq computes for the same rows: bit for bit when
+the chain picked the same rows per tile and lanes per row as the single-GEMV launch, else
+within the fp32 output tolerance against the oracle.  Chained groups (inputs computed from
+earlier outputs inside the kernel) are checked against the oracle GEMV by GEMV, and their
+in-kernel quantisation (quants and fp32 d8) bit for bit against the oracle's chained-input
+rule.  Also: repeated
+launches (epochs and the two output parities), gate/up pairs, a wait that runs out, and
+argument errors."""
 import numpy as np
 import pytest
 
 torch = pytest.importorskip("torch")
 
+from chain_oracle import Y_TOL, check_chain  # noqa: E402
 from kernel_anvil import mmvq as ops  # noqa: E402
-from kernel_anvil._native import AnvilError  # noqa: E402
+from kernel_anvil._native import ANVIL_ERR_TIMEOUT, AnvilError  # noqa: E402
 from kernel_anvil.chains import DeviceChain, get_chain  # noqa: E402
 from kernel_anvil.mmvq import host_lanes_per_row  # noqa: E402
-from kernel_anvil.pchain import PersistentChain, take_status  # noqa: E402
+from kernel_anvil.pchain import (PersistentChain, output_words_bytes, raise_on_status,  # noqa: E402
+                                 set_wait_limit_ns, take_status, trace_summary)
 from kernel_anvil.quants import make_activation, make_weights, resolve_type  # noqa: E402
 from oracle import oracle  # noqa: E402
 
 pytestmark = pytest.mark.gpu
-Y_TOL = 1e-3
 
 
 def dev(a):
@@ -43,7 +47,7 @@ def _check_against_single(pc, idx, W, qt, x, y, nrows, K):
     assert oracle.max_rel_err(y.cpu().numpy(), y_ref) <= Y_TOL
 
 
-# groups: (K, [(qt, nrows, rows_per_block)]) sharing the group's input
+# groups: (K, [(qt, nrows, rows_per_block)]) sharing the group's fixed input
 CASES = {
     "one_q4k": [(4096, [("Q4_K", 4096, 0)])],
     "qkv_mixed": [(4096, [("Q4_K", 4096, 0), ("Q4_K", 1024, 0), ("Q6_K", 1024, 0)]),
@@ -60,27 +64,28 @@ CASES = {
 
 @pytest.mark.parametrize("case", sorted(CASES))
 @pytest.mark.parametrize("ncols", [1, 2])
-def test_pchain_matches_single_gemv(case, ncols):
+def test_pchain_fixed_inputs_match_single_gemv(case, ncols):
     pc = PersistentChain()
     items = []
     seed = 10
     for K, gemvs in CASES[case]:
         x = dev(make_activation(K, ncols=ncols, seed=seed))
-        pc.add_group(x, wait=True)
+        pc.add_group(x)
         for qt, nrows, rpb in gemvs:
             seed += 1
             W = dev(make_weights(qt, nrows, K, seed=seed))
-            y = torch.full((ncols, nrows), float("nan"), device="cuda")
-            pc.add_gemv(W, qt, y, nrows=nrows, rows_per_block=rpb)
-            items.append((W, qt, x, y, nrows, K))
+            idx = pc.add_gemv(W, qt, nrows=nrows, rows_per_block=rpb)
+            items.append((idx, W, qt, x, nrows, K))
     pc.instantiate()
-    for _ in range(3):  # three launches: the barrier targets advance per launch
+    for _ in range(3):  # three launches: epochs 1..3, both output parities
         pc.launch()
     torch.cuda.synchronize()
     assert take_status() == 0
-    for i, (W, qt, x, y, nrows, K) in enumerate(items):
+    assert pc.epoch == 3
+    for idx, W, qt, x, nrows, K in items:
+        y = pc.output(idx)
         assert not torch.isnan(y).any()
-        _check_against_single(pc, i, W, qt, x, y, nrows, K)
+        _check_against_single(pc, idx, W, qt, x, y, nrows, K)
     pc.close()
 
 
@@ -88,30 +93,138 @@ def test_pchain_repeated_launches_identical():
     K, nrows = 4096, 3000
     x = dev(make_activation(K, seed=3))
     W = dev(make_weights("Q4_K", nrows, K, seed=4))
-    y = torch.empty((1, nrows), device="cuda")
     pc = PersistentChain()
     pc.add_group(x)
-    pc.add_gemv(W, "Q4_K", y, nrows=nrows)
+    pc.add_gemv(W, "Q4_K", nrows=nrows)
     pc.instantiate(nwarps=4, ctas_per_sm=2)
     pc.launch()
-    torch.cuda.synchronize()
-    first = y.clone()
-    for _ in range(20):
+    first = pc.output(0)
+    for _ in range(21):  # ends on the other parity
         pc.launch()
     torch.cuda.synchronize()
-    assert torch.equal(first, y)
+    assert torch.equal(first, pc.output(0))
     # new input values in the same buffer are picked up by the next launch
     x.mul_(-2.0)
     pc.launch()
     torch.cuda.synchronize()
-    assert torch.equal(y, _single(W, "Q4_K", x, pc.gemv_shape(0)[0]))
+    assert torch.equal(pc.output(0), _single(W, "Q4_K", x.view(1, -1), pc.gemv_shape(0)[0]))
     pc.close()
 
 
-def test_device_chain_persistent_equals_graph():
+def _decoder(pc, K=1024, inter=3072, seed=40, types=("Q4_K", "Q6_K", "Q8_0")):
+    """A two-layer decoder-shaped chain with every chained input kind: q/k/v on a fixed x,
+    o on q's output, a gate/up pair on o's, down on silu(gate)*up, and the next layer's
+    q on down's output.  Returns the GEMV descriptions for the oracle."""
+    qa, qb, qc = types
+    rng_seed = [seed]
+
+    def w(qt, n, k):
+        rng_seed[0] += 1
+        return dev(make_weights(qt, n, k, seed=rng_seed[0]))
+
+    desc = []
+    x = dev(make_activation(K, seed=seed))
+    g0 = pc.add_group(x)
+    Wq, Wk, Wv = w(qa, K, K), w(qa, 256, K), w(qb, 256, K)
+    iq = pc.add_gemv(Wq, qa, nrows=K)
+    desc += [(iq, "plain", qa, Wq, None, K, K, ("fixed", x))]
+    desc += [(pc.add_gemv(Wk, qa, nrows=256), "plain", qa, Wk, None, 256, K, ("fixed", x))]
+    desc += [(pc.add_gemv(Wv, qb, nrows=256), "plain", qb, Wv, None, 256, K, ("fixed", x))]
+    g1 = pc.add_group_chained(iq)
+    Wo = w(qa, K, K)
+    io = pc.add_gemv(Wo, qa, nrows=K)
+    desc += [(io, "plain", qa, Wo, None, K, K, ("chained", iq))]
+    g2 = pc.add_group_chained(io)
+    Wg, Wu = w(qa, inter, K), w(qa, inter, K)
+    iglu = pc.add_glu(Wg, Wu, qa, nrows=inter)
+    desc += [(iglu, "glu", qa, Wg, Wu, inter, K, ("chained", io))]
+    g3 = pc.add_group_chained(iglu)
+    Wd = w(qb, K, inter)
+    idn = pc.add_gemv(Wd, qb, nrows=K)
+    desc += [(idn, "plain", qb, Wd, None, K, inter, ("chained", iglu))]
+    g4 = pc.add_group_chained(idn)
+    Wq2 = w(qc, K, K)
+    desc += [(pc.add_gemv(Wq2, qc, nrows=K), "plain", qc, Wq2, None, K, K, ("chained", idn))]
+    return desc, (g0, g1, g2, g3, g4)
+
+
+def _oracle_check(pc, desc):
+    outs = {d[0]: pc.output(d[0]).cpu().numpy() for d in desc}
+    for idx, kind, qt, W, W2, n, K, (how, src) in desc:
+        assert not np.isnan(outs[idx]).any(), f"GEMV {idx}: values missing"
+        if how == "fixed":
+            xq, scale = oracle.quantize_q8_1(src.cpu().numpy()), None
+        else:
+            xq, scale = oracle.quantize_q8_1_chained(outs[src])
+        if kind == "glu":
+            W2n = W2.cpu().numpy()
+            ref = (oracle.mmvq_glu(qt, W.cpu().numpy(), W2n, xq, n, K) if scale is None else
+                   oracle.mmvq_glu_chained(qt, W.cpu().numpy(), W2n, xq, scale, n, K))
+        else:
+            ref = (oracle.mmvq(qt, W.cpu().numpy(), xq, n, K) if scale is None else
+                   oracle.mmvq_chained(qt, W.cpu().numpy(), xq, scale, n, K))
+        err = oracle.max_rel_err(outs[idx], ref)
+        assert err <= Y_TOL, f"GEMV {idx} ({kind} {qt} {n}x{K}): error {err}"
+    return outs
+
+
+@pytest.mark.parametrize("types", [("Q4_K", "Q6_K", "Q8_0"), ("Q5_K", "Q8_0", "Q4_K")])
+def test_pchain_chained_groups_match_oracle(types):
+    pc = PersistentChain()
+    desc, groups = _decoder(pc, types=types)
+    # the chained groups' staged Q8_1, written out by the kernel, against the oracle's rule
+    dumps = {g: torch.zeros(1024 // 32 * 36 if g != groups[3] else 3072 // 32 * 36, dtype=torch.uint8,
+                            device="cuda") for g in groups[1:]}
+    for g, buf in dumps.items():
+        pc.set_group_dump(g, buf)
+    pc.instantiate()
+    for _ in range(3):
+        pc.launch()
+    torch.cuda.synchronize()
+    assert take_status() == 0
+    outs = _oracle_check(pc, desc)
+    src_of = {groups[1]: desc[0][0], groups[2]: desc[3][0], groups[3]: desc[4][0], groups[4]: desc[5][0]}
+    for g, buf in dumps.items():
+        want = oracle.quantize_q8_1_chained(outs[src_of[g]])[0].reshape(-1)
+        assert np.array_equal(buf.cpu().numpy(), want), f"group {g}: staged Q8_1 differs from the oracle"
+    pc.close()
+
+
+def test_pchain_chain_trace_and_epochs():
+    pc = PersistentChain()
+    desc, groups = _decoder(pc)
+    pc.instantiate()
+    trace = pc.enable_trace()
+    for _ in range(4):
+        pc.launch()
+    torch.cuda.synchronize()
+    assert take_status() == 0 and pc.epoch == 4
+    _oracle_check(pc, desc)
+    summ = trace_summary(trace)
+    assert len(summ) == len(groups)
+    for g, s in enumerate(summ):
+        assert s["stage_start"][0] <= s["stage_end"][1] <= s["staged"][1] <= s["tiles_done"][1]
+        if g:  # a group's staging barrier comes after the previous group's staging barrier
+            assert s["staged"][0] >= summ[g - 1]["staged"][0]
+    pc.close()
+
+
+def test_device_chain_dataflow_matches_oracle():
     spec = get_chain("qwen3_8b").head(14)  # two decoder layers, both Q6_K mixes
+    dc = DeviceChain(spec, executor="persistent")
+    assert dc.dataflow and dc.external_inputs == ["attn_in.0"]
+    for _ in range(2):
+        dc.launch()
+    torch.cuda.synchronize()
+    assert take_status() == 0 and ops.take_device_status() == 0
+    check_chain(dc)
+    dc.close()
+
+
+def test_device_chain_fixed_inputs_equal_graph():
+    spec = get_chain("qwen3_8b").head(14)
     a = DeviceChain(spec, executor="graph")
-    b = DeviceChain(spec, executor="persistent")
+    b = DeviceChain(spec, executor="persistent", dataflow=False)
     stream = torch.cuda.Stream()
     with torch.cuda.stream(stream):
         a.instantiate()
@@ -119,27 +232,91 @@ def test_device_chain_persistent_equals_graph():
         b.launch()
     torch.cuda.synchronize()
     assert take_status() == 0 and ops.take_device_status() == 0
-    for ya, yb in zip(a.outputs, b.outputs):
-        torch.testing.assert_close(yb, ya, rtol=1e-5, atol=1e-5 * float(ya.abs().max()))
+    for i, gm in enumerate(spec.gemvs):
+        if b._items[b.pidx[i]] != [i]:
+            continue  # gate/up pairs: silu(gate) * up, checked by check_chain
+        torch.testing.assert_close(b.output(i), a.outputs[i], rtol=1e-5,
+                                   atol=1e-5 * float(a.outputs[i].abs().max()))
+    check_chain(b)
     a.close()
     b.close()
+
+
+def test_pchain_input_wait_times_out_and_recovers():
+    """A chained group whose producer rows never arrive: a two-rank chain built on one GPU
+    whose "peer" output buffers are local zeroed buffers that no other rank writes.  Rank 0
+    writes its rows; the chained group waits for rank 1's rows, gives up after the 10 ms
+    bound, and the host reads the flag as ANVIL_ERR_TIMEOUT.  A rebuilt one-rank chain then
+    matches the oracle."""
+    K, n = 1024, 1024
+    x = dev(make_activation(K, seed=5))
+    Wq = dev(make_weights("Q4_K", n, K, seed=6))
+    Wo = dev(make_weights("Q4_K", n, K, seed=7))
+    bufs = [torch.zeros(output_words_bytes(n) // 8, dtype=torch.int64, device="cuda") for _ in range(4)]
+    set_wait_limit_ns(10_000_000)
+    try:
+        pc = PersistentChain(world=2, rank=0)
+        pc.add_group(x)
+        iq = pc.add_gemv(Wq[: n // 2], "Q4_K", nrows=n // 2, row0=0, nrows_full=n,
+                         y_ptrs=[bufs[0].data_ptr(), bufs[1].data_ptr()])
+        pc.add_group_chained(iq)
+        pc.add_gemv(Wo[: n // 2], "Q4_K", nrows=n // 2, row0=0, nrows_full=n,
+                    y_ptrs=[bufs[2].data_ptr(), bufs[3].data_ptr()])
+        pc.instantiate()
+        pc.launch()
+        torch.cuda.synchronize()  # the launch ends: every wait is bounded
+        status = take_status()
+        assert status & 2, f"status {status}: the input wait did not report"
+        with pytest.raises(AnvilError) as e:
+            raise_on_status(status)
+        assert e.value.status == ANVIL_ERR_TIMEOUT
+        pc.close()
+    finally:
+        set_wait_limit_ns(0)
+    assert take_status() == 0
+    # the context is still usable: a one-rank chain of the same GEMVs matches the oracle
+    pc = PersistentChain()
+    pc.add_group(x)
+    iq = pc.add_gemv(Wq, "Q4_K", nrows=n)
+    pc.add_group_chained(iq)
+    io = pc.add_gemv(Wo, "Q4_K", nrows=n)
+    pc.instantiate()
+    pc.launch()
+    torch.cuda.synchronize()
+    assert take_status() == 0
+    yq = pc.output(iq).cpu().numpy()
+    ref_q = oracle.mmvq("Q4_K", Wq.cpu().numpy(), oracle.quantize_q8_1(x.cpu().numpy()), n, K)
+    assert oracle.max_rel_err(yq, ref_q) <= Y_TOL
+    xo, so = oracle.quantize_q8_1_chained(yq)
+    ref_o = oracle.mmvq_chained("Q4_K", Wo.cpu().numpy(), xo, so, n, K)
+    assert oracle.max_rel_err(pc.output(io).cpu().numpy(), ref_o) <= Y_TOL
+    pc.close()
 
 
 def test_pchain_argument_errors():
     pc = PersistentChain()
     W = torch.zeros(144 * 16, dtype=torch.uint8, device="cuda")
-    y = torch.zeros(16, device="cuda")
     with pytest.raises(AnvilError, match="add a group first"):
-        pc.add_gemv(W, "Q4_K", y, nrows=1)
+        pc.add_gemv(W, "Q4_K", nrows=1)
     with pytest.raises(AnvilError, match="ncols"):
         pc.add_group(torch.zeros((3, 256), device="cuda"))
     with pytest.raises(AnvilError, match="multiple of 32"):
         pc.add_group(torch.zeros(100, device="cuda"))
+    with pytest.raises(AnvilError, match="earlier GEMV"):
+        pc.add_group_chained(0)
     pc.add_group(torch.zeros(512, device="cuda"))
     with pytest.raises(AnvilError, match="outside"):
-        pc.add_gemv(W, "Q4_K", y, nrows=4, row0=2, nrows_full=5)
+        pc.add_gemv(W, "Q4_K", nrows=4, row0=2, nrows_full=5)
+    with pytest.raises(AnvilError, match="multiple of 16 bytes"):
+        pc.add_glu(torch.zeros(210 * 4, dtype=torch.uint8, device="cuda"),
+                   torch.zeros(210 * 4, dtype=torch.uint8, device="cuda"), "Q6_K", nrows=2)
     with pytest.raises(AnvilError, match="empty|no GEMV"):
         pc.instantiate()
+    pc.close()
+    pc = PersistentChain(world=2, rank=1)
+    pc.add_group(torch.zeros(512, device="cuda"))
+    with pytest.raises(AnvilError, match="every rank's output"):
+        pc.add_gemv(W, "Q4_K", nrows=1)
     pc.close()
 
 
@@ -166,17 +343,16 @@ def test_pchain_quantisation_at_half_integers(qt):
     K, nrows = 2048, 1024
     x = dev(_half_integer_activation(K, seed=21))
     W = dev(make_weights(qt, nrows, K, seed=22))
-    y = torch.empty((1, nrows), device="cuda")
     pc = PersistentChain()
     pc.add_group(x)
-    pc.add_gemv(W, qt, y, nrows=nrows)
+    pc.add_gemv(W, qt, nrows=nrows)
     pc.instantiate()
     pc.launch()
     torch.cuda.synchronize()
     rpb, lb = pc.gemv_shape(0)
     assert lb == host_lanes_per_row(K // resolve_type(qt).qk, rpb)
     # the quantiser kernel divides every value; the persistent kernel must agree bit for bit
-    assert torch.equal(y, _single(W, qt, x.view(1, -1), rpb))
+    assert torch.equal(pc.output(0), _single(W, qt, x.view(1, -1), rpb))
     xq = ops.quantize_q8_1(x.view(1, -1)).cpu().numpy().reshape(-1)
     assert np.array_equal(xq, oracle.quantize_q8_1(x.cpu().numpy()).reshape(-1))
     pc.close()

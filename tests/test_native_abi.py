@@ -36,7 +36,7 @@ def test_python_signatures_cover_header():
 
 def test_cpu_safe_entry_points():
     lib = _native.lib()
-    assert lib.anvil_abi_version() == 1
+    assert lib.anvil_abi_version() == 2
     qk, nb = ctypes.c_int(), ctypes.c_int()
     expect = {2: (32, 18), 3: (32, 20), 6: (32, 22), 7: (32, 24), 8: (32, 34), 9: (32, 36),
               10: (256, 84), 11: (256, 110), 12: (256, 144), 13: (256, 176), 14: (256, 210),
@@ -49,6 +49,13 @@ def test_cpu_safe_entry_points():
     assert lib.anvil_row_bytes(12, 4096) == 16 * 144
     assert lib.anvil_row_bytes(14, 12288) == 48 * 210
     assert lib.anvil_row_bytes(12, 4000) == _native.ANVIL_ERR_INVALID
+    # the device wait bound: host state only, no launch
+    assert lib.anvil_get_wait_limit_ns() == 2_000_000_000
+    assert lib.anvil_set_wait_limit_ns(10_000_000) == 0
+    assert lib.anvil_get_wait_limit_ns() == 10_000_000
+    assert lib.anvil_set_wait_limit_ns(61_000_000_000) == _native.ANVIL_ERR_INVALID
+    assert lib.anvil_set_wait_limit_ns(0) == 0
+    assert lib.anvil_get_wait_limit_ns() == 2_000_000_000
 
 
 def test_check_raises_with_message():

@@ -41,9 +41,14 @@ def _noalloc(qt, W, x, nrows, K, ncols, y=None):
     return y
 
 
+# The last two shapes use the static buffer the hardest: K = 28672 with 8 columns does not
+# fit one launch's shared memory, so the GEMV runs as column chunks that read their Q8_1
+# columns at offsets inside the buffer; K = 98304 with 8 columns fills 884,736 of its
+# 1,048,576 bytes (one-column chunks, the last reading near the end of the buffer).
 @pytest.mark.parametrize("qt,nrows,K,ncols", [("Q4_K", 1000, 4096, 1), ("Q5_K", 257, 2048, 2),
                                               ("Q6_K", 640, 3072, 1), ("Q8_0", 513, 1024, 3),
-                                              ("Q4_K", 4096, 12288, 1)])
+                                              ("Q4_K", 4096, 12288, 1), ("Q4_K", 256, 28672, 8),
+                                              ("Q4_K", 64, 98304, 8)])
 def test_noalloc_matches_caller_scratch_two_calls(qt, nrows, K, ncols):
     W = torch.from_numpy(make_weights(qt, nrows, K, seed=11)).cuda()
     xa = torch.from_numpy(make_activation(K, ncols=ncols, seed=12)).cuda()
