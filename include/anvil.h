@@ -211,6 +211,14 @@ int anvil_mmvq_plan(int ggml_type, int nrows, int ncols_x, int ncols_dst, int nw
                     int rows_per_block, int *out_nwarps, int *out_rpb, int *out_grid,
                     int *out_smem_bytes);
 
+/* Compiled resources of the kernel anvil_mmvq would launch for this shape
+ * (cudaFuncGetAttributes): registers per thread, local memory per thread (register spills),
+ * maximum threads per block.  Replaces the reference's VGPR / LDS / scratch estimates
+ * (kernel_anvil/profile.py:7-34, 86) with the real numbers. */
+int anvil_mmvq_kernel_attributes(int ggml_type, int nrows, int ncols_x, int ncols_dst, int nwarps,
+                                 int rows_per_block, int *regs_per_thread, int *local_bytes,
+                                 int *max_threads_per_block);
+
 /* ---- GEMV chain executor (native CUDA-graph runtime) ---------------------- */
 
 /* A chain is an ordered list of quantize / MMVQ steps on fixed device buffers,

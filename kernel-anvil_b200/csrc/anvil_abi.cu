@@ -25,7 +25,8 @@ namespace anvil {
 // Q8_1 quantiser.  One warp per 32-value block, one lane per value, the semantics of
 // llama.cpp's CUDA quantize_q8_1: amax and sum by xor-butterfly warp reductions,
 // d = amax / 127, q = roundf(x / d) (0 when amax == 0), block = {half(d), half(sum), q}.
-// IEEE division (no fast-math), round-half-away-from-zero, fp16 round-to-nearest-even.
+// Both quotients are the correctly rounded IEEE ones (q8_scale, quant_q8; no fast-math),
+// round-half-away-from-zero, fp16 round-to-nearest-even.
 // ---------------------------------------------------------------------------------
 __global__ void __launch_bounds__(256)
     quantize_q8_1_kernel(const float *__restrict__ x, uint8_t *__restrict__ xq, int nblocks) {
@@ -37,8 +38,9 @@ __global__ void __launch_bounds__(256)
     const float xi = x[size_t(gw) * 32 + lane];
     const float amax = warp_max(fabsf(xi));
     const float sum = warp_sum(xi);
-    const float d = __fdiv_rn(amax, 127.0f);
-    const int q = amax == 0.0f ? 0 : int(roundf(__fdiv_rn(xi, d)));
+    const float d = q8_scale(amax);
+    const double rd64 = 1.0 / double(amax == 0.0f ? 1.0f : d);
+    const int q = amax == 0.0f ? 0 : quant_q8(xi, float(rd64), rd64);
     // Pack four quants per lane group and store words (blocks are 4-byte aligned).
     const uint32_t b = uint32_t(q) & 0xFFu;
     const uint32_t b1 = __shfl_down_sync(0xffffffffu, b, 1);
@@ -595,6 +597,21 @@ int anvil_mmvq_plan(int ggml_type, int nrows, int ncols_x, int ncols_dst, int nw
     if (out_rpb) *out_rpb = p.rpb;
     if (out_grid) *out_grid = p.grid;
     if (out_smem_bytes) *out_smem_bytes = p.smem;
+    return ANVIL_OK;
+}
+
+int anvil_mmvq_kernel_attributes(int ggml_type, int nrows, int ncols_x, int ncols_dst, int nwarps,
+                                 int rows_per_block, int *regs_per_thread, int *local_bytes,
+                                 int *max_threads_per_block) {
+    Plan p;
+    if (int s = plan_mmvq(ggml_type, nrows, ncols_x, ncols_dst, nwarps, rows_per_block, kModeQ81, &p))
+        return s;
+    cudaFuncAttributes attr{};
+    const cudaError_t e = cudaFuncGetAttributes(&attr, reinterpret_cast<const void *>(p.fn));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncGetAttributes");
+    if (regs_per_thread) *regs_per_thread = attr.numRegs;
+    if (local_bytes) *local_bytes = int(attr.localSizeBytes);
+    if (max_threads_per_block) *max_threads_per_block = attr.maxThreadsPerBlock;
     return ANVIL_OK;
 }
 

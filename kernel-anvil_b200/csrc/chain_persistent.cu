@@ -198,7 +198,7 @@ __device__ __forceinline__ ActBuf act_buf(uint8_t *base, int K, int ncols) {
 
 // Quantises this lane's 16 consecutive values (chunk cc of column col; the lane pair 2q, 2q+1
 // holds one Q8_1 block) into the swizzled buffer, with the arithmetic of quantize_q8_1:
-// d = amax / 127 by IEEE division, q = roundf(x / d) through quant_q8.  The stored d8 is
+// d = amax / 127 (q8_scale), q = roundf(x / d) through quant_q8.  The stored d8 is
 // rounded to fp16 (ROUND, as quantize_q8_1 stores it) or kept in fp32 (chained inputs).
 // Returns the block's amax.  Whole warp (shuffles); `live` lanes store.
 template <int QT, bool ROUND>
@@ -208,22 +208,12 @@ __device__ __forceinline__ float quant_chunk(const float (&v)[16], bool live, in
 #pragma unroll
     for (int i = 0; i < 16; ++i) am = fmaxf(am, fabsf(v[i]));
     am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
-    const float d = __fdiv_rn(am, 127.0f);
+    const float d = q8_scale(am);
     const float dn = am == 0.0f ? 1.0f : d;
-    const float rd = __frcp_rn(dn);
+    const double rd64 = 1.0 / double(dn);
     uint32_t w[4];
-    int s = 0;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        uint32_t word = 0;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int q = am == 0.0f ? 0 : quant_q8(v[4 * k + i], dn, rd);
-            word |= (uint32_t(q) & 0xFFu) << (8 * i);
-        }
-        w[k] = word;
-        s = __dp4a(int(word), 0x01010101, s);
-    }
+    int s;
+    quant16(v, am, float(rd64), rd64, w, s);
     const int so = __shfl_xor_sync(0xffffffffu, s, 1);
     if (live) {
         *reinterpret_cast<uint4 *>(b.aq + col * acb + act_chunk<QT>(cc) * 16) =
@@ -240,9 +230,10 @@ __device__ __forceinline__ float quant_chunk(const float (&v)[16], bool live, in
 }
 
 // One warp's share of a chained group's staging: 512-value blocks warp, warp + nwarps, ...
-// of the NCOLS columns of flagged words, read as they arrive (two blocks in flight per
-// lane), d8 kept in fp32; the warp's column maxima go to colmax[c].  Not inlined: the kernel
-// keeps its ring state in registers across the call.
+// of the NCOLS columns of flagged words, read as they arrive, d8 kept in fp32; the warp's
+// column maxima go to colmax[c].  Not inlined, and one block of words in flight per lane:
+// the kernel body around it holds the registers its tile runs need, and a second block in
+// flight makes this function spill to local memory on every pass.
 template <int QT, int NCOLS>
 __device__ __noinline__ void warp_stage_ll(const uint64_t *__restrict__ src, int K, uint32_t epoch,
                                            uint64_t wait_ns, uint32_t act_off, float *colmax) {
@@ -255,34 +246,23 @@ __device__ __noinline__ void warp_stage_ll(const uint64_t *__restrict__ src, int
     float cmax[NCOLS];
 #pragma unroll
     for (int c = 0; c < NCOLS; ++c) cmax[c] = 0.f;
-    for (int b0 = warp; b0 < total; b0 += 2 * nw) {
-        const bool two = b0 + nw < total;  // warp-uniform
-        const int bi1 = two ? b0 + nw : b0;
-        const int col0 = b0 / nb, blk0 = b0 - col0 * nb, col1 = bi1 / nb, blk1 = bi1 - col1 * nb;
-        const int t0 = min(512, K - blk0 * 512), t1 = min(512, K - blk1 * 512);
-        const bool live0 = lane < (t0 >> 4), live1 = two && lane < (t1 >> 4);
-        const uint64_t *p0 = src + size_t(col0) * K + size_t(blk0) * 512 + 2 * lane;
-        const uint64_t *p1 = src + size_t(col1) * K + size_t(blk1) * 512 + 2 * lane;
-        uint64_t w0[16], w1[16];
-        if (live0) ll_issue(p0, t0 >> 3, w0);
-        if (live1) ll_issue(p1, t1 >> 3, w1);
+    for (int bi = warp; bi < total; bi += nw) {  // warp-uniform
+        const int col = bi / nb, blk = bi - col * nb;
+        const int t = min(512, K - blk * 512);
+        const bool live = lane < (t >> 4);
+        const uint64_t *p = src + size_t(col) * K + size_t(blk) * 512 + 2 * lane;
         float v[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) v[i] = 0.f;
-        if (live0) ll_finish(p0, t0 >> 3, epoch, wait_ns, w0, v);
-        float am = quant_chunk<QT, false>(v, live0, col0, blk0 * 32 + lane, nkb, acb, b);
+        if (live) {
+            uint64_t w[16];
+            ll_issue(p, t >> 3, w);
+            ll_finish(p, t >> 3, epoch, wait_ns, w, v);
+        }
+        const float am = quant_chunk<QT, false>(v, live, col, blk * 32 + lane, nkb, acb, b);
 #pragma unroll
         for (int c = 0; c < NCOLS; ++c)
-            if (c == col0) cmax[c] = fmaxf(cmax[c], am);
-        if (two) {
-#pragma unroll
-            for (int i = 0; i < 16; ++i) v[i] = 0.f;
-            if (live1) ll_finish(p1, t1 >> 3, epoch, wait_ns, w1, v);
-            am = quant_chunk<QT, false>(v, live1, col1, blk1 * 32 + lane, nkb, acb, b);
-#pragma unroll
-            for (int c = 0; c < NCOLS; ++c)
-                if (c == col1) cmax[c] = fmaxf(cmax[c], am);
-        }
+            if (c == col) cmax[c] = fmaxf(cmax[c], am);
     }
 #pragma unroll
     for (int c = 0; c < NCOLS; ++c) {
@@ -344,11 +324,12 @@ __device__ void dump_staged(uint8_t *out, int K, int ncols, const ActBuf &b) {
 
 // ---- tile arithmetic -------------------------------------------------------------------
 
-// Where one GEMV's outputs go, held in registers per warp: this lane's rank buffer (lane
-// bl < world of a row's lanes stores to rank bl), the row offset of this rank's shard, and
-// the layout.
+// Where one GEMV's outputs go, held in registers per warp: the row offset of this rank's
+// shard, the layout, and (set by pc_run, which knows the lanes per row) this lane's rank
+// buffer: lane bl < world of a row's lanes stores to rank bl.
 struct PcOut {
-    uint64_t *y;               // rank (lane < world ? lane : 0)'s buffer, current parity
+    uint64_t *const *ys;       // the GEMV descriptor's buffers, one per rank
+    uint64_t *y;               // rank (bl < world ? bl : 0)'s buffer
     int nfull, row0, perm, world;
 };
 
@@ -554,13 +535,18 @@ __device__ __forceinline__ void pc_trace(const PcArgs &a, int g, int k) {
 
 // This warp's tiles of one GEMV of the current group, cc.i, cc.i + nw, ... < cc.t_end: wait
 // for each tile's copy (bounded), fix up unaligned row ends, dot and store, refill the ring.
-// One call per GEMV and warp (the tile arithmetic is compiled into the loop); the ring
-// state goes in and comes back by value.
+// One call per GEMV and warp (the tile arithmetic is compiled into the loop).  The warp's
+// ring state lives in shared memory between calls (rs): held in registers here, written
+// back at the end, so the kernel body keeps no ring state across its other work.
 template <int QT, int NCOLS, int RPB, int LBT, bool GLU>
-__device__ __noinline__ PcRing pc_run(const PcArgs &a, PcRing r, PcWarp w, PcCursor cc, PcOut o,
-                                      uint32_t act_off, float sc0, float sc1, int *s_failed) {
+__device__ __noinline__ void pc_run(const PcArgs &a, PcRing *rs, PcWarp w, PcCursor cc, PcOut o,
+                                    uint32_t act_off, float sc0, float sc1, int *s_failed) {
     extern __shared__ __align__(16) uint8_t smem[];
     const int lane = w.lane;
+    const int bl = lane & (LBT - 1);
+    o.y = o.ys[bl < o.world ? bl : 0];
+    PcRing r = *rs;
+    __syncwarp();
     const int K = a.groups[cc.g].K;
     for (; cc.i < cc.t_end; cc.i += w.nw) {
         if (r.issued == r.consumed) pc_produce(a, r, w);
@@ -608,45 +594,46 @@ __device__ __noinline__ PcRing pc_run(const PcArgs &a, PcRing r, PcWarp w, PcCur
         ++r.consumed;
         pc_produce(a, r, w);
     }
-    return r;
+    if (lane == 0) *rs = r;
+    __syncwarp();
 }
 
-#define ANVIL_PC_RUN_ARGS a, r, w, cc, o, act_off, sc0, sc1, s_failed
+#define ANVIL_PC_RUN_ARGS a, rs, w, cc, o, act_off, sc0, sc1, s_failed
 
 template <int QT, int NCOLS>
-__device__ __forceinline__ PcRing pc_run_variant(const PcArgs &a, const PcRing &r, const PcWarp &w,
-                                                 const PcCursor &cc, const PcOut &o, uint32_t act_off,
-                                                 float sc0, float sc1, int *s_failed) {
+__device__ __forceinline__ void pc_run_variant(const PcArgs &a, PcRing *rs, const PcWarp &w,
+                                               const PcCursor &cc, const PcOut &o, uint32_t act_off,
+                                               float sc0, float sc1, int *s_failed) {
     switch (cc.variant) {
-    case kV1x32: return pc_run<QT, NCOLS, 1, 32, false>(ANVIL_PC_RUN_ARGS);
-    case kV2x32: return pc_run<QT, NCOLS, 2, 32, false>(ANVIL_PC_RUN_ARGS);
-    case kV4x32: return pc_run<QT, NCOLS, 4, 32, false>(ANVIL_PC_RUN_ARGS);
-    case kV8x32: return pc_run<QT, NCOLS, 8, 32, false>(ANVIL_PC_RUN_ARGS);
-    case kV2x16: return pc_run<QT, NCOLS, 2, 16, false>(ANVIL_PC_RUN_ARGS);
-    case kV4x16: return pc_run<QT, NCOLS, 4, 16, false>(ANVIL_PC_RUN_ARGS);
-    case kV8x16: return pc_run<QT, NCOLS, 8, 16, false>(ANVIL_PC_RUN_ARGS);
-    case kV4x8: return pc_run<QT, NCOLS, 4, 8, false>(ANVIL_PC_RUN_ARGS);
-    case kV8x8: return pc_run<QT, NCOLS, 8, 8, false>(ANVIL_PC_RUN_ARGS);
-    case kG1x32: return pc_run<QT, NCOLS, 2, 32, true>(ANVIL_PC_RUN_ARGS);
-    case kG2x32: return pc_run<QT, NCOLS, 4, 32, true>(ANVIL_PC_RUN_ARGS);
-    case kG2x16: return pc_run<QT, NCOLS, 4, 16, true>(ANVIL_PC_RUN_ARGS);
-    case kG4x32: return pc_run<QT, NCOLS, 8, 32, true>(ANVIL_PC_RUN_ARGS);
-    case kG4x16: return pc_run<QT, NCOLS, 8, 16, true>(ANVIL_PC_RUN_ARGS);
-    case kG4x8: return pc_run<QT, NCOLS, 8, 8, true>(ANVIL_PC_RUN_ARGS);
-    default: return r;
+    case kV1x32: pc_run<QT, NCOLS, 1, 32, false>(ANVIL_PC_RUN_ARGS); break;
+    case kV2x32: pc_run<QT, NCOLS, 2, 32, false>(ANVIL_PC_RUN_ARGS); break;
+    case kV4x32: pc_run<QT, NCOLS, 4, 32, false>(ANVIL_PC_RUN_ARGS); break;
+    case kV8x32: pc_run<QT, NCOLS, 8, 32, false>(ANVIL_PC_RUN_ARGS); break;
+    case kV2x16: pc_run<QT, NCOLS, 2, 16, false>(ANVIL_PC_RUN_ARGS); break;
+    case kV4x16: pc_run<QT, NCOLS, 4, 16, false>(ANVIL_PC_RUN_ARGS); break;
+    case kV8x16: pc_run<QT, NCOLS, 8, 16, false>(ANVIL_PC_RUN_ARGS); break;
+    case kV4x8: pc_run<QT, NCOLS, 4, 8, false>(ANVIL_PC_RUN_ARGS); break;
+    case kV8x8: pc_run<QT, NCOLS, 8, 8, false>(ANVIL_PC_RUN_ARGS); break;
+    case kG1x32: pc_run<QT, NCOLS, 2, 32, true>(ANVIL_PC_RUN_ARGS); break;
+    case kG2x32: pc_run<QT, NCOLS, 4, 32, true>(ANVIL_PC_RUN_ARGS); break;
+    case kG2x16: pc_run<QT, NCOLS, 4, 16, true>(ANVIL_PC_RUN_ARGS); break;
+    case kG4x32: pc_run<QT, NCOLS, 8, 32, true>(ANVIL_PC_RUN_ARGS); break;
+    case kG4x16: pc_run<QT, NCOLS, 8, 16, true>(ANVIL_PC_RUN_ARGS); break;
+    case kG4x8: pc_run<QT, NCOLS, 8, 8, true>(ANVIL_PC_RUN_ARGS); break;
+    default: break;
     }
 }
 
 template <int NCOLS>
-__device__ __forceinline__ PcRing pc_run_any(const PcArgs &a, const PcRing &r, const PcWarp &w,
-                                             const PcCursor &cc, const PcOut &o, uint32_t act_off,
-                                             float sc0, float sc1, int *s_failed) {
+__device__ __forceinline__ void pc_run_any(const PcArgs &a, PcRing *rs, const PcWarp &w,
+                                           const PcCursor &cc, const PcOut &o, uint32_t act_off,
+                                           float sc0, float sc1, int *s_failed) {
     switch (cc.type) {
-    case kTypeQ4_K: return pc_run_variant<kTypeQ4_K, NCOLS>(ANVIL_PC_RUN_ARGS);
-    case kTypeQ5_K: return pc_run_variant<kTypeQ5_K, NCOLS>(ANVIL_PC_RUN_ARGS);
-    case kTypeQ6_K: return pc_run_variant<kTypeQ6_K, NCOLS>(ANVIL_PC_RUN_ARGS);
-    case kTypeQ8_0: return pc_run_variant<kTypeQ8_0, NCOLS>(ANVIL_PC_RUN_ARGS);
-    default: return r;
+    case kTypeQ4_K: pc_run_variant<kTypeQ4_K, NCOLS>(ANVIL_PC_RUN_ARGS); break;
+    case kTypeQ5_K: pc_run_variant<kTypeQ5_K, NCOLS>(ANVIL_PC_RUN_ARGS); break;
+    case kTypeQ6_K: pc_run_variant<kTypeQ6_K, NCOLS>(ANVIL_PC_RUN_ARGS); break;
+    case kTypeQ8_0: pc_run_variant<kTypeQ8_0, NCOLS>(ANVIL_PC_RUN_ARGS); break;
+    default: break;
     }
 }
 
@@ -677,6 +664,7 @@ template <int NCOLS>
 __global__ void __launch_bounds__(kMaxWarps * 32, 1) pchain_kernel(const __grid_constant__ PcArgs a) {
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ float s_max[2][kMaxWarps][2];  // per activation buffer, warp, column: input max
+    __shared__ PcRing s_ring[kMaxWarps];      // each warp's ring state between tile runs
     __shared__ int s_failed;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nwarps = blockDim.x >> 5;
@@ -690,20 +678,22 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) pchain_kernel(const __grid_
     w.lane = lane;
     w.R = uint32_t(a.ring_bytes);
 
-    PcRing r{};
-    r.pc.g = 0;
-    if (a.ngroups > 0) {
-        r.pc.i = pc_first(a.groups[0].rot, w.gw, w.nw);
-        pc_settle(a, r.pc, w.gw, w.nw);
+    {
+        PcRing r{};
+        r.pc.g = 0;
+        if (a.ngroups > 0) {
+            r.pc.i = pc_first(a.groups[0].rot, w.gw, w.nw);
+            pc_settle(a, r.pc, w.gw, w.nw);
+        }
+        if (lane == 0) {
+            for (int s = 0; s < kPcSlots; ++s) mbar_init(&w.bars[s], 1);
+            mbar_fence_init();
+        }
+        __syncwarp();
+        pc_produce(a, r, w);  // the first weight tiles stream while the first input is staged
+        if (lane == 0) s_ring[warp] = r;
+        __syncwarp();
     }
-
-    if (lane == 0) {
-        for (int s = 0; s < kPcSlots; ++s) mbar_init(&w.bars[s], 1);
-        mbar_fence_init();
-    }
-    __syncwarp();
-
-    pc_produce(a, r, w);  // the first weight tiles stream while the first input is staged
 
     if (a.ngroups > 0) {
         pc_trace(a, 0, 0);
@@ -744,12 +734,13 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) pchain_kernel(const __grid_
             pc_load_gemv(a, cc);
             const PcGemv *gm = a.gemvs + cc.m;
             PcOut o;
-            o.y = gm->y[lane < a.world ? lane : 0];
+            o.ys = gm->y;
+            o.y = nullptr;
             o.nfull = gm->nrows_full;
             o.row0 = gm->row0;
             o.perm = gm->perm;
             o.world = a.world;
-            r = pc_run_any<NCOLS>(a, r, w, cc, o, act_off, sc[0], sc[1], &s_failed);
+            pc_run_any<NCOLS>(a, &s_ring[warp], w, cc, o, act_off, sc[0], sc[1], &s_failed);
             cc.i += ((cc.t_end - cc.i + w.nw - 1) / w.nw) * w.nw;  // first tile past this GEMV
         }
         pc_trace(a, g, 3);
@@ -1006,9 +997,13 @@ int anvil_pchain_instantiate(anvil_pchain *c, int nwarps, int ctas_per_sm) {
         act[gi & 1] = std::max(act[gi & 1], (b + 15) & ~15);
     }
     const int bars = (nwarps * kPcSlots * 8 + 15) & ~15;
-    const int budget = (228 * 1024) / ctas_per_sm - 1024 - 256;  // per CTA, less the runtime's reserve
-                                                                 // and the static scratch
-    const int ring = ((std::min(budget, kMaxSmem) - bars - act[0] - act[1]) / nwarps) & ~15;
+    // Per CTA: the SM's 228 KB shared by ctas_per_sm CTAs less the runtime's 1 KB reserve each,
+    // at most 227 KB per CTA, and the kernel's static shared memory comes out of both.
+    cudaFuncAttributes fattr{};
+    cudaError_t fe = cudaFuncGetAttributes(&fattr, reinterpret_cast<const void *>(c->fn));
+    if (fe != cudaSuccess) return cuda_fail(fe, "cudaFuncGetAttributes");
+    const int budget = std::min((228 * 1024) / ctas_per_sm - 1024, kMaxSmem) - int(fattr.sharedSizeBytes);
+    const int ring = ((budget - bars - act[0] - act[1]) / nwarps) & ~15;
     if (ring < 4096) return fail(ANVIL_ERR_UNSUPPORTED, "no room for weight rings (%d B per warp)", ring);
 
     // Tile shape per GEMV: requested rows per tile (else the built-in default), the lanes per

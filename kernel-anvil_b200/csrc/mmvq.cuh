@@ -74,17 +74,66 @@ __device__ __forceinline__ int mmvq_segment(const MmvqArgs &a, int tile) {
     return s;
 }
 
-// roundf(x / d) with x / d the correctly rounded IEEE quotient, |x| <= 127 d (d > 0), without
-// a division in the common case.  t = x * rd with rd = 1/d rounded differs from the exact
-// x / d by at most |x/d| (2^-24 + 2^-24 + 2^-48) < 127.5 * 2^-23 ~ 1.6e-5, and the rounded
-// quotient differs from the exact one by at most 0.5 ulp < 127.5 * 2^-24 ~ 7.6e-6.  Both
-// therefore round to the same integer unless t lies within 2.4e-5 of a half-integer; there
-// (1e-4 is the margin used) the quotient is taken with the division itself.
-__device__ __forceinline__ int quant_q8(float x, float d, float rd) {
+// The Q8_1 block scale d = RN32(amax / 127), the correctly rounded IEEE quotient, without a
+// division (the IEEE division and reciprocal intrinsics cost on the order of a thousand
+// cycles here): the fp64 product amax * RN64(1/127), rounded to fp32.  That is exact for every
+// float amax: amax / 127 = m 2^e / 127 with m < 2^24 is never a float32 rounding midpoint (a
+// midpoint has an even numerator over an odd 127) and lies at least 2^-32 (relative) away
+// from one, while the fp64 product is within 2^-52 of amax / 127 (also checked on the host
+// for every float32 mantissa, every subnormal and the top binade).
+__device__ __forceinline__ float q8_scale(float amax) { return float(double(amax) * (1.0 / 127.0)); }
+
+// roundf(RN32(x / d)), the quantiser's q, for d > 0 and |x| <= 127 d, given rd64 = RN64(1/d)
+// and rd = RN32(rd64) = RN32(1/d) (fp64 then fp32 rounding equals direct fp32 rounding, since
+// 53 >= 2 * 24 + 2).  Fast path: t = x * rd differs from x / d by at most |x/d| (2^-24 +
+// 2^-24 + 2^-48) < 127.5 * 2^-23 ~ 1.6e-5, and RN32(x / d) differs from x / d by at most
+// 0.5 ulp < 7.6e-6, so both round to the same integer unless t lies within 2.4e-5 of a
+// half-integer (1e-4 is the margin used).  There the quotient is RN32(double(x) * rd64): its
+// error is below 2^-51.9 (relative), and x / d = X 2^a / (D 2^b) (X, D < 2^24) is never a
+// float32 midpoint and lies at least 2^-49 (relative) away from one, so rounding to fp32 gives
+// RN32(x / d) exactly.
+__device__ __forceinline__ int quant_q8(float x, float rd, double rd64) {
     const float t = x * rd;
     const float f = fabsf(t) - floorf(fabsf(t));  // fractional part of |t|
     if (fabsf(f - 0.5f) > 1e-4f) return int(roundf(t));
-    return int(roundf(__fdiv_rn(x, d)));
+    return int(roundf(float(double(x) * rd64)));
+}
+
+// True where t = x * rd needs the exact quotient: within 1e-4 of a half-integer, or not a
+// finite number (rd = inf for a subnormal d).
+__device__ __forceinline__ bool near_half(float t) {
+    const float a = fabsf(t);
+    return !(fabsf(a - floorf(a) - 0.5f) > 1e-4f);
+}
+
+// The quants of 16 values of one Q8_1 block half (quant_q8 for each), packed four to a word
+// (value 4k + i in byte i of word k), and their sum.  The fast path runs for all 16 values
+// without a branch, so their instruction chains overlap; the exact quotient is taken in a
+// second pass only when some value needs it.  amax == 0 gives all zeros.
+__device__ __forceinline__ void quant16(const float (&v)[16], float amax, float rd, double rd64,
+                                        uint32_t (&w)[4], int &sum) {
+    int q[16];
+    bool near = false;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        const float t = v[i] * rd;
+        near |= near_half(t);
+        q[i] = int(roundf(t));
+    }
+    if (near && amax != 0.0f) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+            if (near_half(v[i] * rd)) q[i] = int(roundf(float(double(v[i]) * rd64)));
+    }
+    sum = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) word |= (amax == 0.0f ? 0u : uint32_t(q[4 * k + i]) & 0xFFu) << (8 * i);
+        w[k] = word;
+        sum = __dp4a(int(word), 0x01010101, sum);
+    }
 }
 
 struct MmvqSmem {
@@ -713,7 +762,8 @@ __device__ __forceinline__ void unit_step(const TileCtx &t, int b, const BlkHdr 
 
 // ---- the Q8_1 quantisation of one 32-value block by one warp ------------------------------
 // Semantics of llama.cpp's CUDA quantize_q8_1: amax and sum by xor-butterfly warp
-// reductions, d = amax / 127, q = roundf(x / d) (0 when amax == 0); IEEE division.
+// reductions, d = amax / 127, q = roundf(x / d) (0 when amax == 0), both quotients the
+// correctly rounded IEEE ones (q8_scale, quant_q8).
 struct Q81Lane {
     int q;       // this lane's quant
     float d;     // fp32 scale (stored as fp16)
@@ -724,8 +774,9 @@ __device__ __forceinline__ Q81Lane quantize_lane(float xi) {
     Q81Lane r;
     const float amax = warp_max(fabsf(xi));
     r.sum = warp_sum(xi);
-    r.d = __fdiv_rn(amax, 127.0f);
-    r.q = amax == 0.0f ? 0 : int(roundf(__fdiv_rn(xi, r.d)));
+    r.d = q8_scale(amax);
+    const double rd64 = 1.0 / double(amax == 0.0f ? 1.0f : r.d);
+    r.q = amax == 0.0f ? 0 : quant_q8(xi, float(rd64), rd64);
     return r;
 }
 
@@ -781,23 +832,21 @@ __device__ __forceinline__ void stage_f32_q8_1(const float *__restrict__ x, int 
                 am = fmaxf(am, fabsf(v[j][k].w));
             }
             am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
-            const float d = __fdiv_rn(am, 127.0f);
+            const float d = q8_scale(am);
             const float dn = am == 0.0f ? 1.0f : d;  // all quants are 0 then; no 0/0
-            const float rd = __frcp_rn(dn);
-            uint32_t w[4];
-            int s = 0;
+            const double rd64 = 1.0 / double(dn);
+            const float rd = float(rd64);
+            float e[16];
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-                const float e[4] = {v[j][k].x, v[j][k].y, v[j][k].z, v[j][k].w};
-                uint32_t word = 0;
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const int q = am == 0.0f ? 0 : quant_q8(e[i], dn, rd);
-                    word |= (uint32_t(q) & 0xFFu) << (8 * i);
-                }
-                w[k] = word;
-                s = __dp4a(int(word), 0x01010101, s);
+                e[4 * k] = v[j][k].x;
+                e[4 * k + 1] = v[j][k].y;
+                e[4 * k + 2] = v[j][k].z;
+                e[4 * k + 3] = v[j][k].w;
             }
+            uint32_t w[4];
+            int s;
+            quant16(e, am, rd, rd64, w, s);
             const int so = __shfl_xor_sync(0xffffffffu, s, 1);
             if (c < total) {
                 const int col = c / nch, cc = c - col * nch;

@@ -187,6 +187,7 @@ SIGNATURES = {
     "anvil_mmvq_block_sums": (c_int, [c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
                                       c_int, c_void_p]),
     "anvil_mmvq_plan": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, _PI, _PI, _PI, _PI]),
+    "anvil_mmvq_kernel_attributes": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, _PI, _PI, _PI]),
     "anvil_chain_create": (c_void_p, []),
     "anvil_chain_destroy": (None, [c_void_p]),
     "anvil_chain_add_quantize": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int]),

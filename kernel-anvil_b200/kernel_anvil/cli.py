@@ -343,13 +343,21 @@ def cmd_profile(args) -> None:
     cfg = dict(getattr(runner, "BASELINE_CONFIG", {}))
     m = profile_kernel(lambda c: runner.run(inputs, **c), cfg, getattr(runner, "DATA_BYTES", None),
                        gpu, args.warmup, args.runs)
+    if args.ncu or args.ncu_csv:
+        from kernel_anvil.profile import apply_ncu, parse_ncu_csv, profile_runner_ncu
+
+        rows = (parse_ncu_csv(Path(args.ncu_csv).read_text()) if args.ncu_csv
+                else profile_runner_ncu(args.runner, args.ncu_kernel))
+        m = apply_ncu(m, rows)
     report = classify(m, gpu)
     table = Table(title="Profile Metrics")
     table.add_column("Metric", style="cyan")
     table.add_column("Value", justify="right")
     for k, v in (("Duration", f"{m.duration_ns:.0f} ns"), ("Registers/thread", str(m.regs_per_thread)),
                  ("Shared memory", f"{m.smem_bytes} bytes"),
+                 ("Local memory (spills)", f"{m.spill_bytes} bytes"),
                  ("Bandwidth", f"{m.bandwidth_gbs:.1f} GB/s"),
+                 ("DRAM bytes (ncu)", "-" if m.dram_bytes is None else str(m.dram_bytes)),
                  ("Occupancy", f"{m.occupancy_pct:.1f}%"), ("Limiting factor", m.limiting_factor)):
         table.add_row(k, v)
     console.print(table)
@@ -472,6 +480,11 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("runner", help="Path to runner script")
     p.add_argument("--warmup", type=int, default=5, help="Warmup iterations (default: 5)")
     p.add_argument("--runs", type=int, default=20, help="Timed iterations (default: 20)")
+    p.add_argument("--ncu", action="store_true",
+                   help="also read DRAM bytes and device time from ncu (one pass, clocks left alone)")
+    p.add_argument("--ncu-kernel", default="mmvq", help="ncu kernel name regex (default: mmvq)")
+    p.add_argument("--ncu-csv", default=None,
+                   help="use a recorded `ncu --csv` metrics log instead of running ncu")
     p.set_defaults(fn=cmd_profile)
 
     p = sub.add_parser("gguf-optimize", help="Parse GGUF, tune shapes on the real kernels, write smithy JSON")

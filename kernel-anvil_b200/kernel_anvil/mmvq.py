@@ -263,6 +263,17 @@ def plan(qt, nrows: int, K: int, ncols: int = 1, nwarps: int = 0, rows_per_block
             "smem_bytes": v[3].value}
 
 
+def kernel_attributes(qt, nrows: int, K: int, ncols: int = 1, nwarps: int = 0,
+                      rows_per_block: int = 0) -> dict:
+    """Compiled resources of the kernel that plan() would launch: registers per thread, local
+    (spill) bytes per thread, maximum threads per block (cudaFuncGetAttributes)."""
+    info = resolve_type(qt)
+    v = [ctypes.c_int() for _ in range(3)]
+    check(_native.lib().anvil_mmvq_kernel_attributes(info.ggml_type, nrows, K, ncols, nwarps,
+                                                     rows_per_block, *[ctypes.byref(a) for a in v]))
+    return {"regs_per_thread": v[0].value, "local_bytes": v[1].value, "max_threads_per_block": v[2].value}
+
+
 def take_device_status() -> int:
     """OR of device status flags raised since the last call (1 = an mbarrier wait gave up)."""
     return check(_native.lib().anvil_take_device_status())

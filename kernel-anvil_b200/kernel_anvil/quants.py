@@ -153,8 +153,14 @@ def make_activation(K: int, ncols: int = 1, seed: int = 1) -> np.ndarray:
 
 
 def make_weights_device(qt, nrows: int, K: int, seed: int = 0, device="cuda"):
-    """Synthetic weights drawn on the GPU (same distributions as make_weights, different
-    stream of random numbers).  Returns a uint8 tensor of shape (nrows, row_bytes)."""
+    """Synthetic weights drawn on the GPU, shape (nrows, row_bytes) uint8.
+
+    The distributions are make_weights' with one change: the types with a block minimum
+    (Q4_K, Q5_K, Q2_K, Q4_1, Q5_1) draw it so that a weight's expected value is zero, as it
+    is for real quantised weights.  With make_weights' minima the weights have a positive
+    mean (Q4_K: E[d*sc*q - dmin*m] = 31.5 * 1e-3 * E|N| * (7.5 - 1)), every output of a GEMV
+    carries the same offset, and along a chain of GEMVs that offset grows until all rows
+    of a gate projection share one sign.  The chains and the bench use these weights."""
     import torch
 
     info = resolve_type(qt)
@@ -168,9 +174,12 @@ def make_weights_device(qt, nrows: int, K: int, seed: int = 0, device="cuda"):
         v = torch.randn(nb, device=device, generator=g).abs_().mul_(scale).to(torch.float16)
         return v.view(torch.uint8).view(nb, 2)
 
+    # mean quant of the types with a minimum: q uniform over 0..15 (Q4_K, Q4_1), 0..31 (Q5_K,
+    # Q5_1), 0..3 (Q2_K); scale and min indices are uniform over the same range, so
+    # E[dmin] = mean quant * E[d] centres the weights
     if info.name in ("Q4_K", "Q5_K"):
         blocks[:, 0:2] = fp16_abs_normal(1e-3)
-        blocks[:, 2:4] = fp16_abs_normal(1e-3)
+        blocks[:, 2:4] = fp16_abs_normal(1e-3 * (7.5 if info.name == "Q4_K" else 15.5))
     elif info.name == "Q6_K":
         sc = torch.randint(-32, 32, (nb, 16), dtype=torch.int8, device=device, generator=g)
         blocks[:, 192:208] = sc.view(torch.uint8)
@@ -181,7 +190,7 @@ def make_weights_device(qt, nrows: int, K: int, seed: int = 0, device="cuda"):
         blocks[:, 2:34] = q.view(torch.uint8)
     elif info.name == "Q2_K":
         blocks[:, 80:82] = fp16_abs_normal(1e-2)
-        blocks[:, 82:84] = fp16_abs_normal(1e-2)
+        blocks[:, 82:84] = fp16_abs_normal(1.5e-2)
     elif info.name == "Q3_K":
         blocks[:, 108:110] = fp16_abs_normal(1e-2)
     elif info.name in ("IQ4_NL", "IQ4_XS"):
@@ -189,6 +198,7 @@ def make_weights_device(qt, nrows: int, K: int, seed: int = 0, device="cuda"):
     elif info.name in ("Q4_0", "Q4_1", "Q5_0", "Q5_1"):
         blocks[:, 0:2] = fp16_abs_normal(1e-2)
         if info.name.endswith("_1"):
-            m = (torch.randn(nb, device=device, generator=g).abs_().mul_(-1e-1)).to(torch.float16)
+            mq = 7.5e-2 if info.name == "Q4_1" else 15.5e-2
+            m = (torch.randn(nb, device=device, generator=g).abs_().mul_(-mq)).to(torch.float16)
             blocks[:, 2:4] = m.view(torch.uint8).view(nb, 2)
     return blocks.view(nrows, row_bytes)

@@ -5,9 +5,10 @@ gathered output of its producer as the words arrive.
 Checks, on every rank: the gathered outputs of every GEMV hold no stale or missing value;
 this rank's rows of every GEMV match the oracle computed from the gathered input (the
 fixed vector, or the producer's gathered output under the chained-input rule); and the
-gathered vectors are identical on both ranks.  Runs as two spawned processes, one per GPU
-(NCCL with NVLS off, only for set-up and the comparison); skipped with fewer than two
-GPUs."""
+gathered vectors are identical on both ranks (checksums exchanged once).  Every rank takes
+the same collective steps whatever its local checks find.  Runs as two spawned processes,
+one per GPU (NCCL with NVLS off, only for set-up and the comparison); skipped with fewer
+than two GPUs."""
 import os
 import socket
 from datetime import timedelta
@@ -28,6 +29,7 @@ def _free_port() -> int:
 
 
 def _worker(rank, world, port, out_dir, spec_name, ngemv):
+    import hashlib
     import sys
     from pathlib import Path
 
@@ -42,43 +44,39 @@ def _worker(rank, world, port, out_dir, spec_name, ngemv):
     from kernel_anvil.chains import DeviceChain, get_chain
     from kernel_anvil.pchain import take_status
 
-    msg = "ok"
-    dc = None
+    status, sums, dc = "ok", [], None
     try:
         spec = get_chain(spec_name).head(ngemv)
         dc = DeviceChain(spec, rank=rank, world=world, executor="persistent", dist=dist, seed=0)
         for _ in range(3):  # three tokens: epochs 1..3, both output parities
             dc.launch()
         torch.cuda.synchronize()
-        dist.barrier()
-        status = take_status()
-        if status:
-            msg = f"device status {status}"
-        worst = check_chain(dc)
-        for j in range(dc.pchain.n_gemv):
-            mine = dc.pchain.output(j)
-            other = torch.empty_like(mine)
-            # rank 0 sends its gathered vector to rank 1 and receives rank 1's
-            if rank == 0:
-                dist.send(mine, 1)
-                dist.recv(other, 1)
-            else:
-                dist.recv(other, 0)
-                dist.send(mine, 0)
-            if not torch.equal(mine, other):
-                msg = f"chain GEMV {j}: gathered outputs differ between ranks"
-        if msg == "ok":
-            msg = f"ok {worst:.2e}"
-        dist.barrier()
-    except AssertionError as e:
-        msg = f"fail: {e}"
+        st = take_status()
+        if st:
+            status = f"device status {st}"
+        sums = [hashlib.sha1(dc.pchain.output(j).cpu().numpy().tobytes()).hexdigest()
+                for j in range(dc.pchain.n_gemv)]
+        try:
+            worst = check_chain(dc)
+            if status == "ok":
+                status = f"ok {worst:.2e}"
+        except AssertionError as e:
+            status = f"fail: {e}"
+    except Exception as e:  # noqa: BLE001 -- reported, and the collectives below still run
+        status = f"error: {type(e).__name__}: {e}"
     finally:
+        got = [None] * world
+        dist.all_gather_object(got, sums)
+        if status.startswith("ok") and any(g != sums for g in got):
+            status = "fail: gathered outputs differ between ranks"
+        dist.barrier()
         if dc is not None:
             dc.close()
-        Path(out_dir, f"rank{rank}.txt").write_text(msg)
+        Path(out_dir, f"rank{rank}.txt").write_text(status)
         dist.destroy_process_group()
 
 
+@pytest.mark.timeout(600)
 @pytest.mark.parametrize("spec_name,ngemv", [("qwen3_8b", 15), ("llama3_70b", 8)])
 def test_sharded_dataflow_chain_two_gpus(tmp_path, spec_name, ngemv):
     if torch.cuda.device_count() < 2:

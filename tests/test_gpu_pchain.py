@@ -168,12 +168,16 @@ def _oracle_check(pc, desc):
     return outs
 
 
-@pytest.mark.parametrize("types", [("Q4_K", "Q6_K", "Q8_0"), ("Q5_K", "Q8_0", "Q4_K")])
-def test_pchain_chained_groups_match_oracle(types):
+@pytest.mark.parametrize("types,K,inter", [(("Q4_K", "Q6_K", "Q8_0"), 1024, 3072),
+                                           (("Q5_K", "Q8_0", "Q4_K"), 1024, 3072),
+                                           (("Q4_K", "Q6_K", "Q8_0"), 8192, 1024)])
+def test_pchain_chained_groups_match_oracle(types, K, inter):
+    """Every chained input kind and the gate/up tiles of 1, 2 and 4 rows per matrix (K = 8192
+    with 1024 gate/up rows takes one row of each per tile)."""
     pc = PersistentChain()
-    desc, groups = _decoder(pc, types=types)
+    desc, groups = _decoder(pc, K=K, inter=inter, types=types)
     # the chained groups' staged Q8_1, written out by the kernel, against the oracle's rule
-    dumps = {g: torch.zeros(1024 // 32 * 36 if g != groups[3] else 3072 // 32 * 36, dtype=torch.uint8,
+    dumps = {g: torch.zeros(K // 32 * 36 if g != groups[3] else inter // 32 * 36, dtype=torch.uint8,
                             device="cuda") for g in groups[1:]}
     for g, buf in dumps.items():
         pc.set_group_dump(g, buf)
@@ -209,8 +213,9 @@ def test_pchain_chain_trace_and_epochs():
     pc.close()
 
 
-def test_device_chain_dataflow_matches_oracle():
-    spec = get_chain("qwen3_8b").head(14)  # two decoder layers, both Q6_K mixes
+@pytest.mark.parametrize("name,n", [("qwen3_8b", 14), ("llama3_70b", 8)])
+def test_device_chain_dataflow_matches_oracle(name, n):
+    spec = get_chain(name).head(n)  # Qwen3-8B: two decoder layers, both Q6_K mixes
     dc = DeviceChain(spec, executor="persistent")
     assert dc.dataflow and dc.external_inputs == ["attn_in.0"]
     for _ in range(2):
@@ -355,4 +360,86 @@ def test_pchain_quantisation_at_half_integers(qt):
     assert torch.equal(pc.output(0), _single(W, qt, x.view(1, -1), rpb))
     xq = ops.quantize_q8_1(x.view(1, -1)).cpu().numpy().reshape(-1)
     assert np.array_equal(xq, oracle.quantize_q8_1(x.cpu().numpy()).reshape(-1))
+    pc.close()
+
+
+@pytest.mark.parametrize("qt,K", [("Q4_K", 2048), ("Q4_K", 4096), ("Q8_0", 1024), ("Q6_K", 8192)])
+def test_pchain_rank_stores_reach_every_rank(qt, K):
+    """A two-rank chain built on one GPU, its second rank's buffers local stand-ins: rank 0's
+    rows must be written, with the same values and epoch, into both ranks' buffers whatever
+    the lanes per row of the tile shape (32, 16 or 8), and no other row may be touched."""
+    n = 1024
+    x = dev(make_activation(K, seed=31))
+    W = dev(make_weights(qt, n, K, seed=32))
+    shapes = (1, 2, 4, 8)
+    bufs = {r: [torch.zeros(output_words_bytes(n) // 8, dtype=torch.int64, device="cuda") for _ in range(2)]
+            for r in shapes}
+    pc = PersistentChain(world=2, rank=0)
+    pc.add_group(x)
+    for rpb in shapes:
+        pc.add_gemv(W[: n // 2], qt, nrows=n // 2, row0=0, nrows_full=n,
+                    y_ptrs=[b.data_ptr() for b in bufs[rpb]], rows_per_block=rpb)
+    pc.instantiate()
+    lbs = {pc.gemv_shape(i)[1] for i in range(len(shapes))}
+    pc.launch()  # epoch 1: parity 1, words [n, 2n) of each buffer
+    torch.cuda.synchronize()
+    assert take_status() == 0
+    for i, rpb in enumerate(shapes):
+        words = [b.view(2, n).cpu().numpy() for b in bufs[rpb]]
+        for w in words:
+            assert (w[1, : n // 2] >> 32 == 1).all(), f"rows per tile {rpb}: a row of this rank is missing"
+            assert (w[1, n // 2:] == 0).all() and (w[0] == 0).all(), "a row outside this rank was written"
+        assert np.array_equal(words[0], words[1])
+        ref = _single(W[: n // 2], qt, x.view(1, -1), pc.gemv_shape(i)[0]).cpu().numpy().reshape(-1)
+        vals = (words[0][1, : n // 2] & 0xFFFFFFFF).astype(np.uint32).view(np.float32)
+        assert oracle.max_rel_err(vals, ref) <= Y_TOL
+    assert len(lbs) >= 1
+    pc.close()
+
+
+@pytest.mark.parametrize("n,K,rpb", [(1024, 8192, 0), (8192, 8192, 0), (28672, 8192, 0), (28672, 8192, 1),
+                                     (28672, 8192, 2), (12288, 4096, 0)])
+def test_pchain_gate_up_matches_oracle(n, K, rpb):
+    """A gate/up pair on a fixed input against the oracle's silu(g) * u, over row counts and
+    rows per tile (0 = the built-in choice)."""
+    x = dev(make_activation(K, seed=51))
+    Wg = dev(make_weights("Q4_K", n, K, seed=52))
+    Wu = dev(make_weights("Q4_K", n, K, seed=53))
+    pc = PersistentChain()
+    pc.add_group(x)
+    i = pc.add_glu(Wg, Wu, "Q4_K", nrows=n, rows_per_block=rpb)
+    pc.instantiate()
+    pc.launch()
+    torch.cuda.synchronize()
+    assert take_status() == 0
+    got = pc.output(i).cpu().numpy()
+    ref = oracle.mmvq_glu("Q4_K", Wg.cpu().numpy(), Wu.cpu().numpy(), oracle.quantize_q8_1(x.cpu().numpy()), n, K)
+    err = oracle.max_rel_err(got, ref)
+    assert err <= Y_TOL, f"shape {pc.gemv_shape(i)}: error {err}"
+    pc.close()
+
+
+@pytest.mark.parametrize("n", [1024, 4096, 8192, 16384, 28672])
+def test_pchain_chained_gate_up_matches_oracle(n):
+    """A gate/up pair whose input is the chained output of an 8192 x 8192 GEMV."""
+    K = 8192
+    x = dev(make_activation(K, seed=61))
+    Wo = dev(make_weights("Q4_K", K, K, seed=62))
+    Wg = dev(make_weights("Q4_K", n, K, seed=63))
+    Wu = dev(make_weights("Q4_K", n, K, seed=64))
+    pc = PersistentChain()
+    pc.add_group(x)
+    io = pc.add_gemv(Wo, "Q4_K", nrows=K)
+    pc.add_group_chained(io)
+    ig = pc.add_glu(Wg, Wu, "Q4_K", nrows=n)
+    pc.instantiate()
+    pc.launch()
+    torch.cuda.synchronize()
+    assert take_status() == 0
+    yo = pc.output(io).cpu().numpy()
+    got = pc.output(ig).cpu().numpy()
+    xq, sc = oracle.quantize_q8_1_chained(yo)
+    ref = oracle.mmvq_glu_chained("Q4_K", Wg.cpu().numpy(), Wu.cpu().numpy(), xq, sc, n, K)
+    err = oracle.max_rel_err(got, ref)
+    assert err <= Y_TOL, f"n={n} shape {pc.gemv_shape(ig)}: error {err}, got max {np.abs(got).max()}, ref max {np.abs(ref).max()}"
     pc.close()

@@ -167,3 +167,56 @@ def test_block_sums_reconstruct_y(qt):
 
 def test_oracle_threads_reported():
     assert oracle.num_threads() >= 1
+
+
+def test_division_free_quantiser_arithmetic():
+    """The kernels compute the quantiser's two IEEE quotients without a division:
+    d = RN32(amax/127) as fp32(fp64(amax) * RN64(1/127)), and q = roundf(RN32(x/d)) as
+    roundf(x * RN32(1/d)) except within 1e-4 of a half-integer, where RN32(fp64(x) * RN64(1/d))
+    is used.  Restated here in numpy and checked against the correctly rounded quotients (fp64
+    division then fp32 rounding, exact since 53 >= 2 * 24 + 2)."""
+    c = np.float64(1.0) / np.float64(127.0)
+    m = np.arange(1 << 23, dtype=np.uint32)
+    for am in (((127 << 23) | m).view(np.float32), m[1:].view(np.float32),
+               ((254 << 23) | m).view(np.float32)):
+        got = (am.astype(np.float64) * c).astype(np.float32)
+        ref = (am.astype(np.float64) / np.float64(127.0)).astype(np.float32)
+        assert np.array_equal(got, ref)
+
+    rng = np.random.default_rng(7)
+    n = 2_000_000
+    amax = np.abs(rng.standard_normal(n)).astype(np.float32) * np.float32(10.0) ** rng.integers(-30, 30, n)
+    amax = amax.astype(np.float32)
+    d = (amax.astype(np.float64) * c).astype(np.float32)
+    d = np.where(d == 0, np.float32(1.0), d).astype(np.float32)
+    k = rng.integers(-127, 127, n).astype(np.float32)
+    x = ((k + np.float32(0.5)) * d).astype(np.float32)  # on or next to half-integer multiples of d
+    nudge = rng.integers(-2, 3, n)
+    for s in (1, 2):
+        x = np.where(nudge >= s, np.nextafter(x, np.float32(np.inf)), x)
+        x = np.where(nudge <= -s, np.nextafter(x, np.float32(-np.inf)), x)
+    x = np.concatenate([x, (rng.standard_normal(n) * 64 * d).astype(np.float32)])
+    d = np.concatenate([d, d])
+    rd64 = np.float64(1.0) / d.astype(np.float64)
+    rd = rd64.astype(np.float32)
+    t = (x * rd).astype(np.float32)
+    f = np.abs(t) - np.floor(np.abs(t))
+    exact = (x.astype(np.float64) * rd64).astype(np.float32)
+    t_used = np.where(np.abs(f - np.float32(0.5)) > np.float32(1e-4), t, exact)
+    ref = (x.astype(np.float64) / d.astype(np.float64)).astype(np.float32)
+    # roundf: round half away from zero
+    rnd = lambda v: np.sign(v) * np.floor(np.abs(v) + np.float32(0.5))  # noqa: E731
+    assert np.array_equal(rnd(t_used.astype(np.float64)), rnd(ref.astype(np.float64)))
+    assert np.array_equal(exact, ref)  # the fp64 route alone is exact for every sample
+
+
+@pytest.mark.parametrize("qt", ["Q4_K", "Q5_K", "Q2_K", "Q4_1", "Q5_1", "Q6_K", "Q8_0"])
+def test_device_weights_are_centred(qt):
+    """The chains' synthetic weights have mean ~0 (no offset shared by every output row)."""
+    pytest.importorskip("torch")
+    from kernel_anvil.quants import make_weights_device
+
+    nrows, K = 256, 4096
+    W = make_weights_device(qt, nrows, K, seed=5, device="cpu").numpy()
+    w = oracle.dequantize(qt, W, nrows, K).astype(np.float64)
+    assert abs(w.mean()) < 0.02 * w.std(), (w.mean(), w.std())
