@@ -90,6 +90,9 @@ def parse_args():
                          "scaling)")
     ap.add_argument("--nwarps", type=int, default=0, help="persistent executor: warps per CTA (0 = 8)")
     ap.add_argument("--ctas-per-sm", type=int, default=0, help="persistent executor: CTAs per SM (0 = 1)")
+    ap.add_argument("--static-share", type=int, default=None,
+                    help="persistent executor: percent of each group's tiles dealt round-robin, the "
+                         "rest claimed at run time (default: the library's)")
     return ap.parse_args()
 
 
@@ -447,7 +450,8 @@ def run_anvil(args) -> None:
                      coresident=args.coresident, executor=args.executor,
                      dist=dist if shard and world > 1 else None, nwarps=args.nwarps,
                      ctas_per_sm=args.ctas_per_sm, grouped=bool(args.grouped) and not persistent,
-                     glu=bool(args.glu), dataflow=not args.fixed_inputs)
+                     glu=bool(args.glu), dataflow=not args.fixed_inputs,
+                     static_share=args.static_share)
     stream = torch.cuda.Stream(device=dev)
     hbm_peak, peak_kind = measured_peaks()
     # whole job: the unsharded chain once (shards), or every replica's chain
@@ -577,6 +581,7 @@ def run_anvil(args) -> None:
     if persistent:
         status |= take_status()
         pinfo = dc.pchain.info()
+        pinfo["static_share_pct"] = args.static_share if args.static_share is not None else "default"
         n_groups = pinfo["groups"]
     if graph is not None:
         # the graph holds NCCL work: release it before the process group goes away

@@ -316,6 +316,12 @@ int anvil_pchain_add_glu(anvil_pchain *chain, int ggml_type, const void *W_gate,
 /* Parity probe: the staged activation of group `group` ({fp32 d8, 32 quants} per 32 values,
  * ncols * K/32 blocks of 36 bytes) is written to `out` by the first CTA. */
 int anvil_pchain_set_group_dump(anvil_pchain *chain, int group, void *out);
+/* Load balance (before anvil_pchain_instantiate): `percent` of each group's tiles (rounded
+ * down to whole tiles per warp) are dealt round-robin over the grid's warps; the rest are
+ * claimed one at a time, from a per-group counter, by whichever warp has room for its next
+ * weight copy first.  Default 100 (only the tiles left over after whole rounds are
+ * claimed); 0 claims every tile.  The outputs do not depend on it. */
+int anvil_pchain_set_static_share(anvil_pchain *chain, int percent);
 /* nwarps per CTA (0 = 8), CTAs per SM (0 = 1); allocates the device descriptors. */
 int anvil_pchain_instantiate(anvil_pchain *chain, int nwarps, int ctas_per_sm);
 /* Optional timestamps: buf holds grid * ngroups * 4 words; for each CTA and group,

@@ -56,6 +56,7 @@ namespace anvil {
 
 constexpr int kPcMaxRanks = ANVIL_MAX_RANKS;
 constexpr int kPcSlots = 8;              // tiles in flight per warp
+constexpr int kPcStaticPct = 100;        // default share of a group's tiles dealt round-robin
 // Status flags: 1 (kStatusMbarTimeout) = a weight copy did not land in time, set by
 // mbar_wait_bounded; 2 = an input word did not arrive in time.
 constexpr int kStatusInputTimeout = 2;
@@ -83,21 +84,28 @@ struct PcGemv {
     int tile_base, ntiles;     // tiles of this GEMV within its group
 };
 
+// Tiles of a group: tiles [0, spw * nw) are dealt round-robin over the nw warps of the grid
+// (warp gw takes rot-shifted tiles gw - rot + k nw, k < spw); the rest are claimed one at a
+// time from the group's counter by whichever warp has ring room first, so warps that start
+// the group early (or run faster) take more of its tail.
 struct PcGroup {
     const float *x;            // fixed fp32 input (ncols x K), or null
     const uint64_t *src;       // chained: this rank's output words of the source GEMV
     uint8_t *dump;             // optional: staged Q8_1 blocks written here (parity probe)
     int K, first, count, ntiles, rot, family;
+    int spw;                   // round-robin tiles per warp
 };
 
 struct PcArgs {
     const PcGroup *groups;
     const PcGemv *gemvs;
     uint64_t *trace;            // optional: per CTA and group {start, staged, done, 1}
+    int *claims;                // tile counters: [2 epoch parities][ngroups]
     uint64_t wait_ns;           // bound on every wait
     int ngroups, world, rank;
     int act_off[2], ring_off, ring_bytes;  // activation buffers of even / odd groups, rings
-    uint32_t epoch;             // this launch's number (1, 2, ...): the flag of its words
+    uint32_t epoch;             // this launch's number: the flag of its words (never 0; its
+                                // parity alternates from launch to launch)
 };
 
 // ---- flagged words -----------------------------------------------------------------------
@@ -232,8 +240,8 @@ __device__ __forceinline__ float quant_chunk(const float (&v)[16], bool live, in
 // One warp's share of a chained group's staging: 512-value blocks warp, warp + nwarps, ...
 // of the NCOLS columns of flagged words, read as they arrive, d8 kept in fp32; the warp's
 // column maxima go to colmax[c].  Not inlined, and one block of words in flight per lane:
-// the kernel body around it holds the registers its tile runs need, and a second block in
-// flight makes this function spill to local memory on every pass.
+// the kernel body around it holds the registers its tile runs need.  (A second block in
+// flight measured slower on the Llama-3-70B chain: 11.7 against 11.1 ms per token.)
 template <int QT, int NCOLS>
 __device__ __noinline__ void warp_stage_ll(const uint64_t *__restrict__ src, int K, uint32_t epoch,
                                            uint64_t wait_ns, uint32_t act_off, float *colmax) {
@@ -409,6 +417,7 @@ __device__ __forceinline__ void pc_tile(const PcOut &o, uint32_t stage_off, int 
 struct PcCursor {
     int g, i;
     int g_ntiles;              // tiles of group g
+    int k;                     // tiles this warp has taken of group g so far
     int m, t_base, t_end;      // current GEMV index and its tile range in the group
     const uint8_t *W, *W2;
     int row_bytes, rpb, trows, nrows, alloc, type, variant;
@@ -425,6 +434,7 @@ struct PcRing {
 struct PcWarp {
     uint8_t *ring;
     uint64_t *bars;
+    int2 *tiles;               // per ring slot: {group, tile} of the copy issued into it
     int gw, nw, lane;
     uint32_t R;
 };
@@ -455,34 +465,37 @@ __device__ __forceinline__ void pc_load_gemv(const PcArgs &a, PcCursor &c) {
     c.variant = gm->variant;
 }
 
-// Moves `c` to the first group (from c.g on) that holds a tile of this warp
-// (c.g == ngroups: none left) and loads that tile's GEMV.
-__device__ __forceinline__ void pc_settle(const PcArgs &a, PcCursor &c, int gw, int nw) {
+// Moves the producer cursor to this warp's next tile: its round-robin tiles of group c.g
+// first, then tiles claimed from the group's counter (lane 0 claims, every lane takes the
+// result), then on to the next group once the group has none left (c.g == ngroups: the
+// chain is done).  Loads the tile's GEMV when it differs from the current one.  Called by
+// the whole warp.
+__device__ __forceinline__ void pc_next(const PcArgs &a, PcCursor &c, const PcWarp &w) {
     while (c.g < a.ngroups) {
-        c.g_ntiles = a.groups[c.g].ntiles;
-        if (c.i < c.g_ntiles) {
-            pc_load_gemv(a, c);
+        const PcGroup *gp = a.groups + c.g;
+        int i;
+        if (c.k < gp->spw) {
+            i = pc_first(gp->rot, w.gw, w.nw) + c.k * w.nw;
+        } else {
+            int t = 0;
+            if (w.lane == 0) t = atomicAdd(a.claims + (a.epoch & 1u) * a.ngroups + c.g, 1);
+            i = gp->spw * w.nw + __shfl_sync(0xffffffffu, t, 0);
+        }
+        ++c.k;
+        if (i < gp->ntiles) {
+            c.g_ntiles = gp->ntiles;
+            c.i = i;
+            if (i < c.t_base || i >= c.t_end) pc_load_gemv(a, c);
             return;
         }
         ++c.g;
-        if (c.g < a.ngroups) c.i = pc_first(a.groups[c.g].rot, gw, nw);
+        c.k = 0;
+        c.t_base = c.t_end = 0;  // the next tile loads its GEMV
     }
 }
 
-__device__ __forceinline__ void pc_advance(const PcArgs &a, PcCursor &c, int gw, int nw) {
-    c.i += nw;
-    if (c.i >= c.t_end) {
-        if (c.i < c.g_ntiles) {
-            pc_load_gemv(a, c);
-        } else {
-            ++c.g;
-            if (c.g < a.ngroups) c.i = pc_first(a.groups[c.g].rot, gw, nw);
-            pc_settle(a, c, gw, nw);
-        }
-    }
-}
-
-// Issues tiles while the ring and the mbarrier slots have room.
+// Issues tiles while the ring and the mbarrier slots have room, recording each slot's tile
+// for the consumer.  The cursor holds the next tile, claimed as the previous one is issued.
 __device__ __forceinline__ void pc_produce(const PcArgs &a, PcRing &r, const PcWarp &w) {
     while (r.pc.g < a.ngroups && r.issued - r.consumed < uint32_t(kPcSlots)) {
         const uint32_t alloc = uint32_t(r.pc.alloc);
@@ -494,6 +507,7 @@ __device__ __forceinline__ void pc_produce(const PcArgs &a, PcRing &r, const PcW
         const uint32_t pos = wrap ? 0u : r.p_pos;
         if (w.lane == 0) {
             const int slot = int(r.issued % kPcSlots);
+            w.tiles[slot] = make_int2(r.pc.g, r.pc.i);
             const int r0 = (r.pc.i - r.pc.t_base) * r.pc.trows;
             const int rows = min(r.pc.trows, r.pc.nrows - r0);
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -523,8 +537,22 @@ __device__ __forceinline__ void pc_produce(const PcArgs &a, PcRing &r, const PcW
         r.p_total += need;
         r.p_pos = pos + alloc;
         ++r.issued;
-        pc_advance(a, r.pc, w.gw, w.nw);
+        pc_next(a, r.pc, w);
     }
+    __syncwarp();  // the slots' tile records are visible to every lane
+}
+
+// The tile at the head of this warp's ring ({ngroups, 0}: the chain has no tile left for
+// it), issuing copies first if the ring is empty.  The ring state stays in shared memory.
+__device__ __noinline__ int2 pc_head(const PcArgs &a, PcRing *rs, const PcWarp &w) {
+    PcRing r = *rs;
+    __syncwarp();
+    if (r.issued == r.consumed) {
+        pc_produce(a, r, w);
+        if (w.lane == 0) *rs = r;
+        __syncwarp();
+    }
+    return r.issued == r.consumed ? make_int2(a.ngroups, 0) : w.tiles[r.consumed % kPcSlots];
 }
 
 // Trace stamps of warp 0 (thread 0) per CTA and group: 0 its staging share starts, 1 it ends,
@@ -533,11 +561,12 @@ __device__ __forceinline__ void pc_trace(const PcArgs &a, int g, int k) {
     if (a.trace && threadIdx.x == 0) a.trace[(size_t(blockIdx.x) * a.ngroups + g) * 4 + k] = global_timer_ns();
 }
 
-// This warp's tiles of one GEMV of the current group, cc.i, cc.i + nw, ... < cc.t_end: wait
-// for each tile's copy (bounded), fix up unaligned row ends, dot and store, refill the ring.
-// One call per GEMV and warp (the tile arithmetic is compiled into the loop).  The warp's
-// ring state lives in shared memory between calls (rs): held in registers here, written
-// back at the end, so the kernel body keeps no ring state across its other work.
+// This warp's tiles at the head of its ring while they belong to GEMV cc.m of group cc.g:
+// wait for each tile's copy (bounded), fix up unaligned row ends, dot and store, refill the
+// ring.  One call per run of tiles of one GEMV (the tile arithmetic is compiled into the
+// loop).  The warp's ring state lives in shared memory between calls (rs): held in
+// registers here, written back at the end, so the kernel body keeps no ring state across
+// its other work.
 template <int QT, int NCOLS, int RPB, int LBT, bool GLU>
 __device__ __noinline__ void pc_run(const PcArgs &a, PcRing *rs, PcWarp w, PcCursor cc, PcOut o,
                                     uint32_t act_off, float sc0, float sc1, int *s_failed) {
@@ -548,14 +577,18 @@ __device__ __noinline__ void pc_run(const PcArgs &a, PcRing *rs, PcWarp w, PcCur
     PcRing r = *rs;
     __syncwarp();
     const int K = a.groups[cc.g].K;
-    for (; cc.i < cc.t_end; cc.i += w.nw) {
+    for (;;) {
         if (r.issued == r.consumed) pc_produce(a, r, w);
+        if (r.issued == r.consumed) break;
+        const int slot = int(r.consumed % kPcSlots);
+        const int2 head = w.tiles[slot];
+        if (head.x != cc.g || head.y < cc.t_base || head.y >= cc.t_end) break;
+        cc.i = head.y;
         const uint32_t alloc = uint32_t(cc.alloc);
         const bool wrap = r.c_pos + alloc > w.R;
         const uint32_t pos = wrap ? 0u : r.c_pos;
         const int r0 = (cc.i - cc.t_base) * cc.trows;
         const int rows = min(cc.trows, cc.nrows - r0);
-        const int slot = int(r.consumed % kPcSlots);
         const uint32_t parity = (r.consumed / kPcSlots) & 1u;
         const uint8_t *src = cc.W + size_t(r0) * size_t(cc.row_bytes);
         const uintptr_t s = GLU ? 0 : reinterpret_cast<uintptr_t>(src);
@@ -665,14 +698,20 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) pchain_kernel(const __grid_
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ float s_max[2][kMaxWarps][2];  // per activation buffer, warp, column: input max
     __shared__ PcRing s_ring[kMaxWarps];      // each warp's ring state between tile runs
+    __shared__ int2 s_tiles[kMaxWarps][kPcSlots];
     __shared__ int s_failed;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nwarps = blockDim.x >> 5;
     if (tid == 0) s_failed = pc_failed() ? 1 : 0;
+    // The next launch's tile counters: nothing of this launch touches them, and the next
+    // launch starts after this one has ended.
+    if (blockIdx.x == 0)
+        for (int g = tid; g < a.ngroups; g += blockDim.x) a.claims[((a.epoch + 1u) & 1u) * a.ngroups + g] = 0;
 
     PcWarp w;
     w.ring = smem + a.ring_off + size_t(warp) * a.ring_bytes;
     w.bars = reinterpret_cast<uint64_t *>(smem) + warp * kPcSlots;
+    w.tiles = s_tiles[warp];
     w.nw = gridDim.x * nwarps;
     w.gw = blockIdx.x * nwarps + warp;
     w.lane = lane;
@@ -681,10 +720,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) pchain_kernel(const __grid_
     {
         PcRing r{};
         r.pc.g = 0;
-        if (a.ngroups > 0) {
-            r.pc.i = pc_first(a.groups[0].rot, w.gw, w.nw);
-            pc_settle(a, r.pc, w.gw, w.nw);
-        }
+        pc_next(a, r.pc, w);
         if (lane == 0) {
             for (int s = 0; s < kPcSlots; ++s) mbar_init(&w.bars[s], 1);
             mbar_fence_init();
@@ -728,9 +764,11 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) pchain_kernel(const __grid_
         // ---- 2. this warp's tiles of the group, one run per GEMV ----------------------------
         PcCursor cc{};
         cc.g = g;
-        cc.i = pc_first(cur.rot, w.gw, w.nw);
         cc.g_ntiles = cur.ntiles;
-        while (cc.i < cc.g_ntiles) {
+        for (;;) {
+            const int2 head = pc_head(a, &s_ring[warp], w);
+            if (head.x != g) break;
+            cc.i = head.y;
             pc_load_gemv(a, cc);
             const PcGemv *gm = a.gemvs + cc.m;
             PcOut o;
@@ -741,7 +779,6 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) pchain_kernel(const __grid_
             o.perm = gm->perm;
             o.world = a.world;
             pc_run_any<NCOLS>(a, &s_ring[warp], w, cc, o, act_off, sc[0], sc[1], &s_failed);
-            cc.i += ((cc.t_end - cc.i + w.nw - 1) / w.nw) * w.nw;  // first tile past this GEMV
         }
         pc_trace(a, g, 3);
         // ---- 3. this warp's share of the next group's input, into the other buffer ----------
@@ -814,6 +851,8 @@ struct anvil_pchain {
     PcGroup *d_groups = nullptr;
     PcGemv *d_gemvs = nullptr;
     uint64_t *trace = nullptr;
+    int *claims = nullptr;       // tile counters, [2][groups]
+    int static_pct = kPcStaticPct;
     PcKernel fn = nullptr;
     int grid = 0, nwarps = 0, smem = 0, ring_bytes = 0, ring_off = 0;
     int act_off[2] = {0, 0};
@@ -1091,7 +1130,13 @@ int anvil_pchain_instantiate(anvil_pchain *c, int nwarps, int ctas_per_sm) {
     for (PcGroup &g : c->groups) {
         g.rot = int(cum % nw);
         cum += g.ntiles;
+        g.spw = int((long(g.ntiles) * c->static_pct / 100) / nw);
     }
+    e = cudaMalloc(&c->claims, sizeof(int) * 2 * c->groups.size());
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(claims)");
+    c->owned.push_back(c->claims);
+    e = cudaMemset(c->claims, 0, sizeof(int) * 2 * c->groups.size());
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemset(claims)");
 
     e = cudaMalloc(&c->d_groups, sizeof(PcGroup) * c->groups.size());
     if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(groups)");
@@ -1104,6 +1149,14 @@ int anvil_pchain_instantiate(anvil_pchain *c, int nwarps, int ctas_per_sm) {
     if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy(gemvs)");
     for (size_t m = 0; m < dg.size(); ++m) c->gemvs[m].d = dg[m];
     c->ready = true;
+    return ANVIL_OK;
+}
+
+int anvil_pchain_set_static_share(anvil_pchain *c, int percent) {
+    if (!c) return fail(ANVIL_ERR_INVALID, "null chain");
+    if (c->ready) return fail(ANVIL_ERR_INVALID, "chain already instantiated");
+    if (percent < 0 || percent > 100) return fail(ANVIL_ERR_INVALID, "static share %d%% outside 0..100", percent);
+    c->static_pct = percent;
     return ANVIL_OK;
 }
 
@@ -1121,6 +1174,7 @@ int anvil_pchain_launch(anvil_pchain *c, anvil_stream_t stream) {
     a.groups = c->d_groups;
     a.gemvs = c->d_gemvs;
     a.trace = c->trace;
+    a.claims = c->claims;
     a.wait_ns = wait_limit_ns();
     a.ngroups = int(c->groups.size());
     a.world = c->world;
@@ -1130,7 +1184,7 @@ int anvil_pchain_launch(anvil_pchain *c, anvil_stream_t stream) {
     a.ring_off = c->ring_off;
     a.ring_bytes = c->ring_bytes;
     a.epoch = c->epoch + 1;
-    if (a.epoch == 0) a.epoch = 1;  // 0 is the flag of zeroed buffers
+    if (a.epoch == 0) a.epoch = 2;  // 0 is the flag of zeroed buffers; the parity alternates
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(unsigned(c->grid));
     cfg.blockDim = dim3(unsigned(c->nwarps * 32));

@@ -207,6 +207,7 @@ SIGNATURES = {
     "anvil_pchain_add_glu": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p,
                                      c_int]),
     "anvil_pchain_set_group_dump": (c_int, [c_void_p, c_int, c_void_p]),
+    "anvil_pchain_set_static_share": (c_int, [c_void_p, c_int]),
     "anvil_pchain_instantiate": (c_int, [c_void_p, c_int, c_int]),
     "anvil_pchain_set_trace": (c_int, [c_void_p, c_void_p]),
     "anvil_pchain_launch": (c_int, [c_void_p, c_void_p]),

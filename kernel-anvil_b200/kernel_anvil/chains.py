@@ -236,7 +236,7 @@ class DeviceChain:
                  rank: int = 0, world: int = 1, nwarps: int = 0, rows_per_block: int = 0,
                  configs: dict | None = None, fused: bool = False, coresident: int = 1,
                  executor: str = "graph", dist=None, ctas_per_sm: int = 0, grouped: bool = False,
-                 glu: bool = False, dataflow: bool = True):
+                 glu: bool = False, dataflow: bool = True, static_share: int | None = None):
         import torch
 
         from kernel_anvil.mmvq import Chain, q8_1_bytes
@@ -330,9 +330,10 @@ class DeviceChain:
                                         nwarps=nw, rows_per_block=rpb)
                 self.outputs.append(y)
         else:
-            self._build_persistent(device, nwarps, ctas_per_sm, dist, dataflow)
+            self._build_persistent(device, nwarps, ctas_per_sm, dist, dataflow, static_share)
 
-    def _build_persistent(self, device, nwarps: int, ctas_per_sm: int, dist, dataflow: bool) -> None:
+    def _build_persistent(self, device, nwarps: int, ctas_per_sm: int, dist, dataflow: bool,
+                          static_share: int | None) -> None:
         from kernel_anvil.pchain import PeerArena, PersistentChain, output_words_bytes
 
         spec, ncols = self.spec, self.ncols
@@ -380,6 +381,8 @@ class DeviceChain:
             assert idx == j
             for k in it:
                 self.pidx[k] = j
+        if static_share is not None:
+            pc.set_static_share(static_share)
         pc.instantiate(nwarps=nwarps, ctas_per_sm=ctas_per_sm)
         self.pchain = pc
         self._items = items

@@ -337,12 +337,23 @@ def cmd_profile(args) -> None:
     from kernel_anvil.profile import profile_kernel
     from kernel_anvil.specs import B200, detect_gpu
 
+    import torch
+
     runner = _load_runner(args.runner)
     gpu = detect_gpu() or B200
-    inputs = runner.setup()
     cfg = dict(getattr(runner, "BASELINE_CONFIG", {}))
-    m = profile_kernel(lambda c: runner.run(inputs, **c), cfg, getattr(runner, "DATA_BYTES", None),
-                       gpu, args.warmup, args.runs)
+    if args.ncu_csv and not torch.cuda.is_available():
+        # a recorded capture classified without a GPU: time and DRAM bytes come from the
+        # CSV; registers, shared memory and occupancy are unknown (0) without the device
+        from kernel_anvil.analyze import ProfileMetrics
+
+        console.print("[yellow]No GPU: classifying the recorded ncu capture alone[/yellow]")
+        m = ProfileMetrics(duration_ns=0.0,
+                           threads_per_block=cfg.get("nwarps", 0) * 32 or 128)
+    else:
+        inputs = runner.setup()
+        m = profile_kernel(lambda c: runner.run(inputs, **c), cfg, getattr(runner, "DATA_BYTES", None),
+                           gpu, args.warmup, args.runs)
     if args.ncu or args.ncu_csv:
         from kernel_anvil.profile import apply_ncu, parse_ncu_csv, profile_runner_ncu
 

@@ -194,6 +194,10 @@ class PersistentChain:
         check(self._lib.anvil_pchain_set_group_dump(self._h, group, out.data_ptr()))
         self._keep.append(out)
 
+    def set_static_share(self, percent: int) -> None:
+        """Share of each group's tiles dealt round-robin (the rest are claimed at run time)."""
+        check(self._lib.anvil_pchain_set_static_share(self._h, int(percent)))
+
     def instantiate(self, nwarps: int = 0, ctas_per_sm: int = 0) -> None:
         check(self._lib.anvil_pchain_instantiate(self._h, nwarps, ctas_per_sm))
 

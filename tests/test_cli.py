@@ -263,3 +263,34 @@ def test_parse_ncu_csv():
     assert rows[0]["gpu__time_duration.sum"] == pytest.approx(7.25)
     assert rows[1]["gpu__time_duration.sum"] == pytest.approx(1.5)
     assert parse_ncu_csv("no csv here") == []
+
+
+GOLDEN = Path(__file__).parent / "golden"
+
+
+def test_recorded_ncu_capture_parses_to_per_launch_metrics():
+    """tests/golden/ncu_mmvq_q4k_12288x4096.csv: three launches of the Q4_K 12288 x 4096 MMVQ
+    kernel under ncu (one pass of gpu__time_duration and DRAM bytes, clocks left alone)."""
+    from kernel_anvil.analyze import ProfileMetrics
+    from kernel_anvil.profile import apply_ncu, parse_ncu_csv
+    from kernel_anvil.quants import gemv_bytes
+
+    rows = parse_ncu_csv((GOLDEN / "ncu_mmvq_q4k_12288x4096.csv").read_text())
+    assert len(rows) == 3 and all(r["kernel"].startswith("mmvq_kernel<12, 1") for r in rows)
+    m = apply_ncu(ProfileMetrics(duration_ns=0.0), rows)
+    # DRAM reads are the weight bytes (plus the small activation): no re-reads
+    assert m.dram_bytes == pytest.approx(gemv_bytes("Q4_K", 12288, 4096), rel=0.01)
+    assert 9_000 < m.duration_ns < 12_000
+
+
+def test_profile_cli_classifies_recorded_capture_as_bandwidth_bound(capsys, monkeypatch):
+    """`kernel-anvil profile RUNNER --ncu-csv CSV` on a host without a GPU: the recorded capture
+    of the Q4_K 28672 x 8192 GEMV (132 MB read in about 27 us per cold launch) goes through
+    parse -> apply_ncu -> classify and comes out bandwidth_bound."""
+    import torch
+
+    monkeypatch.setattr(torch.cuda, "is_available", lambda: False)
+    cli.main(["profile", str(GOLDEN / "runner_mmvq_q4k_28672x8192.py"),
+              "--ncu-csv", str(GOLDEN / "ncu_mmvq_q4k_28672x8192.csv")])
+    out = capsys.readouterr().out
+    assert "Classification: bandwidth_bound" in out

@@ -443,3 +443,40 @@ def test_pchain_chained_gate_up_matches_oracle(n):
     err = oracle.max_rel_err(got, ref)
     assert err <= Y_TOL, f"n={n} shape {pc.gemv_shape(ig)}: error {err}, got max {np.abs(got).max()}, ref max {np.abs(ref).max()}"
     pc.close()
+
+
+@pytest.mark.parametrize("share", [0, 40, 100])
+def test_pchain_static_share_does_not_change_outputs(share):
+    """Tiles dealt round-robin or claimed at run time: bit-identical outputs, token after token
+    (the counters of both epoch parities are reused), and the oracle agrees."""
+    pc_ref, pc = PersistentChain(), PersistentChain()
+    desc_ref, _ = _decoder(pc_ref, K=2048, inter=4096, seed=70)
+    desc, _ = _decoder(pc, K=2048, inter=4096, seed=70)
+    pc.set_static_share(share)
+    pc_ref.instantiate()
+    pc.instantiate()
+    for _ in range(3):
+        pc_ref.launch()
+        pc.launch()
+    torch.cuda.synchronize()
+    assert take_status() == 0
+    for d in desc:
+        a, b = pc_ref.output(d[0]), pc.output(d[0])
+        assert torch.equal(a, b), f"GEMV {d[0]} differs with a {share}% static share"
+    _oracle_check(pc, desc)
+    pc_ref.close()
+    pc.close()
+
+
+def test_pchain_static_share_argument_errors():
+    pc = PersistentChain()
+    pc.add_group(dev(make_activation(256, seed=1)))
+    pc.add_gemv(dev(make_weights("Q4_K", 64, 256, seed=2)), "Q4_K", nrows=64)
+    with pytest.raises(AnvilError):
+        pc.set_static_share(101)
+    with pytest.raises(AnvilError):
+        pc.set_static_share(-1)
+    pc.instantiate()
+    with pytest.raises(AnvilError):
+        pc.set_static_share(50)
+    pc.close()
