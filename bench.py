@@ -90,6 +90,9 @@ def parse_args():
                          "scaling)")
     ap.add_argument("--nwarps", type=int, default=0, help="persistent executor: warps per CTA (0 = 8)")
     ap.add_argument("--ctas-per-sm", type=int, default=0, help="persistent executor: CTAs per SM (0 = 1)")
+    ap.add_argument("--ncols", type=int, default=1,
+                    help="activation columns per step (speculative-decode verification batch; the "
+                         "persistent executor takes 1 or 2, the graph executor 1..8)")
     ap.add_argument("--static-share", type=int, default=None,
                     help="persistent executor: percent of each group's tiles dealt round-robin, the "
                          "rest claimed at run time (default: the library's)")
@@ -291,14 +294,19 @@ def time_graph(launch, stream, steps: int) -> float:
 
 
 def dominant_kernel(dc, stream, steps: int, warmup: int) -> dict:
-    """Graph executor: the Q4_K MMVQ launches of one chain step, launched as in the chain (one
-    launch per run of Q4_K GEMVs on one input when grouped) and replayed as their own PDL
-    graph."""
+    """Graph executor: the MMVQ launches of the chain's dominant weight type (the most weight
+    bytes) in one step, launched as in the chain (one launch per run of that type's GEMVs on
+    one input when grouped) and replayed as their own PDL graph."""
     import torch
 
     from kernel_anvil.chains import is_gate_up
     from kernel_anvil.mmvq import Chain, q8_1_bytes
-    from kernel_anvil.quants import gemv_bytes
+    from kernel_anvil.quants import gemv_bytes, resolve_type
+
+    by_type: dict = {}
+    for g in dc.spec.gemvs:
+        by_type[g.qt] = by_type.get(g.qt, 0) + g.nrows * resolve_type(g.qt).row_bytes(g.K)
+    qt_dom = max(by_type, key=by_type.get)
 
     ch = Chain()
     nbytes, n = 0, 0
@@ -311,12 +319,12 @@ def dominant_kernel(dc, stream, steps: int, warmup: int) -> dict:
             while (j < len(gemvs) and j - i < 4 and gemvs[j][0].input == gm.input
                    and gemvs[j][0].qt == gm.qt):
                 j += 1
-        if gm.qt == "Q4_K" and dc.glu and is_gate_up([g for g, _, _, _ in gemvs[i:j]]):
+        if gm.qt == qt_dom and dc.glu and is_gate_up([g for g, _, _, _ in gemvs[i:j]]):
             ch.add_mmvq_glu(gemvs[i][1], gemvs[i + 1][1], gm.qt, dc.xq[gm.input], gemvs[i][2])
             r = gemvs[i][3][1] - gemvs[i][3][0]
             nbytes += 2 * gemv_bytes(gm.qt, r, gm.K, 1) - 4 * r - q8_1_bytes(gm.K)
             n += 1
-        elif gm.qt == "Q4_K":
+        elif gm.qt == qt_dom:
             run = gemvs[i:j]
             rows = [r1 - r0 for _, _, _, (r0, r1) in run]
             ch.add_mmvq_grouped([w for _, w, _, _ in run], gm.qt, dc.xq[gm.input],
@@ -330,7 +338,8 @@ def dominant_kernel(dc, stream, steps: int, warmup: int) -> dict:
             ch.launch()
         ms = time_graph(ch.launch, stream, steps)
     ch.close()
-    return {"launches_per_step": n, "bytes_per_launch": nbytes / n, "ms_per_launch": ms / n}
+    return {"launches_per_step": n, "bytes_per_launch": nbytes / n, "ms_per_launch": ms / n,
+            "qt": qt_dom}
 
 
 def traffic_per_launch(kernel: str) -> tuple[float | None, str | None]:
@@ -451,11 +460,12 @@ def run_anvil(args) -> None:
                      dist=dist if shard and world > 1 else None, nwarps=args.nwarps,
                      ctas_per_sm=args.ctas_per_sm, grouped=bool(args.grouped) and not persistent,
                      glu=bool(args.glu), dataflow=not args.fixed_inputs,
-                     static_share=args.static_share)
+                     static_share=args.static_share, ncols=args.ncols)
     stream = torch.cuda.Stream(device=dev)
     hbm_peak, peak_kind = measured_peaks()
     # whole job: the unsharded chain once (shards), or every replica's chain
-    one_chain = spec.glu_algorithmic_bytes() if (persistent or dc.glu) else spec.algorithmic_bytes()
+    one_chain = (spec.glu_algorithmic_bytes(args.ncols) if (persistent or dc.glu)
+                 else spec.algorithmic_bytes(args.ncols))
     total_bytes = one_chain * (1 if shard else world)
     rank_bytes = dc.algorithmic_bytes       # this rank's launches
 
@@ -571,7 +581,8 @@ def run_anvil(args) -> None:
         roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                     "frac": round(achieved / hbm_peak, 4), "traffic": traffic, "traffic_source": tsrc,
                     "peak_source": peak_source,
-                    "kernel": "mmvq_kernel<Q4_K, ncols=1> (all Q4_K launches of one step, PDL graph)",
+                    "kernel": f"mmvq_kernel<{dk['qt']}, ncols={dc.ncols}> (all {dk['qt']} launches of "
+                              "one step, PDL graph)",
                     "launches_per_step": dk["launches_per_step"],
                     "bytes_per_launch": round(dk["bytes_per_launch"]),
                     "us_per_launch": round(dk["ms_per_launch"] * 1e3, 3)}
@@ -618,7 +629,7 @@ def run_anvil(args) -> None:
         "vs_baseline": None,
         "dtype": "int8 dp4a / fp32", "data": "synthetic",
         "config": {"workload": f"{args.workload} per-token GEMV chain",
-                   "gemvs_per_step": len(spec.gemvs),
+                   "gemvs_per_step": len(spec.gemvs), "ncols": args.ncols,
                    "groups_per_step": n_groups if persistent else None,
                    "quantizations_per_step": n_groups if persistent else n_quantize,
                    "bytes_per_step": total_bytes, "weight_bytes": spec.weight_bytes(),

@@ -411,6 +411,37 @@ def cmd_autoforge(args) -> None:
             json.dump([r.__dict__ for r in res.all_results], f, indent=1)
 
 
+def chain_tensors(spec, layers: int) -> list[tuple[str, str, int, int]]:
+    """(tensor name, quant, N rows, K cols) of a chain's GEMVs in its first `layers` decoder
+    layers (blk.<i>.<name>.weight), its other GEMVs once per unique shape (name.weight)."""
+    out, seen = [], set()
+    for g in spec.gemvs:
+        parts = g.name.split(".")
+        if parts[0] == "blk" and len(parts) > 2 and parts[1].isdigit():
+            if int(parts[1]) < layers:
+                out.append((g.name + ".weight", g.qt, g.nrows, g.K))
+        elif (g.qt, g.nrows, g.K) not in seen:
+            seen.add((g.qt, g.nrows, g.K))
+            out.append((g.name + ".weight", g.qt, g.nrows, g.K))
+    return out
+
+
+def cmd_write_gguf(args) -> None:
+    from kernel_anvil.chains import CHAINS, get_chain
+    from kernel_anvil.gguf import write_gguf
+
+    if args.chain not in CHAINS:
+        console.print(f"[red]Unknown chain {args.chain!r} (known: {', '.join(CHAINS)})[/red]")
+        sys.exit(1)
+    if args.layers < 1:
+        console.print("[red]--layers must be at least 1[/red]")
+        sys.exit(1)
+    tensors = chain_tensors(get_chain(args.chain), args.layers)
+    path = write_gguf(args.output, tensors, name=args.chain, arch=args.chain.split("_")[0],
+                      seed=args.seed)
+    console.print(f"Wrote {path}: {len(tensors)} tensors")
+
+
 def cmd_chain_sweep(args) -> None:
     """Time a whole decode chain (CUDA graph, PDL) once with the built-in per-shape launch and
     once per global nwarps; report us/token and optionally write the winner as smithy JSON."""
@@ -532,6 +563,16 @@ def build_parser() -> argparse.ArgumentParser:
                    help="key cells by the reference's (ne0, ne1) instead of (rows, cols)")
     p.add_argument("--json", help="also write every measured point here")
     p.set_defaults(fn=cmd_autoforge)
+
+    p = sub.add_parser("write-gguf", help="Write a GGUF of a built-in chain's weight tensors "
+                                          "(seeded synthetic blocks) for gguf-optimize / autoforge")
+    p.add_argument("chain", help="built-in chain (qwen3_8b, qwen3_0_6b, llama3_70b, qwen35_27b)")
+    p.add_argument("output", help="GGUF path to write")
+    p.add_argument("--layers", type=int, default=1,
+                   help="decoder layers to write (the tail, e.g. the output head, is always written); "
+                        "every unique GEMV shape appears from one layer on (default: 1)")
+    p.add_argument("--seed", type=int, default=0)
+    p.set_defaults(fn=cmd_write_gguf)
 
     p = sub.add_parser("chain-sweep", help="Pick one nwarps for a whole decode chain by chain time")
     p.add_argument("--chain", default="qwen3_8b")

@@ -294,3 +294,25 @@ def test_profile_cli_classifies_recorded_capture_as_bandwidth_bound(capsys, monk
               "--ncu-csv", str(GOLDEN / "ncu_mmvq_q4k_28672x8192.csv")])
     out = capsys.readouterr().out
     assert "Classification: bandwidth_bound" in out
+
+
+def test_write_gguf_chain_layers(tmp_path):
+    """write-gguf: one decoder layer of a chain holds every unique GEMV shape of the chain."""
+    from kernel_anvil.chains import get_chain
+
+    out = tmp_path / "draft.gguf"
+    cli.main(["write-gguf", "qwen3_0_6b", str(out), "--layers", "1"])
+    prof = parse_gguf(out)
+    assert set(prof.gemv_shapes()) == set(get_chain("qwen3_0_6b").unique_shapes())
+    assert {t.name for t in prof.tensors} == {f"blk.0.{n}.weight" for n in (
+        "attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up", "ffn_down")}
+    assert _run(["write-gguf", "no_such_chain", str(tmp_path / "x.gguf")]) == 1
+    assert _run(["write-gguf", "qwen3_0_6b", str(tmp_path / "y.gguf"), "--layers", "0"]) == 1
+
+
+def test_chain_tensors_keeps_tail_once():
+    from kernel_anvil.chains import get_chain
+
+    t = cli.chain_tensors(get_chain("qwen3_8b"), 2)
+    assert sum(1 for n, *_ in t if n.startswith("blk.")) == 14
+    assert [n for n, *_ in t if not n.startswith("blk.")] == ["output.weight"]

@@ -192,3 +192,23 @@ def test_concurrent_lookups_and_resets(sandbox_home, tmp_path, monkeypatch):
     for t in ts:
         t.join()
     assert not bad
+
+
+@pytest.mark.parametrize("name,types", [("smithy_qwen3_8b_plus_draft.json", {8, 12, 14}),
+                                        ("smithy_qwen35_27b.json", {12, 13})])
+def test_recorded_tuner_outputs_load_like_the_reference(golden_dir, tmp_path, name, types):
+    """Configs the tuner wrote on a B200 (gguf-optimize with a draft model; autoforge on the
+    Qwen3.5-27B shapes) load with the same cells in this loader and in the reference's."""
+    doc = (golden_dir / name).read_text()
+    n, cells = anvil_load_doc(tmp_path, doc, name)
+    assert n > 0 and {c[0] for c in cells} == types
+    ref = oracle.ref_smithy()
+    if ref is None:
+        pytest.skip("oracle/_ref/libsmithy_ref.so not built (reference tree absent)")
+    p = tmp_path / f"ref_{name}"
+    p.write_text(doc)
+    ref.ref_smithy_clear()
+    assert ref.ref_smithy_load(str(p).encode())
+    ref_cells = table_cells(lambda t, n_, k, a, b: ref.ref_smithy_cell(
+        t, bucket_index(n_), bucket_index(k), a, b))
+    assert cells == ref_cells
