@@ -67,8 +67,15 @@ enum anvil_ggml_type {
     ANVIL_TYPE_Q4_K = 12,
     ANVIL_TYPE_Q5_K = 13,
     ANVIL_TYPE_Q6_K = 14,
+    ANVIL_TYPE_IQ2_XXS = 16,
+    ANVIL_TYPE_IQ2_XS = 17,
+    ANVIL_TYPE_IQ3_XXS = 18,
+    ANVIL_TYPE_IQ1_S = 19,
     ANVIL_TYPE_IQ4_NL = 20,
-    ANVIL_TYPE_IQ4_XS = 23
+    ANVIL_TYPE_IQ3_S = 21,
+    ANVIL_TYPE_IQ2_S = 22,
+    ANVIL_TYPE_IQ4_XS = 23,
+    ANVIL_TYPE_IQ1_M = 29
 };
 
 /* Launch flags for anvil_mmvq_ex / anvil_quantize_q8_1_ex. */

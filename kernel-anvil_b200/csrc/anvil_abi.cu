@@ -162,7 +162,9 @@ static int prepare_fn(const void *fn, int dev, int threads, int smem, int *occ) 
 static bool supported_type(int t) {
     return t == kTypeQ4_K || t == kTypeQ5_K || t == kTypeQ6_K || t == kTypeQ8_0 || t == kTypeQ4_0 ||
            t == kTypeQ4_1 || t == kTypeQ5_0 || t == kTypeQ5_1 || t == kTypeQ2_K || t == kTypeQ3_K ||
-           t == kTypeIQ4_NL || t == kTypeIQ4_XS;
+           t == kTypeIQ4_NL || t == kTypeIQ4_XS || t == kTypeIQ2_XXS || t == kTypeIQ2_XS ||
+           t == kTypeIQ2_S || t == kTypeIQ3_XXS || t == kTypeIQ3_S || t == kTypeIQ1_S ||
+           t == kTypeIQ1_M;
 }
 
 static MmvqKernelFn kernel_for(int t, int ncols, int rpb, int lbt, int mode) {
@@ -179,6 +181,13 @@ static MmvqKernelFn kernel_for(int t, int ncols, int rpb, int lbt, int mode) {
     case kTypeQ3_K: return mmvq_kernel_q3k(ncols, rpb, lbt, mode);
     case kTypeIQ4_NL: return mmvq_kernel_iq4nl(ncols, rpb, lbt, mode);
     case kTypeIQ4_XS: return mmvq_kernel_iq4xs(ncols, rpb, lbt, mode);
+    case kTypeIQ2_XXS: return mmvq_kernel_iq2xxs(ncols, rpb, lbt, mode);
+    case kTypeIQ2_XS: return mmvq_kernel_iq2xs(ncols, rpb, lbt, mode);
+    case kTypeIQ2_S: return mmvq_kernel_iq2s(ncols, rpb, lbt, mode);
+    case kTypeIQ3_XXS: return mmvq_kernel_iq3xxs(ncols, rpb, lbt, mode);
+    case kTypeIQ3_S: return mmvq_kernel_iq3s(ncols, rpb, lbt, mode);
+    case kTypeIQ1_S: return mmvq_kernel_iq1s(ncols, rpb, lbt, mode);
+    case kTypeIQ1_M: return mmvq_kernel_iq1m(ncols, rpb, lbt, mode);
     default: return nullptr;
     }
 }
@@ -387,7 +396,8 @@ static int launch_mmvq_segs(const Plan &p, const Segs &sg, const void *x, int32_
                             unsigned flags, cudaStream_t stream, int share = 1) {
     if (p.chunk == 0) return launch_segs_one(p, sg, x, sums, K, flags, stream, share);
     const int nkb = K / 32;
-    const bool sub16 = p.type == kTypeQ6_K || p.type == kTypeQ2_K || p.type == kTypeQ3_K;
+    const bool sub16 = p.type == kTypeQ6_K || p.type == kTypeQ2_K || p.type == kTypeQ3_K ||
+                       p.type == kTypeIQ2_XS || p.type == kTypeIQ2_S || p.type == kTypeIQ1_M;
     const int nsub = K / (sub16 ? 16 : 32);  // int32 sums per row and column (block-sum mode)
     for (int c0 = 0; c0 < p.ncols; c0 += p.chunk) {
         const Plan &q = p.ncols - c0 >= p.chunk ? p : *p.tail;
@@ -560,6 +570,13 @@ int anvil_type_geometry(int ggml_type, int *qk, int *block_bytes) {
     case ANVIL_TYPE_Q2_K: q = 256; b = 84; break;
     case ANVIL_TYPE_IQ4_NL: q = 32; b = 18; break;
     case ANVIL_TYPE_IQ4_XS: q = 256; b = 136; break;
+    case ANVIL_TYPE_IQ2_XXS: q = 256; b = 66; break;
+    case ANVIL_TYPE_IQ2_XS: q = 256; b = 74; break;
+    case ANVIL_TYPE_IQ2_S: q = 256; b = 82; break;
+    case ANVIL_TYPE_IQ3_XXS: q = 256; b = 98; break;
+    case ANVIL_TYPE_IQ3_S: q = 256; b = 110; break;
+    case ANVIL_TYPE_IQ1_S: q = 256; b = 50; break;
+    case ANVIL_TYPE_IQ1_M: q = 256; b = 56; break;
     case ANVIL_TYPE_Q3_K: q = 256; b = 110; break;
     case ANVIL_TYPE_Q4_K: q = 256; b = 144; break;
     case ANVIL_TYPE_Q5_K: q = 256; b = 176; break;
@@ -759,13 +776,16 @@ int anvil_mmvq_block_sums(int ggml_type, const void *W, const void *xq, int32_t 
 // flags (0 = no bounded wait gave up) or a negative status.
 int anvil_take_device_status(void) {
     int v = 0;
-    int parts[13] = {take_quantize_status(), mmvq_kernel_q4k_take_status(),
+    int parts[20] = {take_quantize_status(), mmvq_kernel_q4k_take_status(),
                     mmvq_kernel_q5k_take_status(), mmvq_kernel_q6k_take_status(),
                     mmvq_kernel_q80_take_status(), mmvq_kernel_q40_take_status(),
                     mmvq_kernel_q41_take_status(), mmvq_kernel_q50_take_status(),
                     mmvq_kernel_q51_take_status(), mmvq_kernel_q2k_take_status(),
                     mmvq_kernel_q3k_take_status(), mmvq_kernel_iq4nl_take_status(),
-                    mmvq_kernel_iq4xs_take_status()};
+                    mmvq_kernel_iq4xs_take_status(), mmvq_kernel_iq2xxs_take_status(),
+                    mmvq_kernel_iq2xs_take_status(), mmvq_kernel_iq2s_take_status(),
+                    mmvq_kernel_iq3xxs_take_status(), mmvq_kernel_iq3s_take_status(),
+                    mmvq_kernel_iq1s_take_status(), mmvq_kernel_iq1m_take_status()};
     for (int x : parts) {
         if (x < 0) return fail(ANVIL_ERR_CUDA, "reading device status failed");
         v |= x;

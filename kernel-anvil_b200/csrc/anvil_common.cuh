@@ -43,8 +43,15 @@ constexpr int kTypeQ3_K = 11;
 constexpr int kTypeQ4_K = 12;
 constexpr int kTypeQ5_K = 13;
 constexpr int kTypeQ6_K = 14;
+constexpr int kTypeIQ2_XXS = 16;
+constexpr int kTypeIQ2_XS = 17;
+constexpr int kTypeIQ3_XXS = 18;
+constexpr int kTypeIQ1_S = 19;
 constexpr int kTypeIQ4_NL = 20;
+constexpr int kTypeIQ3_S = 21;
+constexpr int kTypeIQ2_S = 22;
 constexpr int kTypeIQ4_XS = 23;
+constexpr int kTypeIQ1_M = 29;
 
 constexpr int kQK_K = 256;
 constexpr int kQK8_1 = 32;
@@ -86,6 +93,27 @@ template <> struct QTraits<kTypeIQ4_NL> {
 };
 template <> struct QTraits<kTypeIQ4_XS> {
     static constexpr int qk = 256, bytes = 136, units = 4, sub = 32;
+};
+template <> struct QTraits<kTypeIQ2_XXS> {
+    static constexpr int qk = 256, bytes = 66, units = 4, sub = 32;
+};
+template <> struct QTraits<kTypeIQ2_XS> {
+    static constexpr int qk = 256, bytes = 74, units = 4, sub = 16;
+};
+template <> struct QTraits<kTypeIQ2_S> {
+    static constexpr int qk = 256, bytes = 82, units = 4, sub = 16;
+};
+template <> struct QTraits<kTypeIQ3_XXS> {
+    static constexpr int qk = 256, bytes = 98, units = 4, sub = 32;
+};
+template <> struct QTraits<kTypeIQ3_S> {
+    static constexpr int qk = 256, bytes = 110, units = 4, sub = 32;
+};
+template <> struct QTraits<kTypeIQ1_S> {
+    static constexpr int qk = 256, bytes = 50, units = 4, sub = 32;
+};
+template <> struct QTraits<kTypeIQ1_M> {
+    static constexpr int qk = 256, bytes = 56, units = 4, sub = 16;
 };
 template <> struct QTraits<kTypeQ8_0> {
     static constexpr int qk = 32, bytes = 34, units = 1, sub = 32;

@@ -148,6 +148,13 @@ __host__ __device__ inline int mmvq_type_bytes(int qt) {
     case kTypeQ5_1: return 24;
     case kTypeIQ4_NL: return 18;
     case kTypeIQ4_XS: return 136;
+    case kTypeIQ2_XXS: return 66;
+    case kTypeIQ2_XS: return 74;
+    case kTypeIQ2_S: return 82;
+    case kTypeIQ3_XXS: return 98;
+    case kTypeIQ3_S: return 110;
+    case kTypeIQ1_S: return 50;
+    case kTypeIQ1_M: return 56;
     case kTypeQ2_K: return 84;
     case kTypeQ3_K: return 110;
     case kTypeQ4_K: return 144;
@@ -157,10 +164,10 @@ __host__ __device__ inline int mmvq_type_bytes(int qt) {
     }
 }
 __host__ __device__ inline int mmvq_type_qk(int qt) {
-    return qt == kTypeQ4_K || qt == kTypeQ5_K || qt == kTypeQ6_K || qt == kTypeQ2_K ||
-                   qt == kTypeQ3_K || qt == kTypeIQ4_XS
-               ? 256
-               : 32;
+    return qt == kTypeQ8_0 || qt == kTypeQ4_0 || qt == kTypeQ4_1 || qt == kTypeQ5_0 ||
+                   qt == kTypeQ5_1 || qt == kTypeIQ4_NL
+               ? 32
+               : 256;
 }
 
 // The 32-weight "basic" types (one Q8_1 block per weight block, one unit per block).
@@ -168,9 +175,15 @@ template <int QT>
 constexpr bool kBasic = QT == kTypeQ4_0 || QT == kTypeQ4_1 || QT == kTypeQ5_0 || QT == kTypeQ5_1;
 template <int QT>
 constexpr bool kBlock32 = QT == kTypeQ8_0 || kBasic<QT> || QT == kTypeIQ4_NL;
-// The K-quants with 16-weight scale groups (two per Q8_1 block).
+// The lattice I-quants (256-weight super-blocks of signed grid rows).
 template <int QT>
-constexpr bool kSub16 = QT == kTypeQ6_K || QT == kTypeQ2_K || QT == kTypeQ3_K;
+constexpr bool kIQLattice = QT == kTypeIQ2_XXS || QT == kTypeIQ2_XS || QT == kTypeIQ2_S ||
+                            QT == kTypeIQ3_XXS || QT == kTypeIQ3_S || QT == kTypeIQ1_S ||
+                            QT == kTypeIQ1_M;
+// The types with 16-weight scale groups (two per Q8_1 block): one block sum per group.
+template <int QT>
+constexpr bool kSub16 = QT == kTypeQ6_K || QT == kTypeQ2_K || QT == kTypeQ3_K ||
+                        QT == kTypeIQ2_XS || QT == kTypeIQ2_S || QT == kTypeIQ1_M;
 
 // Bytes of one column's swizzled activation quants: 2 chunks of 16 B per Q8_1 block,
 // padded to whole 16-chunk groups so the XOR swizzle never leaves the column.
@@ -306,7 +319,7 @@ __device__ __forceinline__ void load_act(const ActView &v, int kb, ActBlk &a) {
     a.slo = a.shi = 0;
     if constexpr (QT == kTypeQ4_K || QT == kTypeQ5_K || QT == kTypeQ4_1 || QT == kTypeQ5_1)
         a.ds = v.ads[kb];
-    if constexpr (kSub16<QT> || QT == kTypeQ4_0 || QT == kTypeQ5_0) {
+    if constexpr (kSub16<QT> || QT == kTypeQ4_0 || QT == kTypeQ5_0 || QT == kTypeIQ1_S) {
         const int2 s = v.as[kb];
         a.slo = s.x;
         a.shi = s.y;
@@ -408,6 +421,10 @@ __device__ __forceinline__ BlkHdr load_hdr(const uint8_t *blk) {
     } else if constexpr (QT == kTypeQ4_1 || QT == kTypeQ5_1) {
         h.d = h2f(lds16(blk));
         h.dmin = h2f(lds16(blk + 2));  // m, the block's added minimum
+    } else if constexpr (QT == kTypeIQ1_M) {
+        // bits 12-15 of scale word i (bytes 48 + 2i) are bits 4i..4i+3 of the fp16 d
+        h.d = h2f((lds16(blk + 48) >> 12) | ((lds16(blk + 50) >> 12) << 4) |
+                  ((lds16(blk + 52) >> 12) << 8) | ((lds16(blk + 54) >> 12) << 12));
     } else {
         h.d = h2f(lds16(blk));
     }
@@ -437,6 +454,130 @@ __device__ __forceinline__ void scale_min_pair(const BlkHdr &h, int &sc0, int &s
         m1 = (mp >> 8) & 0xFF;
     }
 }
+
+// ---- lattice I-quants ----------------------------------------------------------------
+// Grid rows are read through L1 from the generated tables (one word of 8 or 4 int8 values
+// per row, value 0 in the lowest byte).  Layouts, with sub-block j = weights 32j..32j+31
+// and group k = weights 8k..8k+7 (gguf-py gguf/quants.py IQ*.dequantize_blocks):
+//   IQ2_XXS  66 B: d @0; at 2+8j: 4 row bytes (256-row grid), then a u32 of four 7-bit sign
+//            indices (bits 7l) and the scale (bits 28-31)
+//   IQ2_XS   74 B: d @0; u16 per group @2+2k: row (bits 0-8, 512 rows), sign index (9-15);
+//            scale nibbles @66, one per 16 weights
+//   IQ2_S    82 B: d @0; row bits 0-7 @2+k, sign byte @34+k, row bits 8-9 at bit 2l of
+//            byte 66+j (1024 rows), scale nibbles @74
+//   IQ3_XXS  98 B: d @0; a row byte per 4 weights @2 (256 rows of 4); u32 @66+4j: sign
+//            indices and scale as IQ2_XXS
+//   IQ3_S   110 B: d @0; row bits 0-7 per 4 weights @2, bit 8 at bit r of byte 66+j (512
+//            rows of 4), sign byte @74+k, scale nibble j @106
+//   IQ1_S    50 B: d @0; row bits 0-7 @2+k; u16 @34+2j: row bits 8-10 of group 4j+l at
+//            bits 3l, scale bits 12-14, delta sign bit 15 (2048 rows of -1/0/1)
+//   IQ1_M    56 B: row bits 0-7 @k; nibble k @32 (low first): row bits 8-10, delta sign
+//            bit 3; u16 scale words @48: 3-bit scale of 16 weights 16(4i+t) at bits 3t of
+//            word i, d in the top nibbles (load_hdr)
+// A weight is d * F * M * L: L the signed grid value (IQ1: 8 grid +- 1 with the delta),
+// M = 2 scale + 1 (IQ3_S: 1 + 2 scale) for its 16- or 32-weight group, F = 1/8 (IQ2, IQ1),
+// 1/4 (IQ3_XXS) or 1 (IQ3_S).
+#define ANVIL_IQ_TABLE static __device__ const
+#include "iq_grids.h"
+#undef ANVIL_IQ_TABLE
+
+// The sign byte of 7-bit index i: bit 7 completes an even count of set bits (the rule of
+// the kIqSigns table, computed instead of loaded).
+__device__ __forceinline__ uint32_t iq_sign_byte(uint32_t i) {
+    return i | ((__popc(i) & 1u) << 7);
+}
+
+// Four positive int8 values with bits 0..3 of b negating values 0..3: b's bits spread to
+// 0x00 / 0xFF byte masks, then -v = (v ^ 0xFF) + 1 per byte (grid values are >= 1, so no
+// byte carries into the next).
+__device__ __forceinline__ uint32_t iq_signed4(uint32_t v, uint32_t b) {
+    const uint32_t m = (((b & 15u) * 0x00204081u) & 0x01010101u) * 0xFFu;
+    return (v ^ m) + (m & 0x01010101u);
+}
+
+// One 8-value grid row with its sign byte, as two words.
+__device__ __forceinline__ void iq_row8(uint64_t row, uint32_t sgn, uint32_t &lo, uint32_t &hi) {
+    lo = iq_signed4(uint32_t(row), sgn);
+    hi = iq_signed4(uint32_t(row >> 32), sgn >> 4);
+}
+
+__device__ __forceinline__ uint32_t lds32_2(const uint8_t *p) { return lds16(p) | (lds16(p + 2) << 16); }
+
+// The 32 signed levels of sub-block j as 8 words (word w = values 4w..4w+3).
+template <int QT>
+__device__ __forceinline__ void iq_sub(const uint8_t *blk, int j, uint32_t (&q)[8]) {
+    if constexpr (QT == kTypeIQ2_XXS) {
+        const uint32_t rows = lds32_2(blk + 2 + 8 * j), aux = lds32_2(blk + 6 + 8 * j);
+#pragma unroll
+        for (int l = 0; l < 4; ++l)
+            iq_row8(__ldg(&kIq2xxsGrid[(rows >> (8 * l)) & 0xFFu]),
+                    iq_sign_byte((aux >> (7 * l)) & 127u), q[2 * l], q[2 * l + 1]);
+    } else if constexpr (QT == kTypeIQ2_XS) {
+#pragma unroll
+        for (int l = 0; l < 4; ++l) {
+            const uint32_t e = lds16(blk + 2 + 8 * j + 2 * l);
+            iq_row8(__ldg(&kIq2xsGrid[e & 511u]), iq_sign_byte(e >> 9), q[2 * l], q[2 * l + 1]);
+        }
+    } else if constexpr (QT == kTypeIQ2_S) {
+        const uint32_t lo = lds32_2(blk + 2 + 4 * j), sg = lds32_2(blk + 34 + 4 * j);
+        const uint32_t hb = blk[66 + j];
+#pragma unroll
+        for (int l = 0; l < 4; ++l) {
+            const uint32_t r = ((lo >> (8 * l)) & 0xFFu) | (((hb >> (2 * l)) & 3u) << 8);
+            iq_row8(__ldg(&kIq2sGrid[r]), sg >> (8 * l), q[2 * l], q[2 * l + 1]);
+        }
+    } else if constexpr (QT == kTypeIQ3_XXS) {
+        const uint32_t r0 = lds32_2(blk + 2 + 8 * j), r1 = lds32_2(blk + 6 + 8 * j);
+        const uint32_t aux = lds32_2(blk + 66 + 4 * j);
+#pragma unroll
+        for (int l = 0; l < 4; ++l) {
+            const uint32_t rr = l < 2 ? r0 : r1;
+            const uint32_t sgn = iq_sign_byte((aux >> (7 * l)) & 127u);
+            q[2 * l] = iq_signed4(__ldg(&kIq3xxsGrid[(rr >> (16 * (l & 1))) & 0xFFu]), sgn);
+            q[2 * l + 1] = iq_signed4(__ldg(&kIq3xxsGrid[(rr >> (16 * (l & 1) + 8)) & 0xFFu]), sgn >> 4);
+        }
+    } else if constexpr (QT == kTypeIQ3_S) {
+        const uint32_t r0 = lds32_2(blk + 2 + 8 * j), r1 = lds32_2(blk + 6 + 8 * j);
+        const uint32_t hb = blk[66 + j], sg = lds32_2(blk + 74 + 4 * j);
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+            const uint32_t idx = (((r < 4 ? r0 : r1) >> (8 * (r & 3))) & 0xFFu) | (((hb >> r) & 1u) << 8);
+            q[r] = iq_signed4(__ldg(&kIq3sGrid[idx]), sg >> (4 * r));
+        }
+    } else if constexpr (QT == kTypeIQ1_S) {
+        const uint32_t lo = lds32_2(blk + 2 + 4 * j), qh = lds16(blk + 34 + 2 * j);
+#pragma unroll
+        for (int l = 0; l < 4; ++l) {
+            const uint64_t row = __ldg(&kIq1sGrid[((lo >> (8 * l)) & 0xFFu) | (((qh >> (3 * l)) & 7u) << 8)]);
+            q[2 * l] = uint32_t(row);
+            q[2 * l + 1] = uint32_t(row >> 32);
+        }
+    } else if constexpr (QT == kTypeIQ1_M) {
+        const uint32_t lo = lds32_2(blk + 4 * j), nb = lds16(blk + 32 + 2 * j);
+#pragma unroll
+        for (int l = 0; l < 4; ++l) {
+            const uint64_t row = __ldg(&kIq1sGrid[((lo >> (8 * l)) & 0xFFu) | (((nb >> (4 * l)) & 7u) << 8)]);
+            q[2 * l] = uint32_t(row);
+            q[2 * l + 1] = uint32_t(row >> 32);
+        }
+    }
+}
+
+// Scale multiplier M of scale group sg (a sub-block, or 16 weights for the kSub16 types).
+template <int QT>
+__device__ __forceinline__ int iq_mult(const uint8_t *blk, int sg) {
+    if constexpr (QT == kTypeIQ2_XXS) return 2 * int(blk[2 + 8 * sg + 7] >> 4) + 1;
+    if constexpr (QT == kTypeIQ2_XS) return 2 * int((blk[66 + (sg >> 1)] >> (4 * (sg & 1))) & 15) + 1;
+    if constexpr (QT == kTypeIQ2_S) return 2 * int((blk[74 + (sg >> 1)] >> (4 * (sg & 1))) & 15) + 1;
+    if constexpr (QT == kTypeIQ3_XXS) return 2 * int(blk[66 + 4 * sg + 3] >> 4) + 1;
+    if constexpr (QT == kTypeIQ3_S) return 1 + 2 * int((blk[106 + (sg >> 1)] >> (4 * (sg & 1))) & 15);
+    if constexpr (QT == kTypeIQ1_S) return 2 * int((lds16(blk + 34 + 2 * sg) >> 12) & 7) + 1;
+    if constexpr (QT == kTypeIQ1_M) return 2 * int((lds16(blk + 48 + 2 * (sg >> 2)) >> (3 * (sg & 3))) & 7) + 1;
+    return 0;
+}
+
+template <int QT>
+constexpr float kIQFactor = QT == kTypeIQ3_XXS ? 0.25f : QT == kTypeIQ3_S ? 1.0f : 0.125f;
 
 // Decoded weight bytes of one unit of one row (q0 pairs with Q8_1 block kb0, q1 with kb1).
 struct WBytes {
@@ -485,6 +626,9 @@ __device__ __forceinline__ void load_unit(const uint8_t *blk, WBytes &w) {
             iq4_levels8(v[k], w.q0[k], w.q0[4 + k]);
             iq4_levels8(v[4 + k], w.q1[k], w.q1[4 + k]);
         }
+    } else if constexpr (kIQLattice<QT>) {
+        iq_sub<QT>(blk, 2 * U, w.q0);
+        iq_sub<QT>(blk, 2 * U + 1, w.q1);
     } else if constexpr (QT == kTypeIQ4_NL) {
         uint32_t v[4];
         lds16B_a2(blk + 2, v);
@@ -610,6 +754,61 @@ __device__ __forceinline__ float dot_unit(const uint8_t *blk, const BlkHdr &h, c
         const int ls0 = int(((h.s1 >> (8 * U)) & 15u) | (((h.s0 >> (4 * U)) & 3u) << 4)) - 32;
         const int ls1 = int(((h.s1 >> (8 * U + 4)) & 15u) | (((h.s0 >> (4 * U + 2)) & 3u) << 4)) - 32;
         return h.d * (a0.d * float(i0 * ls0) + a1.d * float(i1 * ls1));
+    } else if constexpr (kIQLattice<QT> && !kSub16<QT>) {
+        // one scale per sub-block: d * F * sum_j d8_j * M_j * sum(L q8)
+        int i0 = 0, i1 = 0;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            i0 = __dp4a(int(w.q0[k]), int(a0.q[k]), i0);
+            i1 = __dp4a(int(w.q1[k]), int(a1.q[k]), i1);
+        }
+        if constexpr (QT == kTypeIQ1_S) {
+            // L = 8 grid +- 1: 8 sum(grid q8) plus or minus the block's sum of q8
+            const uint32_t h0 = lds16(blk + 34 + 4 * U), h1 = lds16(blk + 36 + 4 * U);
+            const int q0 = a0.slo + a0.shi, q1 = a1.slo + a1.shi;
+            i0 = 8 * i0 + ((h0 & 0x8000u) ? -q0 : q0);
+            i1 = 8 * i1 + ((h1 & 0x8000u) ? -q1 : q1);
+        }
+        isum[0] = i0;
+        isum[1] = i1;
+        const int m0 = iq_mult<QT>(blk, 2 * U), m1 = iq_mult<QT>(blk, 2 * U + 1);
+        return h.d * kIQFactor<QT> * (a0.d * float(i0 * m0) + a1.d * float(i1 * m1));
+    } else if constexpr (kIQLattice<QT>) {
+        // one scale per 16 weights (two per sub-block)
+        int p00 = 0, p01 = 0, p10 = 0, p11 = 0;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            p00 = __dp4a(int(w.q0[k]), int(a0.q[k]), p00);
+            p01 = __dp4a(int(w.q0[k + 4]), int(a0.q[k + 4]), p01);
+            p10 = __dp4a(int(w.q1[k]), int(a1.q[k]), p10);
+            p11 = __dp4a(int(w.q1[k + 4]), int(a1.q[k + 4]), p11);
+        }
+        if constexpr (QT == kTypeIQ1_M) {
+            // L = 8 grid +- 1 with a delta sign per 8 weights (bit 3 of the group's nibble):
+            // 8 sum(grid q8) plus or minus each group's sum of q8
+            const uint32_t nb = lds32_2(blk + 32 + 4 * U);  // nibbles of groups 8U..8U+7
+            int g8[8];
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+                g8[g] = __dp4a(0x01010101, int(a0.q[2 * g]), __dp4a(0x01010101, int(a0.q[2 * g + 1]), 0));
+                g8[4 + g] = __dp4a(0x01010101, int(a1.q[2 * g]), __dp4a(0x01010101, int(a1.q[2 * g + 1]), 0));
+            }
+#pragma unroll
+            for (int g = 0; g < 8; ++g)
+                if ((nb >> (4 * g + 3)) & 1u) g8[g] = -g8[g];
+            p00 = 8 * p00 + g8[0] + g8[1];
+            p01 = 8 * p01 + g8[2] + g8[3];
+            p10 = 8 * p10 + g8[4] + g8[5];
+            p11 = 8 * p11 + g8[6] + g8[7];
+        }
+        isum[0] = p00;
+        isum[1] = p01;
+        isum[2] = p10;
+        isum[3] = p11;
+        const int m00 = iq_mult<QT>(blk, 4 * U), m01 = iq_mult<QT>(blk, 4 * U + 1);
+        const int m10 = iq_mult<QT>(blk, 4 * U + 2), m11 = iq_mult<QT>(blk, 4 * U + 3);
+        return h.d * kIQFactor<QT> *
+               (a0.d * float(p00 * m00 + p01 * m01) + a1.d * float(p10 * m10 + p11 * m11));
     } else if constexpr (QT == kTypeIQ4_NL) {
         int i0 = 0;
 #pragma unroll
@@ -1144,6 +1343,13 @@ MmvqKernelFn mmvq_kernel_q2k(int ncols, int rpb, int lbt, int mode);
 MmvqKernelFn mmvq_kernel_q3k(int ncols, int rpb, int lbt, int mode);
 MmvqKernelFn mmvq_kernel_iq4nl(int ncols, int rpb, int lbt, int mode);
 MmvqKernelFn mmvq_kernel_iq4xs(int ncols, int rpb, int lbt, int mode);
+MmvqKernelFn mmvq_kernel_iq2xxs(int ncols, int rpb, int lbt, int mode);
+MmvqKernelFn mmvq_kernel_iq2xs(int ncols, int rpb, int lbt, int mode);
+MmvqKernelFn mmvq_kernel_iq2s(int ncols, int rpb, int lbt, int mode);
+MmvqKernelFn mmvq_kernel_iq3xxs(int ncols, int rpb, int lbt, int mode);
+MmvqKernelFn mmvq_kernel_iq3s(int ncols, int rpb, int lbt, int mode);
+MmvqKernelFn mmvq_kernel_iq1s(int ncols, int rpb, int lbt, int mode);
+MmvqKernelFn mmvq_kernel_iq1m(int ncols, int rpb, int lbt, int mode);
 // Reads and clears the device status word of that type's translation unit (current device).
 int mmvq_kernel_q4k_take_status();
 int mmvq_kernel_q5k_take_status();
@@ -1157,13 +1363,24 @@ int mmvq_kernel_q2k_take_status();
 int mmvq_kernel_q3k_take_status();
 int mmvq_kernel_iq4nl_take_status();
 int mmvq_kernel_iq4xs_take_status();
+int mmvq_kernel_iq2xxs_take_status();
+int mmvq_kernel_iq2xs_take_status();
+int mmvq_kernel_iq2s_take_status();
+int mmvq_kernel_iq3xxs_take_status();
+int mmvq_kernel_iq3s_take_status();
+int mmvq_kernel_iq1s_take_status();
+int mmvq_kernel_iq1m_take_status();
 
 }  // namespace anvil
 
 // Builds the [ncols 1..8] x [rpb 1,2,4,8] x [mode] x [lanes per row 16 / 32 / runtime]
 // table for one type (compile-time lanes per row for 1, 2, 4 and 8 columns).  lbt is 16 or
 // 32 for the compile-time variants, anything else for the runtime-LB kernel.
-#define ANVIL_MMVQ_TABLE(FN, QT)                                                          \
+// ANVIL_MMVQ_TABLE_RT builds the runtime-LB kernels only (same results, a third of the code:
+// the lattice I-quants, whose decode makes each instantiation large); it has no gate/up mode.
+#define ANVIL_MMVQ_TABLE(FN, QT) ANVIL_MMVQ_TABLE_IMPL(FN, QT, true)
+#define ANVIL_MMVQ_TABLE_RT(FN, QT) ANVIL_MMVQ_TABLE_IMPL(FN, QT, false)
+#define ANVIL_MMVQ_TABLE_IMPL(FN, QT, COMPILE_LB)                                         \
     namespace anvil {                                                                     \
     template <int NC, int R, int LBT>                                                     \
     static MmvqKernelFn FN##_glu() {                                                      \
@@ -1183,7 +1400,7 @@ int mmvq_kernel_iq4xs_take_status();
     }                                                                                     \
     template <int NC, int R>                                                              \
     static MmvqKernelFn FN##_lb(int lbt, int mode) {                                      \
-        if constexpr (NC == 1 || NC == 2 || NC == 4 || NC == 8) {                         \
+        if constexpr (COMPILE_LB && (NC == 1 || NC == 2 || NC == 4 || NC == 8)) {         \
             if (lbt == 16) return FN##_mode<NC, R, 16>(mode);                             \
             if (lbt == 32) return FN##_mode<NC, R, 32>(mode);                             \
         }                                                                                 \

@@ -35,7 +35,9 @@ GGML_TYPE_MAP = {
     "Q4_0": 2, "Q4_1": 3, "Q5_0": 6, "Q5_1": 7, "Q8_0": 8, "Q8_1": 9,
     "Q2_K": 10, "Q3_K": 11, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14, "Q8_K": 15,
     "IQ2_XXS": 16, "IQ2_XS": 17, "IQ3_XXS": 18, "IQ1_S": 19, "IQ4_NL": 20,
-    "IQ3_S": 21, "IQ2_S": 22, "IQ4_XS": 23, "IQ1_M": 24,
+    # IQ1_M is ggml type 29 (gguf-py GGMLQuantizationType); the reference's map says 24,
+    # ggml's I8, under which a tuned IQ1_M cell would never be looked up
+    "IQ3_S": 21, "IQ2_S": 22, "IQ4_XS": 23, "IQ1_M": 29,
     "BF16": 30,
     "MXFP4": 39, "NVFP4": 40,
 }

@@ -223,7 +223,8 @@ def block_sums(W: torch.Tensor, qt, xq: torch.Tensor, nrows: int | None = None, 
                ncols: int | None = None, nwarps: int = 0, rows_per_block: int = 0) -> torch.Tensor:
     """The production kernel's exact int32 block dots, shape (ncols, nrows, nsub).
 
-    nsub = K/16 for Q6_K (one per int8 scale group), K/32 otherwise (one per Q8_1 block).
+    nsub = K/16 for the types with 16-weight scale groups (Q6_K, Q2_K, Q3_K, IQ2_XS, IQ2_S,
+    IQ1_M), K/32 otherwise (one per Q8_1 block).
     """
     info = resolve_type(qt)
     _require_cuda("W", W, torch.uint8)
@@ -231,7 +232,7 @@ def block_sums(W: torch.Tensor, qt, xq: torch.Tensor, nrows: int | None = None, 
     nrows, K = _shape_args(W, info, nrows, K)
     if ncols is None:
         ncols = xq.numel() // q8_1_bytes(K)
-    nsub = K // 16 if info.name in ("Q6_K", "Q2_K", "Q3_K") else K // 32
+    nsub = K // 16 if info.name in ("Q6_K", "Q2_K", "Q3_K", "IQ2_XS", "IQ2_S", "IQ1_M") else K // 32
     out = torch.empty((ncols, nrows, nsub), dtype=torch.int32, device=W.device)
     check(_native.lib().anvil_mmvq_block_sums(info.ggml_type, W.data_ptr(), xq.data_ptr(),
                                               out.data_ptr(), nrows, K, ncols, nwarps,

@@ -61,9 +61,29 @@ QUANT_TYPES: dict[str, QuantTypeInfo] = {
     "Q4_K": QuantTypeInfo("Q4_K", 12, 256, 32, 2, 144),
     "Q5_K": QuantTypeInfo("Q5_K", 13, 256, 32, 2, 176),
     "Q6_K": QuantTypeInfo("Q6_K", 14, 256, 32, 1, 210),
+    "IQ2_XXS": QuantTypeInfo("IQ2_XXS", 16, 256, 16, 2, 66),
+    "IQ2_XS": QuantTypeInfo("IQ2_XS", 17, 256, 16, 2, 74),
+    "IQ2_S": QuantTypeInfo("IQ2_S", 22, 256, 16, 2, 82),
+    "IQ3_XXS": QuantTypeInfo("IQ3_XXS", 18, 256, 16, 2, 98),
+    "IQ3_S": QuantTypeInfo("IQ3_S", 21, 256, 16, 2, 110),
+    "IQ1_S": QuantTypeInfo("IQ1_S", 19, 256, 8, 1, 50),
+    # ggml's id of IQ1_M is 29 (gguf-py GGMLQuantizationType.IQ1_M); the reference's table
+    # says 24, which ggml assigns to I8
+    "IQ1_M": QuantTypeInfo("IQ1_M", 29, 256, 8, 1, 56),
     "IQ4_NL": QuantTypeInfo("IQ4_NL", 20, 32, 4, 2, 18),
     "IQ4_XS": QuantTypeInfo("IQ4_XS", 23, 256, 32, 4, 136),
 }
+# The I-quants whose fp16 d sits in bytes 0-1 (IQ1_M spreads it over its scale words).
+_IQ_D_AT_0 = ("IQ2_XXS", "IQ2_XS", "IQ2_S", "IQ3_XXS", "IQ3_S", "IQ1_S")
+
+
+def _iq1m_set_d(blocks: np.ndarray, d_bits: np.ndarray) -> None:
+    """IQ1_M: fp16 d bits -> the top nibbles of the four scale words at bytes 48..55
+    (bits 12-15 of word i hold bits 4i..4i+3 of d); the 3-bit scales below are kept."""
+    sc = blocks[:, 48:56].copy().view(np.uint16).reshape(-1, 4)
+    for i in range(4):
+        sc[:, i] = (sc[:, i] & np.uint16(0x0FFF)) | (((d_bits >> np.uint16(4 * i)) & np.uint16(15)) << np.uint16(12))
+    blocks[:, 48:56] = sc.view(np.uint8).reshape(-1, 8)
 TYPE_BY_ID = {q.ggml_type: q for q in QUANT_TYPES.values()}
 
 
@@ -141,6 +161,14 @@ def make_weights(qt, nrows: int, K: int, seed: int = 0) -> np.ndarray:
         if info.name.endswith("_1"):
             m = (-np.abs(rng.standard_normal(nb)) * 1e-1).astype(np.float16)
             blocks[:, 2:4] = m.view(np.uint8).reshape(nb, 2)
+    elif info.name in _IQ_D_AT_0 or info.name == "IQ1_M":
+        # lattice indices, sign bits, scales and delta bits uniform; d from |N(0,1)| * 1e-3
+        blocks[:] = rng.integers(0, 256, size=(nb, info.block_size), dtype=np.uint8)
+        d = _fp16_abs_normal(rng, nb, 1e-3)
+        if info.name == "IQ1_M":
+            _iq1m_set_d(blocks, d.copy().view(np.uint16).reshape(nb))
+        else:
+            blocks[:, 0:2] = d
     else:  # pragma: no cover - resolve_type rejects other types
         raise ValueError(info.name)
     return blocks.reshape(nrows, row_bytes)
@@ -195,6 +223,15 @@ def make_weights_device(qt, nrows: int, K: int, seed: int = 0, device="cuda"):
         blocks[:, 108:110] = fp16_abs_normal(1e-2)
     elif info.name in ("IQ4_NL", "IQ4_XS"):
         blocks[:, 0:2] = fp16_abs_normal(1e-3)
+    elif info.name in _IQ_D_AT_0:
+        blocks[:, 0:2] = fp16_abs_normal(1e-3)
+    elif info.name == "IQ1_M":
+        d = torch.randn(nb, device=device, generator=g).abs_().mul_(1e-3).to(torch.float16)
+        dbits = d.view(torch.int16).to(torch.int32) & 0xFFFF
+        sc = blocks[:, 48:56].contiguous().view(torch.int16).to(torch.int32) & 0xFFFF
+        for i in range(4):
+            sc[:, i] = (sc[:, i] & 0x0FFF) | (((dbits >> (4 * i)) & 15) << 12)
+        blocks[:, 48:56] = sc.to(torch.int16).view(torch.uint8).view(nb, 8)
     elif info.name in ("Q4_0", "Q4_1", "Q5_0", "Q5_1"):
         blocks[:, 0:2] = fp16_abs_normal(1e-2)
         if info.name.endswith("_1"):

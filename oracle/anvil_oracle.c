@@ -9,6 +9,11 @@
  *     dependency, kernel-anvil pyproject.toml:19, gguf 0.19.0) gguf/quants.py Q4_0..Q5_1,
  *     Q2_K, Q3_K, IQ4_NL and IQ4_XS dequantize_blocks, 378-401 (Q8_0), 474-523 (Q4_K incl. get_scale_min), 525-549
  *     (Q5_K), 552-572 (Q6_K).
+ *     The seven lattice I-quants IQ2_XXS, IQ2_XS, IQ2_S, IQ3_XXS, IQ3_S, IQ1_S and IQ1_M
+ *     (the reference's QUANT_TYPES, kernel_anvil/hip_codegen.py:89-96): gguf-py
+ *     gguf/quants.py <type>.dequantize_blocks with the grids of <type>.grid_hex /
+ *     grid_map and IQ2_XXS.ksigns, here as the generated table header
+ *     kernel-anvil_b200/csrc/iq_grids.h.
  *     Pinned in tests against gguf.quants.dequantize (fixtures and live).
  *   - Q8_1 activation quantisation: llama.cpp's CUDA quantize_q8_1 semantics (the
  *     reference's runtime path: kernel_anvil/hip_codegen.py:392-396 layout, 101-102 size;
@@ -41,7 +46,11 @@
 #endif
 
 enum { T_Q4_0 = 2, T_Q4_1 = 3, T_Q5_0 = 6, T_Q5_1 = 7, T_Q8_0 = 8, T_Q2_K = 10, T_Q3_K = 11,
-       T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14, T_IQ4_NL = 20, T_IQ4_XS = 23 };
+       T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14, T_IQ2_XXS = 16, T_IQ2_XS = 17, T_IQ3_XXS = 18,
+       T_IQ1_S = 19, T_IQ4_NL = 20, T_IQ3_S = 21, T_IQ2_S = 22, T_IQ4_XS = 23, T_IQ1_M = 29 };
+
+#define ANVIL_IQ_TABLE static const
+#include "iq_grids.h"
 
 /* The 16 levels of IQ4_NL / IQ4_XS (gguf-py quants.py IQ4_NL.kvalues). */
 static const int iq4_levels[16] = {-127, -104, -83, -65, -49, -35, -22, -10,
@@ -258,6 +267,13 @@ static inline int q3k_scale(const uint8_t *blk, int j) {
 
 static int type_bytes(int t) {
     switch (t) {
+    case T_IQ2_XXS: return 66;
+    case T_IQ2_XS: return 74;
+    case T_IQ2_S: return 82;
+    case T_IQ3_XXS: return 98;
+    case T_IQ3_S: return 110;
+    case T_IQ1_S: return 50;
+    case T_IQ1_M: return 56;
     case T_IQ4_NL: return 18;
     case T_IQ4_XS: return 136;
     case T_Q2_K: return 84;
@@ -295,6 +311,129 @@ static inline int basic_quant(int t, const uint8_t *blk, int e) {
     return q;
 }
 
+/* ---- lattice I-quants ---------------------------------------------------------------
+ * Block layouts (256 weights; sub-block j = weights 32j..32j+31, group k = weights 8k..8k+7):
+ *   IQ2_XXS  66 B: d @0; per j at 2+8j: 4 grid bytes (one 8-value row of the 256-row grid per
+ *            group), then a u32 whose bits 7l..7l+6 index the sign byte of group 4j+l and
+ *            whose bits 28-31 are the scale ls.              w = d (0.5 + ls) / 4 * grid * sign
+ *   IQ2_XS   74 B: d @0; u16 qs[32] @2 (bits 0-8 a row of the 512-row grid, 9-15 a sign
+ *            index, one per group); scales[8] @66, a nibble per 16 weights (low first).
+ *   IQ2_S    82 B: d @0; qs[32] @2 (row index bits 0-7), signs[32] @34 (one byte per group),
+ *            qh[8] @66 (2 bits per group: index bits 8-9 of group 4j+l at bit 2l of qh[j]),
+ *            scales[8] @74 as IQ2_XS; grid of 1024 rows.
+ *   IQ3_XXS  98 B: d @0; qs[64] @2 (one 4-value row of the 256-row grid per 4 weights);
+ *            u32 @66+4j: sign indices and scale as IQ2_XXS.  w = d (0.5 + ls) / 2 * grid * sign
+ *   IQ3_S   110 B: d @0; qs[64] @2 (row index bits 0-7), qh[8] @66 (bit 8 of row 8j+b at bit
+ *            b of qh[j]), signs[32] @74, scales[4] @106 (a nibble per sub-block).
+ *                                                            w = d (1 + 2 ls) * grid * sign
+ *   IQ1_S    50 B: d @0; qs[32] @2 (row index bits 0-7 per group); u16 qh[8] @34: bits
+ *            3l..3l+2 index bits 8-10 of group 4j+l, bits 12-14 the scale s, bit 15 the sign
+ *            of the delta.                   w = d (2 s + 1) * (grid + (bit 15 ? -1 : 1) / 8)
+ *   IQ1_M    56 B: qs[32] @0; qh[16] @32 (a nibble per group, low first: bits 0-2 index bits
+ *            8-10, bit 3 the delta sign); u16 scales[4] @48: 3-bit scales at bits 3t of word
+ *            i for the 16 weights 16(4i + t).., and bits 12-15 of word i are bits 4i..4i+3
+ *            of the fp16 d.                                   w = d (2 s + 1) * (grid + delta)
+ * The IQ1 grid holds -1, 0, 1.  For the integer arithmetic every weight is
+ * d * F * M_g * L_w: the level L_w (the signed grid value, or 8 * grid +- 1 for IQ1), the
+ * scale multiplier M_g of its 16- or 32-weight group and the type's factor F (1/8 for IQ2
+ * and IQ1, 1/4 for IQ3_XXS, 1 for IQ3_S). */
+static int is_iq(int t) {
+    return t == T_IQ2_XXS || t == T_IQ2_XS || t == T_IQ2_S || t == T_IQ3_XXS || t == T_IQ3_S ||
+           t == T_IQ1_S || t == T_IQ1_M;
+}
+static int iq_group16(int t) { return t == T_IQ2_XS || t == T_IQ2_S || t == T_IQ1_M; }
+static double iq_factor(int t) { return t == T_IQ3_XXS ? 0.25 : t == T_IQ3_S ? 1.0 : 0.125; }
+static inline uint32_t rd32(const uint8_t *p) {
+    return (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
+}
+static inline int row8(uint64_t row, int i) { return (int)(int8_t)(uint8_t)(row >> (8 * i)); }
+static inline int row4(uint32_t row, int i) { return (int)(int8_t)(uint8_t)(row >> (8 * i)); }
+static inline uint16_t iq1m_d_bits(const uint8_t *blk) {
+    uint16_t d = 0;
+    for (int i = 0; i < 4; ++i) d |= (uint16_t)((rd16(blk + 48 + 2 * i) >> 12) << (4 * i));
+    return d;
+}
+static float iq_d(int t, const uint8_t *blk) {
+    return oracle_half_to_float(t == T_IQ1_M ? iq1m_d_bits(blk) : rd16(blk));
+}
+/* Grid value of weight w (before its sign; IQ1: -1, 0 or 1). */
+static int iq_grid(int t, const uint8_t *blk, int w) {
+    const int j = w >> 5, l = (w >> 3) & 3, k = w >> 3, i = w & 7;
+    switch (t) {
+    case T_IQ2_XXS: return row8(kIq2xxsGrid[blk[2 + 8 * j + l]], i);
+    case T_IQ2_XS: return row8(kIq2xsGrid[rd16(blk + 2 + 2 * k) & 511], i);
+    case T_IQ2_S: return row8(kIq2sGrid[blk[2 + k] | (((blk[66 + j] >> (2 * l)) & 3) << 8)], i);
+    case T_IQ3_XXS: return row4(kIq3xxsGrid[blk[2 + (w >> 2)]], w & 3);
+    case T_IQ3_S: {
+        const int r = w >> 2;
+        return row4(kIq3sGrid[blk[2 + r] | (((blk[66 + j] >> (r & 7)) & 1) << 8)], w & 3);
+    }
+    case T_IQ1_S: return row8(kIq1sGrid[blk[2 + k] | (((rd16(blk + 34 + 2 * j) >> (3 * l)) & 7) << 8)], i);
+    case T_IQ1_M: {
+        const int nib = (blk[32 + (k >> 1)] >> (4 * (k & 1))) & 15;
+        return row8(kIq1sGrid[blk[k] | ((nib & 7) << 8)], i);
+    }
+    default: return 0;
+    }
+}
+/* 1 when weight w is negated (IQ2 / IQ3 sign bits); for IQ1 when its delta is -1/8. */
+static int iq_neg(int t, const uint8_t *blk, int w) {
+    const int j = w >> 5, l = (w >> 3) & 3, k = w >> 3, i = w & 7;
+    switch (t) {
+    case T_IQ2_XXS: return (kIqSigns[(rd32(blk + 2 + 8 * j + 4) >> (7 * l)) & 127] >> i) & 1;
+    case T_IQ2_XS: return (kIqSigns[rd16(blk + 2 + 2 * k) >> 9] >> i) & 1;
+    case T_IQ2_S: return (blk[34 + k] >> i) & 1;
+    case T_IQ3_XXS: return (kIqSigns[(rd32(blk + 66 + 4 * j) >> (7 * l)) & 127] >> i) & 1;
+    case T_IQ3_S: return (blk[74 + k] >> i) & 1;
+    case T_IQ1_S: return rd16(blk + 34 + 2 * j) >> 15;
+    case T_IQ1_M: return (blk[32 + (k >> 1)] >> (4 * (k & 1) + 3)) & 1;
+    default: return 0;
+    }
+}
+/* The integer level L_w. */
+static int iq_level(int t, const uint8_t *blk, int w) {
+    const int g = iq_grid(t, blk, w), neg = iq_neg(t, blk, w);
+    if (t == T_IQ1_S || t == T_IQ1_M) return 8 * g + (neg ? -1 : 1);
+    return neg ? -g : g;
+}
+/* The raw scale field of scale group sg (a 32-weight sub-block, or 16 weights for the
+ * iq_group16 types) and its integer multiplier M. */
+static int iq_scale(int t, const uint8_t *blk, int sg) {
+    switch (t) {
+    case T_IQ2_XXS: return blk[2 + 8 * sg + 7] >> 4;
+    case T_IQ2_XS: return (blk[66 + (sg >> 1)] >> (4 * (sg & 1))) & 15;
+    case T_IQ2_S: return (blk[74 + (sg >> 1)] >> (4 * (sg & 1))) & 15;
+    case T_IQ3_XXS: return blk[66 + 4 * sg + 3] >> 4;
+    case T_IQ3_S: return (blk[106 + (sg >> 1)] >> (4 * (sg & 1))) & 15;
+    case T_IQ1_S: return (rd16(blk + 34 + 2 * sg) >> 12) & 7;
+    case T_IQ1_M: return (rd16(blk + 48 + 2 * (sg >> 2)) >> (3 * (sg & 3))) & 7;
+    default: return 0;
+    }
+}
+static int iq_mult(int t, const uint8_t *blk, int sg) { return 2 * iq_scale(t, blk, sg) + 1; }
+
+/* gguf-py's float32 order per type: IQ2 db = d * (0.5 + ls) * 0.25, IQ3_XXS d * (0.5 + ls)
+ * * 0.5, then db * grid * sign; IQ3_S d * (1 + 2 ls) * grid * sign; IQ1 d * (2 s + 1) *
+ * (grid + delta). */
+static void iq_dequant_block(int t, const uint8_t *blk, float *o) {
+    const float d = iq_d(t, blk);
+    for (int w = 0; w < 256; ++w) {
+        const int sg = iq_group16(t) ? w >> 4 : w >> 5;
+        const int g = iq_grid(t, blk, w), neg = iq_neg(t, blk, w);
+        const int ls = iq_scale(t, blk, sg);
+        if (t == T_IQ1_S || t == T_IQ1_M) {
+            const float dl = d * (float)(2 * ls + 1);
+            o[w] = dl * ((float)g + (neg ? -0.125f : 0.125f));
+        } else if (t == T_IQ3_S) {
+            const float db = d * (float)(1 + 2 * ls);
+            o[w] = neg ? -(db * (float)g) : db * (float)g;
+        } else {
+            const float db = d * (0.5f + (float)ls) * (t == T_IQ3_XXS ? 0.5f : 0.25f);
+            o[w] = neg ? -(db * (float)g) : db * (float)g;
+        }
+    }
+}
+
 /* ---- dequantisation (gguf-py float32 operation order) -------------------------- */
 
 int oracle_dequant(int type, const uint8_t *W, float *out, int64_t nrows, int64_t K) {
@@ -316,6 +455,8 @@ int oracle_dequant(int type, const uint8_t *W, float *out, int64_t nrows, int64_
             } else {
                 for (int e = 0; e < 32; ++e) o[e] = d * (float)basic_quant(type, blk, e);
             }
+        } else if (is_iq(type)) {
+            iq_dequant_block(type, blk, o);
         } else if (type == T_IQ4_NL) {
             const float d = oracle_half_to_float(rd16(blk));
             for (int e = 0; e < 32; ++e) o[e] = d * (float)iq4nl_level(blk + 2, e);
@@ -374,7 +515,8 @@ int oracle_block_sums(int type, const uint8_t *W, const uint8_t *xq, int32_t *su
     const int bytes = type_bytes(type), qk = type_qk(type);
     if (!bytes || K % qk) return -1;
     const int64_t nblk = K / qk, nkb = K / 32;
-    const int64_t nsub = (type == T_Q6_K || type == T_Q2_K || type == T_Q3_K) ? K / 16 : K / 32;
+    const int64_t nsub = (type == T_Q6_K || type == T_Q2_K || type == T_Q3_K || iq_group16(type))
+                             ? K / 16 : K / 32;
 #pragma omp parallel for collapse(2) schedule(static)
     for (int64_t c = 0; c < ncols; ++c)
         for (int64_t r = 0; r < nrows; ++r) {
@@ -395,6 +537,19 @@ int oracle_block_sums(int type, const uint8_t *W, const uint8_t *xq, int32_t *su
                     int32_t s = 0;
                     for (int e = 0; e < 32; ++e) s += basic_quant(type, blk, e) * a[e];
                     out[b] = s;
+                    continue;
+                }
+                if (is_iq(type)) {
+                    /* sum of L_w * q8 per scale group */
+                    const int gs = iq_group16(type) ? 16 : 32, ng = 256 / gs;
+                    for (int g = 0; g < ng; ++g) {
+                        int32_t s = 0;
+                        for (int e = 0; e < gs; ++e) {
+                            const int w = gs * g + e;
+                            s += iq_level(type, blk, w) * (int8_t)xc[(8 * b + (w >> 5)) * 36 + 4 + (w & 31)];
+                        }
+                        out[ng * b + g] = s;
+                    }
                     continue;
                 }
                 if (type == T_IQ4_NL) {
@@ -490,6 +645,22 @@ static int mmvq_impl(int type, const uint8_t *W, const uint8_t *xq, double *y, i
                     acc += (double)oracle_half_to_float(rd16(blk)) * d8 * (double)s;
                     if (type == T_Q4_1 || type == T_Q5_1)
                         acc += (double)oracle_half_to_float(rd16(blk + 2)) * d8 * (double)sq;
+                    continue;
+                }
+                if (is_iq(type)) {
+                    /* d * F * sum_g d8 * M_g * sum(L_w q8) */
+                    const int gs = iq_group16(type) ? 16 : 32, ng = 256 / gs;
+                    double sb = 0.0;
+                    for (int g = 0; g < ng; ++g) {
+                        const uint8_t *ab = xc + (8 * b + (gs * g >> 5)) * 36;
+                        int32_t s = 0;
+                        for (int e = 0; e < gs; ++e) {
+                            const int w = gs * g + e;
+                            s += iq_level(type, blk, w) * (int8_t)ab[4 + (w & 31)];
+                        }
+                        sb += act_d8(ab, d32) * (double)iq_mult(type, blk, g) * (double)s;
+                    }
+                    acc += (double)iq_d(type, blk) * iq_factor(type) * sb;
                     continue;
                 }
                 if (type == T_IQ4_NL) {

@@ -18,7 +18,10 @@ LIB = HERE / "_build" / "liboracle.so"
 REF_SMITHY = HERE / "_ref" / "libsmithy_ref.so"
 
 TYPE_IDS = {"Q4_0": 2, "Q4_1": 3, "Q5_0": 6, "Q5_1": 7, "Q8_0": 8, "Q2_K": 10, "Q3_K": 11, "Q4_K": 12,
-            "Q5_K": 13, "Q6_K": 14, "IQ4_NL": 20, "IQ4_XS": 23}
+            "Q5_K": 13, "Q6_K": 14, "IQ2_XXS": 16, "IQ2_XS": 17, "IQ3_XXS": 18, "IQ1_S": 19,
+            "IQ4_NL": 20, "IQ3_S": 21, "IQ2_S": 22, "IQ4_XS": 23, "IQ1_M": 29}
+# types with one block sum per 16 weights (their scale groups); the others one per 32
+SUB16_IDS = (10, 11, 14, 17, 22, 29)
 
 _lib = None
 
@@ -119,7 +122,7 @@ def dequantize_q8_1(xq: np.ndarray, K: int) -> np.ndarray:
 
 
 def block_sums(qt, W: np.ndarray, xq: np.ndarray, nrows: int, K: int, ncols: int = 1) -> np.ndarray:
-    nsub = K // 16 if _tid(qt) in (10, 11, 14) else K // 32
+    nsub = K // 16 if _tid(qt) in SUB16_IDS else K // 32
     out = np.empty((ncols, nrows, nsub), dtype=np.int32)
     W = np.ascontiguousarray(W, dtype=np.uint8)
     xq = np.ascontiguousarray(xq, dtype=np.uint8)

@@ -2,7 +2,7 @@
 
 Run in the build container (where the reference tree and gguf-py are present):
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py [--reference /root/reference] [--types IQ2_XXS ...]
 
 Writes:
   dequant_<type>.npz   seeded GGUF-layout blocks and gguf-py ``gguf.quants.dequantize``
@@ -39,7 +39,9 @@ from kernel_anvil.quants import make_activation, make_weights  # noqa: E402
 
 DEQUANT_CASES = {"Q4_K": (8, 512), "Q5_K": (8, 512), "Q6_K": (8, 512), "Q8_0": (8, 256),
                  "Q4_0": (8, 256), "Q4_1": (8, 256), "Q5_0": (8, 256), "Q5_1": (8, 256),
-                 "Q2_K": (8, 512), "Q3_K": (8, 512), "IQ4_NL": (8, 256), "IQ4_XS": (8, 512)}
+                 "Q2_K": (8, 512), "Q3_K": (8, 512), "IQ4_NL": (8, 256), "IQ4_XS": (8, 512),
+                 "IQ2_XXS": (8, 512), "IQ2_XS": (8, 512), "IQ2_S": (8, 512), "IQ3_XXS": (8, 512),
+                 "IQ3_S": (8, 512), "IQ1_S": (8, 512), "IQ1_M": (8, 512)}
 
 # Inputs for the reference's codegen.  Keys are (quant, n, k) -> {nwarps, rows_per_block}.
 CODEGEN_CASES = [
@@ -99,14 +101,18 @@ SMITHY_DOCS = {
 }
 
 
-def write_dequant(out: Path) -> None:
+def write_dequant(out: Path, types=None) -> None:
     import gguf
 
     for qt, (n, k) in DEQUANT_CASES.items():
+        if types and qt not in types:
+            continue
         W = make_weights(qt, n, k, seed=11)
         deq = gguf.quants.dequantize(W, getattr(gguf.GGMLQuantizationType, qt))
         np.savez_compressed(out / f"dequant_{qt}.npz", W=W, dequant=deq.astype(np.float32),
                             nrows=n, K=k)
+    if types:
+        return
     x = make_activation(1024, ncols=2, seed=5)
     x[1, :32] = 0.0  # an all-zero block
     q8 = gguf.quants.quantize(x, gguf.GGMLQuantizationType.Q8_0)
@@ -180,8 +186,13 @@ def write_smithy(out: Path, codegen_res: dict) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--types", nargs="*", default=None,
+                    help="only the dequant fixtures of these types (nothing else is rewritten)")
     args = ap.parse_args()
-    write_dequant(HERE)
+    write_dequant(HERE, args.types)
+    if args.types:
+        print(f"dequant fixtures of {' '.join(args.types)} written to {HERE}")
+        return
     res = write_codegen(HERE, Path(args.reference))
     write_smithy(HERE, res)
     print(f"fixtures written to {HERE}")

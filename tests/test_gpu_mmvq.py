@@ -21,7 +21,7 @@ from oracle import oracle  # noqa: E402
 pytestmark = pytest.mark.gpu
 
 TYPES = ["Q4_K", "Q5_K", "Q6_K", "Q8_0", "Q4_0", "Q4_1", "Q5_0", "Q5_1", "Q2_K", "Q3_K", "IQ4_NL",
-         "IQ4_XS"]
+         "IQ4_XS", "IQ2_XXS", "IQ2_XS", "IQ2_S", "IQ3_XXS", "IQ3_S", "IQ1_S", "IQ1_M"]
 Y_TOL = 1e-3
 
 
@@ -93,6 +93,11 @@ def test_batched_columns(qt, ncols):
     ("Q5_0", 3, 32), ("Q5_0", 11, 160), ("Q5_0", 1024, 14336),  # 22- / 110-byte rows
     ("Q5_1", 9, 224), ("Q5_1", 1024, 4096),
     ("Q8_0", 7, 1056), ("Q8_0", 3072, 1024), ("Q8_0", 1024, 3072),
+    # lattice I-quants: one-block rows of 50..110 bytes (no 16-byte multiple), long rows
+    ("IQ2_XXS", 3, 256), ("IQ2_XXS", 4096, 4096), ("IQ2_XS", 5, 768), ("IQ2_XS", 1024, 4096),
+    ("IQ2_S", 7, 256), ("IQ2_S", 2048, 4096), ("IQ3_XXS", 9, 512), ("IQ3_XXS", 4096, 4096),
+    ("IQ3_S", 1, 256), ("IQ3_S", 1024, 12288), ("IQ1_S", 11, 256), ("IQ1_S", 4096, 4096),
+    ("IQ1_M", 3, 1280), ("IQ1_M", 2048, 8192),
 ])
 def test_shapes(qt, nrows, K):
     check_case(qt, nrows, K, 1, 0, 0, seed=nrows)

@@ -40,11 +40,14 @@ def test_cpu_safe_entry_points():
     qk, nb = ctypes.c_int(), ctypes.c_int()
     expect = {2: (32, 18), 3: (32, 20), 6: (32, 22), 7: (32, 24), 8: (32, 34), 9: (32, 36),
               10: (256, 84), 11: (256, 110), 12: (256, 144), 13: (256, 176), 14: (256, 210),
-              20: (32, 18), 23: (256, 136)}
+              20: (32, 18), 23: (256, 136), 16: (256, 66), 17: (256, 74), 22: (256, 82),
+              18: (256, 98), 21: (256, 110), 19: (256, 50), 29: (256, 56)}
     for t, (q, b) in expect.items():
         assert lib.anvil_type_geometry(t, ctypes.byref(qk), ctypes.byref(nb)) == 0
         assert (qk.value, nb.value) == (q, b)
-    assert lib.anvil_type_geometry(16, ctypes.byref(qk), ctypes.byref(nb)) == _native.ANVIL_ERR_UNSUPPORTED
+    # Q8_K (15) and I8 (24) have no MMVQ block geometry here
+    for t in (15, 24):
+        assert lib.anvil_type_geometry(t, ctypes.byref(qk), ctypes.byref(nb)) == _native.ANVIL_ERR_UNSUPPORTED
     assert "no block geometry" in _native.last_error()
     assert lib.anvil_row_bytes(12, 4096) == 16 * 144
     assert lib.anvil_row_bytes(14, 12288) == 48 * 210

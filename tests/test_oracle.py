@@ -14,7 +14,7 @@ from kernel_anvil.quants import QUANT_TYPES, make_activation, make_weights
 from oracle import oracle
 
 TYPES = ["Q4_K", "Q5_K", "Q6_K", "Q8_0", "Q4_0", "Q4_1", "Q5_0", "Q5_1", "Q2_K", "Q3_K", "IQ4_NL",
-         "IQ4_XS"]
+         "IQ4_XS", "IQ2_XXS", "IQ2_XS", "IQ2_S", "IQ3_XXS", "IQ3_S", "IQ1_S", "IQ1_M"]
 
 
 @pytest.mark.parametrize("qt", TYPES)
@@ -124,6 +124,33 @@ def test_block_sums_reconstruct_y(qt):
             elif qt == "IQ4_NL":
                 d = blk[0:2].copy().view(np.float16).astype(np.float64)[0]
                 y[r] += d * d8[b] * sums[r, b]
+            elif qt.startswith(("IQ1", "IQ2", "IQ3")):
+                # w = d * F * (2 ls + 1 | 1 + 2 ls) * level per scale group of 16 or 32
+                # (gguf-py IQ*.dequantize_blocks scale rules); IQ1_M's d is in the scale words
+                if qt == "IQ1_M":
+                    sw = blk[48:56].copy().view(np.uint16).astype(np.int64)
+                    bits = sum(((int(sw[i]) >> 12) & 15) << (4 * i) for i in range(4))
+                    d = float(np.array([bits], dtype=np.uint16).view(np.float16)[0])
+                else:
+                    d = float(blk[0:2].copy().view(np.float16)[0])
+                g16 = qt in ("IQ2_XS", "IQ2_S", "IQ1_M")
+                F = {"IQ3_XXS": 0.25, "IQ3_S": 1.0}.get(qt, 0.125)
+                for g in range(16 if g16 else 8):
+                    if qt == "IQ2_XXS":
+                        ls = int(blk[2 + 8 * g + 7]) >> 4
+                    elif qt in ("IQ2_XS", "IQ2_S"):
+                        ls = (int(blk[(66 if qt == "IQ2_XS" else 74) + g // 2]) >> (4 * (g % 2))) & 15
+                    elif qt == "IQ3_XXS":
+                        ls = int(blk[66 + 4 * g + 3]) >> 4
+                    elif qt == "IQ3_S":
+                        ls = (int(blk[106 + g // 2]) >> (4 * (g % 2))) & 15
+                    elif qt == "IQ1_S":
+                        ls = (int(blk[34 + 2 * g]) | (int(blk[35 + 2 * g]) << 8)) >> 12 & 7
+                    else:
+                        ls = ((int(blk[48 + 2 * (g // 4)]) | (int(blk[49 + 2 * (g // 4)]) << 8))
+                              >> (3 * (g % 4))) & 7
+                    kb = 8 * b + (g // 2 if g16 else g)
+                    y[r] += d * F * (2 * ls + 1) * d8[kb] * sums[r, (16 if g16 else 8) * b + g]
             elif qt == "IQ4_XS":
                 d = blk[0:2].copy().view(np.float16).astype(np.float64)[0]
                 sh = int(blk[2]) | (int(blk[3]) << 8)
@@ -220,3 +247,23 @@ def test_device_weights_are_centred(qt):
     W = make_weights_device(qt, nrows, K, seed=5, device="cpu").numpy()
     w = oracle.dequantize(qt, W, nrows, K).astype(np.float64)
     assert abs(w.mean()) < 0.02 * w.std(), (w.mean(), w.std())
+
+
+def test_iq_sign_table_is_even_parity():
+    """The sign bytes of the I-quants (gguf-py IQ2_XXS.ksigns): bit 7 makes the count of set
+    bits even, so 7 stored bits carry 8 signs."""
+    gguf = pytest.importorskip("gguf")
+    ks = np.frombuffer(gguf.quants.IQ2_XXS.ksigns, dtype=np.uint8)
+    want = [i | ((bin(i).count("1") & 1) << 7) for i in range(128)]
+    assert ks.tolist() == want
+
+
+def test_type_ids_match_ggml():
+    """Every ggml type id this build uses (kernels, smithy JSON keys) is gguf-py's."""
+    gguf = pytest.importorskip("gguf")
+    from kernel_anvil.codegen import GGML_TYPE_MAP
+
+    for name, info in QUANT_TYPES.items():
+        assert info.ggml_type == int(getattr(gguf.GGMLQuantizationType, name)), name
+        assert GGML_TYPE_MAP[name] == info.ggml_type, name
+        assert oracle.TYPE_IDS[name] == info.ggml_type, name
