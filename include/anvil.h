@@ -355,6 +355,13 @@ int anvil_pchain_take_status(void);
  * At most 60 s.  No counterpart in the reference (its kernels have no waits). */
 int anvil_set_wait_limit_ns(unsigned long long ns);
 unsigned long long anvil_get_wait_limit_ns(void);
+/* Tensor-core path of the batched GEMV: Q4_K and Q5_K launches with at least `min_cols`
+ * activation columns (2..8) and no explicit nwarps / rows_per_block run as mma.sync
+ * m16n8k32 int8 tiles of 16 rows (same block sums, y within fp32 rounding of the dp4a
+ * kernels).  0 turns it off; default 4 (at 2 and 3 columns the dp4a kernels are faster).
+ * Process-wide. */
+int anvil_set_tensor_core_min_cols(int min_cols);
+int anvil_get_tensor_core_min_cols(void);
 
 /* Device buffers shared between the ranks' processes (CUDA IPC): allocate (zeroed) and
  * export a 64-byte handle; open a peer's handle into this process; close; free. */

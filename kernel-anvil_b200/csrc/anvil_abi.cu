@@ -218,6 +218,7 @@ struct Plan {
     // memory, the launch runs `chunk` columns at a time (fn and the fields above are the
     // chunk's plan) and `tail` plans the last ncols % chunk columns.  chunk 0: one launch.
     int ncols, chunk, type;
+    bool cta_tiles = false;  // one tile per CTA (the tensor-core kernel), else one per warp
     std::shared_ptr<const Plan> tail;
 };
 
@@ -231,11 +232,70 @@ static int grid_for(const Plan &p, int share) {
 
 static int round_rpb(int r) { return r >= 8 ? 8 : r >= 4 ? 4 : r >= 2 ? 2 : 1; }
 
+// Tensor-core path (mmvq_mma.cu): Q4_K / Q5_K with 2..8 columns through mma.sync.
+MmvqKernelFn mmvq_mma_kernel_for(int qt, int ncols, int mode);
+int mmvq_mma_smem_bytes(int qt, int K, int ncols, int nwarps, int nstages);
+int mmvq_mma_max_warps();
+int mmvq_mma_take_status();
+constexpr int kMmaTileRows = 16;
+// Smallest column count that takes the tensor-core path (0: never).
+// 4: at 2 columns the MMA tiles compute 8 columns' work and the dp4a kernels are faster
+// (Q4_K 12288 x 4096: 13.4 against 8.2 us), from 4 on the MMA is (14.0 against 17.8 us).
+static std::atomic<int> g_mma_min_cols{4};
+
+static bool mma_eligible(int t, int ncols, int mode, int nwarps, int rpb) {
+    const int m = g_mma_min_cols.load(std::memory_order_relaxed);
+    return m > 0 && ncols >= m && ncols >= 2 && (t == kTypeQ4_K || t == kTypeQ5_K) &&
+           (mode == kModeQ81 || mode == kModeSums) && nwarps == 0 && rpb == 0;
+}
+
+// Plan of the tensor-core kernel: 16-row CTA tiles whose K-chunks the CTA's warps share;
+// warps per CTA up to 16 but no more than the K dimension's 256-weight super-blocks, the
+// most of them (halving) whose rings of 3, else 2, chunk stages fit beside the staged
+// activation.
+static int plan_mma(int t, int nrows, int K, int ncols, int mode, Plan *p) {
+    int nw = 0, ns = 0, smem = 0;
+    int wmax = mmvq_mma_max_warps();
+    while (wmax > 1 && wmax > K / 256) wmax >>= 1;
+    for (int w = wmax; w >= 1 && !nw; w >>= 1)
+        for (int st = 3; st >= 2 && !nw; --st) {
+            const int b = mmvq_mma_smem_bytes(t, K, ncols, w, st);
+            if (b <= kMaxSmem) {
+                nw = w;
+                ns = st;
+                smem = b;
+            }
+        }
+    if (!nw)
+        return fail(ANVIL_ERR_UNSUPPORTED, "ncols_x=%d ncols_dst=%d does not fit in shared memory "
+                                           "(tensor-core path)", K, ncols);
+    int dev, nsm;
+    if (int s = current_device(&dev)) return s;
+    if (int s = sm_count(dev, &nsm)) return s;
+    p->fn = mmvq_mma_kernel_for(t, ncols, mode);
+    if (!p->fn) return fail(ANVIL_ERR_UNSUPPORTED, "no tensor-core kernel for ncols=%d", ncols);
+    p->mode = mode;
+    p->nwarps = nw;
+    p->rpb = kMmaTileRows;
+    p->nstages = ns;
+    p->smem = smem;
+    int occ = 0;
+    if (int s = prepare_fn(reinterpret_cast<const void *>(p->fn), dev, nw * 32, smem, &occ)) return s;
+    const long ntiles = (long(nrows) + kMmaTileRows - 1) / kMmaTileRows;
+    p->ctas_needed = ntiles;  // one CTA per 16-row tile (persistent grid beyond the SMs)
+    p->cta_tiles = true;
+    p->occ = occ;
+    p->nsm = nsm;
+    p->grid = grid_for(*p, 1);
+    return ANVIL_OK;
+}
+
 static int plan_one(int t, int nrows, int K, int ncols, int nwarps, int rpb, int mode,
                     Plan *p) {
     p->ncols = ncols;
     p->chunk = 0;
     p->type = t;
+    p->cta_tiles = false;
     p->tail.reset();
     if (!supported_type(t)) return fail(ANVIL_ERR_UNSUPPORTED, "ggml type %d has no MMVQ kernel", t);
     if (nrows <= 0 || K <= 0) return fail(ANVIL_ERR_INVALID, "nrows=%d ncols_x=%d", nrows, K);
@@ -248,6 +308,7 @@ static int plan_one(int t, int nrows, int K, int ncols, int nwarps, int rpb, int
         return fail(ANVIL_ERR_INVALID, "the gate/up epilogue takes one column, got %d", ncols);
     if (nwarps < 0 || rpb < 0)
         return fail(ANVIL_ERR_INVALID, "nwarps=%d rows_per_block=%d", nwarps, rpb);
+    if (mma_eligible(t, ncols, mode, nwarps, rpb)) return plan_mma(t, nrows, K, ncols, mode, p);
     if (nwarps == 0 || rpb == 0) {
         int lnw = 0, lrpb = 0;
         if (anvil_smithy_lookup(t, nrows, K, &lnw, &lrpb) && lnw > 0 && lrpb > 0) {
@@ -372,7 +433,7 @@ static int launch_segs_one(const Plan &p, const Segs &sg, const void *x, int32_t
     a.segTile[kMaxSeg] = int(tiles);
     if (sg.n < kMaxSeg) a.segTile[sg.n] = int(tiles);
     Plan q = p;
-    q.ctas_needed = (tiles + p.nwarps - 1) / p.nwarps;
+    q.ctas_needed = p.cta_tiles ? tiles : (tiles + p.nwarps - 1) / p.nwarps;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid_for(q, share));
     cfg.blockDim = dim3(p.nwarps * 32);
@@ -443,7 +504,7 @@ static int launch_glu(const Plan &p, const void *Wg, const void *Wu, const void 
     a.segTile[0] = 0;
     for (int i = 1; i <= kMaxSeg; ++i) a.segTile[i] = int(tiles);
     Plan q = p;
-    q.ctas_needed = (tiles + p.nwarps - 1) / p.nwarps;
+    q.ctas_needed = p.cta_tiles ? tiles : (tiles + p.nwarps - 1) / p.nwarps;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid_for(q, share));
     cfg.blockDim = dim3(p.nwarps * 32);
@@ -555,6 +616,15 @@ int anvil_set_wait_limit_ns(unsigned long long ns) {
 }
 
 unsigned long long anvil_get_wait_limit_ns(void) { return wait_limit_ns(); }
+
+int anvil_set_tensor_core_min_cols(int min_cols) {
+    if (min_cols != 0 && (min_cols < 2 || min_cols > kMaxCols))
+        return fail(ANVIL_ERR_INVALID, "tensor-core column threshold %d: 0 or 2..%d", min_cols, kMaxCols);
+    g_mma_min_cols.store(min_cols, std::memory_order_relaxed);
+    return ANVIL_OK;
+}
+
+int anvil_get_tensor_core_min_cols(void) { return g_mma_min_cols.load(std::memory_order_relaxed); }
 
 const char *anvil_last_error(void) { return t_last_error.c_str(); }
 
@@ -776,7 +846,7 @@ int anvil_mmvq_block_sums(int ggml_type, const void *W, const void *xq, int32_t 
 // flags (0 = no bounded wait gave up) or a negative status.
 int anvil_take_device_status(void) {
     int v = 0;
-    int parts[20] = {take_quantize_status(), mmvq_kernel_q4k_take_status(),
+    int parts[21] = {take_quantize_status(), mmvq_mma_take_status(), mmvq_kernel_q4k_take_status(),
                     mmvq_kernel_q5k_take_status(), mmvq_kernel_q6k_take_status(),
                     mmvq_kernel_q80_take_status(), mmvq_kernel_q40_take_status(),
                     mmvq_kernel_q41_take_status(), mmvq_kernel_q50_take_status(),

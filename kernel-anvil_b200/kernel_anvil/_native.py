@@ -208,6 +208,8 @@ SIGNATURES = {
                                      c_int]),
     "anvil_pchain_set_group_dump": (c_int, [c_void_p, c_int, c_void_p]),
     "anvil_pchain_set_static_share": (c_int, [c_void_p, c_int]),
+    "anvil_set_tensor_core_min_cols": (c_int, [c_int]),
+    "anvil_get_tensor_core_min_cols": (c_int, []),
     "anvil_pchain_instantiate": (c_int, [c_void_p, c_int, c_int]),
     "anvil_pchain_set_trace": (c_int, [c_void_p, c_void_p]),
     "anvil_pchain_launch": (c_int, [c_void_p, c_void_p]),

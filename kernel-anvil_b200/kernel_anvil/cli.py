@@ -491,14 +491,18 @@ def cmd_chain_sweep(args) -> None:
 
 
 def cmd_bench_gemv(args) -> None:
+    from kernel_anvil import mmvq as ops
     from kernel_anvil.verify import bench_gemv
 
+    if args.tensor_cores == "off":
+        ops.set_tensor_core_min_cols(0)
     for n in _int_list(args.n):
         for k in _int_list(args.k):
             for pdl in ([False, True] if args.pdl == "both" else [args.pdl == "on"]):
                 res = bench_gemv(args.quant, n, k, ncols=args.ncols, nwarps=args.nwarps,
                                  rows_per_block=args.rpb, warmup=args.warmup, runs=args.runs,
                                  rotate_bytes=int(args.rotate_mb * 1e6), pdl=pdl)
+                res["tensor_cores"] = args.tensor_cores
                 print(json.dumps(res), flush=True)
 
 
@@ -595,6 +599,9 @@ def build_parser() -> argparse.ArgumentParser:
                    help="distinct weight copies cycled through (> L2 so each launch reads HBM)")
     p.add_argument("--pdl", choices=["off", "on", "both"], default="off",
                    help="launch with programmatic dependent launch (consecutive launches overlap)")
+    p.add_argument("--tensor-cores", choices=["on", "off"], default="on",
+                   help="Q4_K / Q5_K with 2-8 columns: the mma.sync kernel (on) or the dp4a "
+                        "kernels (off)")
     p.set_defaults(fn=cmd_bench_gemv)
     return parser
 

@@ -275,6 +275,32 @@ def kernel_attributes(qt, nrows: int, K: int, ncols: int = 1, nwarps: int = 0,
     return {"regs_per_thread": v[0].value, "local_bytes": v[1].value, "max_threads_per_block": v[2].value}
 
 
+def set_tensor_core_min_cols(min_cols: int) -> None:
+    """Q4_K / Q5_K launches with at least min_cols columns (2..8) and no explicit launch shape
+    use the mma.sync tensor-core kernel; 0 turns it off (every launch on the dp4a kernels)."""
+    check(_native.lib().anvil_set_tensor_core_min_cols(int(min_cols)))
+
+
+def tensor_core_min_cols() -> int:
+    return int(_native.lib().anvil_get_tensor_core_min_cols())
+
+
+class tensor_cores:
+    """Context manager: `with tensor_cores(0): ...` runs the block on the dp4a kernels."""
+
+    def __init__(self, min_cols: int):
+        self.min_cols = min_cols
+
+    def __enter__(self):
+        self.saved = tensor_core_min_cols()
+        set_tensor_core_min_cols(self.min_cols)
+        return self
+
+    def __exit__(self, *exc):
+        set_tensor_core_min_cols(self.saved)
+        return False
+
+
 def take_device_status() -> int:
     """OR of device status flags raised since the last call (1 = an mbarrier wait gave up)."""
     return check(_native.lib().anvil_take_device_status())

@@ -222,7 +222,7 @@ def test_argument_errors():
     with pytest.raises(AnvilError, match="CUDA tensor"):
         ops.mmvq(W.cpu(), "Q4_K", xq)
     with pytest.raises(ValueError, match="unsupported quant type"):
-        ops.mmvq(W, "IQ2_XXS", xq)
+        ops.mmvq(W, "Q8_K", xq)  # ggml's dot-product intermediate type: no MMVQ kernel
 
 
 def test_no_device_wait_gave_up():
@@ -280,3 +280,48 @@ def test_grouped_argument_errors():
         ops.mmvq_grouped_f32([W] * 5, "Q4_K", x)
     with pytest.raises(AnvilError, match="1..4"):
         ops.mmvq_grouped_f32([], "Q4_K", x)
+
+
+# ---- tensor-core path (mma.sync m16n8k32 int8): Q4_K / Q5_K, 2..8 columns --------------
+
+@pytest.mark.parametrize("qt", ["Q4_K", "Q5_K"])
+@pytest.mark.parametrize("nrows,K,ncols", [(1, 256, 2), (17, 1280, 3), (1000, 4096, 8),
+                                           (12288, 4096, 8), (300, 12288, 5), (64, 28672, 8),
+                                           (4096, 1024, 2), (33, 768, 7)])
+def test_tensor_core_path_matches_oracle(qt, nrows, K, ncols):
+    """Block sums from the MMA tiles bit-exact, y within the tolerance, and the dp4a kernel's
+    y within fp32 rounding of it; ragged tails (rows not a multiple of 16, K not a multiple
+    of the 1024-weight chunk) included."""
+    with ops.tensor_cores(2):
+        W, xq_ref, xq, y, sums = run_case(qt, nrows, K, ncols, seed=nrows + K)
+    np.testing.assert_array_equal(sums, oracle.block_sums(qt, W, xq_ref, nrows, K, ncols))
+    y_ref = oracle.mmvq(qt, W, xq_ref, nrows, K, ncols)
+    assert oracle.max_rel_err(y, y_ref) <= Y_TOL
+    with ops.tensor_cores(0):
+        _, _, _, y_dp4a, sums_dp4a = run_case(qt, nrows, K, ncols, seed=nrows + K)
+    np.testing.assert_array_equal(sums_dp4a, sums)
+    assert oracle.max_rel_err(y, y_dp4a) <= 1e-5
+
+
+def test_tensor_core_switch_and_grouped():
+    with pytest.raises(AnvilError):
+        ops.set_tensor_core_min_cols(1)
+    with pytest.raises(AnvilError):
+        ops.set_tensor_core_min_cols(9)
+    assert ops.tensor_core_min_cols() == 4
+    # a grouped launch (three matrices on one activation) through the same tiles
+    K, rows, ncols = 2048, [300, 17, 1024], 4
+    Ws = [make_weights("Q4_K", r, K, seed=80 + i) for i, r in enumerate(rows)]
+    x = make_activation(K, ncols=ncols, seed=90)
+    xq = ops.quantize_q8_1(dev(x))
+    ys = [torch.empty((ncols, r), dtype=torch.float32, device="cuda") for r in rows]
+    ch = ops.Chain()
+    ch.add_mmvq_grouped([dev(w) for w in Ws], "Q4_K", xq, ys, rows, K=K, ncols=ncols)
+    with torch.cuda.stream(torch.cuda.Stream()):
+        ch.instantiate()
+        ch.launch()
+    torch.cuda.synchronize()
+    xq_ref = oracle.quantize_q8_1(x)
+    for W, y, r in zip(Ws, ys, rows):
+        assert oracle.max_rel_err(y.cpu().numpy(), oracle.mmvq("Q4_K", W, xq_ref, r, K, ncols)) <= Y_TOL
+    ch.close()
