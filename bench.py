@@ -68,9 +68,11 @@ def parse_args():
                     help="quantise each GEMV input in its own kernel or inside the GEMV (fused)")
     ap.add_argument("--coresident", type=int, default=1,
                     help="graph executor: GEMV kernels sized to share each SM")
-    ap.add_argument("--executor", choices=["persistent", "graph"], default="persistent",
-                    help="one persistent kernel per token (the chain's data flow inside it), or a "
-                         "CUDA graph of quantize + MMVQ launches on fixed inputs")
+    ap.add_argument("--executor", choices=["auto", "persistent", "graph"], default="auto",
+                    help="one persistent kernel per token (the chain's data flow inside it), a CUDA "
+                         "graph of quantize + MMVQ launches on fixed inputs, or auto: the graph on one "
+                         "GPU (the faster single-GPU executor), the persistent kernel on several (its "
+                         "in-kernel exchange of the row-sharded outputs)")
     ap.add_argument("--fixed-inputs", action="store_true",
                     help="persistent executor: every group reads a fixed synthetic input instead of "
                          "its producer's output")
@@ -429,6 +431,28 @@ def extra_qwen3_8b(stream, steps: int, warmup: int) -> dict:
     return res
 
 
+def extra_persistent(spec, stream, steps: int, warmup: int) -> dict:
+    """The headline chain on this GPU through the persistent dataflow executor (the executor
+    of the row-sharded multi-GPU runs): its one-GPU time, for scaling comparisons."""
+    import torch
+
+    from kernel_anvil.chains import DeviceChain
+
+    dc = DeviceChain(spec, executor="persistent")
+    with torch.cuda.stream(stream):
+        dc.instantiate(pdl=True)
+        for _ in range(max(warmup, 3)):
+            dc.launch()
+        ms = time_graph(dc.launch, stream, steps)
+    nbytes = spec.glu_algorithmic_bytes()
+    res = {"us_per_token": round(ms * 1e3, 1), "gbs": round(nbytes / (ms * 1e-3) / 1e9, 1),
+           "launches_per_step": 1, "groups_per_step": dc.pchain.info()["groups"]}
+    dc.close()
+    del dc
+    torch.cuda.empty_cache()
+    return res
+
+
 def run_anvil(args) -> None:
     import torch
     import torch.distributed as dist
@@ -452,6 +476,8 @@ def run_anvil(args) -> None:
     if args.gemvs:
         spec = spec.head(args.gemvs)
     shard = args.multi == "rows"
+    if args.executor == "auto":
+        args.executor = "graph" if world == 1 or not shard else "persistent"
     persistent = args.executor == "persistent"
     # replicas: every rank runs the whole chain on its own inputs (seeded per rank)
     dc = DeviceChain(spec, rank=rank if shard else 0, world=world if shard else 1, device=dev,
@@ -607,6 +633,9 @@ def run_anvil(args) -> None:
     if world == 1 and not args.no_extras:
         extras["config0_single_gemv"] = extra_config0(hbm_peak)
         extras["config1_qwen3_8b_chain"] = extra_qwen3_8b(stream, args.steps, args.warmup)
+        if not persistent:
+            extras["persistent_dataflow_same_chain"] = extra_persistent(spec, stream, args.steps,
+                                                                        args.warmup)
         status |= ops.take_device_status() | take_status()
 
     if world > 1:
