@@ -139,10 +139,15 @@ def test_long_rows_many_columns_in_chunks(qt, ncols):
     check_case(qt, 300, K, ncols, seed=ncols)
     W = dev(make_weights(qt, 64, K, seed=1))
     x = dev(make_activation(K, ncols=ncols, seed=2))
-    y1 = ops.mmvq(W, qt, ops.quantize_q8_1(x), ncols=ncols)
+    with ops.tensor_cores(0):  # the same dp4a kernel on both paths: the same bits
+        y1 = ops.mmvq(W, qt, ops.quantize_q8_1(x), ncols=ncols)
     y2 = ops.mmvq_f32(W, qt, x)
     torch.cuda.synchronize()
     assert torch.equal(y1, y2)
+    # Q4_K at 4+ columns takes the tensor-core kernel by default: other summation order
+    y3 = ops.mmvq(W, qt, ops.quantize_q8_1(x), ncols=ncols)
+    torch.cuda.synchronize()
+    assert oracle.max_rel_err(y3.cpu().numpy(), y2.cpu().numpy()) <= 1e-5
 
 
 def test_pdl_launch_same_result():

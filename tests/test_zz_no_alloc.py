@@ -12,10 +12,19 @@ from kernel_anvil.quants import make_activation, make_weights, resolve_type  # n
 
 pytestmark = pytest.mark.gpu
 
-# The two entry points quantise x identically and run the same GEMV kernel, so the
-# outputs agree to fp32 rounding; this is the tolerance the comparison allows.
-RTOL, ATOL = 1e-6, 1e-6
+# Both entry points quantise x identically.  anvil_mmvq_f32 then runs the dp4a kernel with the
+# quantiser fused in; the no-alloc entry point quantises into its static buffer and runs the
+# Q8_1 kernel, which for Q4_K / Q5_K from 4 columns on is the tensor-core kernel: the same
+# block sums, added up in another order.  So the outputs agree to float rounding: the largest
+# difference may be 1e-5 of the largest output (the bar of the tests comparing two kernels).
+REL = 1e-5
 STATIC_XQ_BYTES = 1 << 20
+
+
+def _assert_close(a, b):
+    diff = float((a - b).abs().max())
+    scale = float(b.abs().max()) or 1.0
+    assert diff <= REL * scale, f"max |a - b| = {diff:.3e} against max |b| = {scale:.3e}"
 
 
 def _stream():
@@ -58,12 +67,12 @@ def test_noalloc_matches_caller_scratch_two_calls(qt, nrows, K, ncols):
     ra = _reference(qt, W, xa, nrows, K, ncols)
     rb = _reference(qt, W, xb, nrows, K, ncols)
     torch.cuda.synchronize()
-    torch.testing.assert_close(ya, ra, rtol=RTOL, atol=ATOL)
-    torch.testing.assert_close(yb, rb, rtol=RTOL, atol=ATOL)
+    _assert_close(ya, ra)
+    _assert_close(yb, rb)
     # the same input again, into the same output buffer: same result
     _noalloc(qt, W, xa, nrows, K, ncols, y=yb)
     torch.cuda.synchronize()
-    torch.testing.assert_close(yb, ra, rtol=RTOL, atol=ATOL)
+    _assert_close(yb, ra)
 
 
 def test_noalloc_rejects_oversize_activation():
