@@ -63,7 +63,8 @@ __host__ __device__ inline MmaSmem mma_smem_layout(int qt, int K, int ncols, int
 
 __device__ __forceinline__ void mma_s8_16x8x32(uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                                uint32_t b0, uint32_t b1, int (&d)[4]) {
-    asm volatile(
+    // not volatile: the instruction has no side effects, so the compiler may schedule it early
+    asm(
         "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
         "{%8, %9}, {%10, %10, %10, %10};"
         : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
@@ -209,6 +210,10 @@ __global__ void __launch_bounds__(kMmaMaxWarps * 32, 1) mmvq_mma_kernel(const __
                     scale_min_pair<U>(h0, sc0[0], sc1[0], m0[0], m1[0]);
                     scale_min_pair<U>(h1, sc0[1], sc1[1], m0[1], m1[1]);
 #pragma unroll
+                    // both MMAs of the unit first, then their epilogues: the second MMA
+                    // runs while the first one's results are still on their way
+                    int d[2][4];
+#pragma unroll
                     for (int j = 0; j < 2; ++j) {  // sub-block 2U + j
                         const int kb = 8 * b + 2 * U + j;
                         uint32_t b0 = 0, b1 = 0;
@@ -217,9 +222,12 @@ __global__ void __launch_bounds__(kMmaMaxWarps * 32, 1) mmvq_mma_kernel(const __
                             b0 = bw.x;
                             b1 = bw.y;
                         }
-                        int d[4];
-                        if (j == 0) mma_s8_16x8x32(lo0, lo1, lo2, lo3, b0, b1, d);
-                        else mma_s8_16x8x32(hi0, hi1, hi2, hi3, b0, b1, d);
+                        if (j == 0) mma_s8_16x8x32(lo0, lo1, lo2, lo3, b0, b1, d[0]);
+                        else mma_s8_16x8x32(hi0, hi1, hi2, hi3, b0, b1, d[1]);
+                    }
+#pragma unroll
+                    for (int j = 0; j < 2; ++j) {
+                        const int kb = 8 * b + 2 * U + j;
                         float2 d8 = make_float2(0.f, 0.f), ds = make_float2(0.f, 0.f);
                         if (tlive) {
                             d8 = *reinterpret_cast<const float2 *>(sd8 + kb * NCP + 2 * t);
@@ -227,10 +235,10 @@ __global__ void __launch_bounds__(kMmaMaxWarps * 32, 1) mmvq_mma_kernel(const __
                         }
                         const int s0 = j == 0 ? sc0[0] : sc1[0], s1 = j == 0 ? sc0[1] : sc1[1];
                         const float q0 = float(j == 0 ? m0[0] : m1[0]), q1 = float(j == 0 ? m0[1] : m1[1]);
-                        fd[0][0] += d8.x * float(d[0] * s0);
-                        fd[0][1] += d8.y * float(d[1] * s0);
-                        fd[1][0] += d8.x * float(d[2] * s1);
-                        fd[1][1] += d8.y * float(d[3] * s1);
+                        fd[0][0] += d8.x * float(d[j][0] * s0);
+                        fd[0][1] += d8.y * float(d[j][1] * s0);
+                        fd[1][0] += d8.x * float(d[j][2] * s1);
+                        fd[1][1] += d8.y * float(d[j][3] * s1);
                         fm[0][0] += ds.x * q0;
                         fm[0][1] += ds.y * q0;
                         fm[1][0] += ds.x * q1;
@@ -240,12 +248,12 @@ __global__ void __launch_bounds__(kMmaMaxWarps * 32, 1) mmvq_mma_kernel(const __
                             const int c0 = 2 * t, c1 = 2 * t + 1;
                             int32_t *out = args.sums;
                             if (g < rows) {
-                                if (c0 < NC) out[(size_t(c0) * nrows + r0 + g) * nsub + kb] = d[0];
-                                if (c1 < NC) out[(size_t(c1) * nrows + r0 + g) * nsub + kb] = d[1];
+                                if (c0 < NC) out[(size_t(c0) * nrows + r0 + g) * nsub + kb] = d[j][0];
+                                if (c1 < NC) out[(size_t(c1) * nrows + r0 + g) * nsub + kb] = d[j][1];
                             }
                             if (g + 8 < rows) {
-                                if (c0 < NC) out[(size_t(c0) * nrows + r0 + g + 8) * nsub + kb] = d[2];
-                                if (c1 < NC) out[(size_t(c1) * nrows + r0 + g + 8) * nsub + kb] = d[3];
+                                if (c0 < NC) out[(size_t(c0) * nrows + r0 + g + 8) * nsub + kb] = d[j][2];
+                                if (c1 < NC) out[(size_t(c1) * nrows + r0 + g + 8) * nsub + kb] = d[j][3];
                             }
                         }
                     }
