@@ -92,6 +92,11 @@ def parse_args():
                          "scaling)")
     ap.add_argument("--nwarps", type=int, default=0, help="persistent executor: warps per CTA (0 = 8)")
     ap.add_argument("--ctas-per-sm", type=int, default=0, help="persistent executor: CTAs per SM (0 = 1)")
+    ap.add_argument("--smithy", default="auto",
+                    help="launch-shape table for the MMVQ launches: auto (the table tuned on a B200 for "
+                         "the workload, kernel_anvil/tuned/<workload>_b200.json, when there is one), "
+                         "none (the built-in shapes), or a smithy JSON path; loaded through the same "
+                         "loader llama.cpp's lookup uses")
     ap.add_argument("--ncols", type=int, default=1,
                     help="activation columns per step (speculative-decode verification batch; the "
                          "persistent executor takes 1 or 2, the graph executor 1..8)")
@@ -431,6 +436,28 @@ def extra_qwen3_8b(stream, steps: int, warmup: int) -> dict:
     return res
 
 
+def load_launch_table(choice: str, workload: str) -> str | None:
+    """Load the smithy table that sets the MMVQ launch shapes (anvil_smithy_load, the loader
+    behind llama.cpp's lookup): the B200-tuned table of the workload for "auto", none for
+    "none", else the given file.  Returns the file's name, or None when no table is active."""
+    from kernel_anvil import _native
+
+    lib = _native.lib()
+    lib.anvil_smithy_reset()
+    if choice == "none":
+        return None
+    path = (ROOT / "kernel-anvil_b200" / "kernel_anvil" / "tuned" / f"{workload}_b200.json"
+            if choice == "auto" else Path(choice))
+    if not path.exists():
+        if choice != "auto":
+            raise SystemExit(f"--smithy {choice}: no such file")
+        return None
+    n = lib.anvil_smithy_load(str(path).encode())
+    if n <= 0:
+        raise SystemExit(f"--smithy: {path} holds no usable cell ({n})")
+    return f"{path.name} ({n} cells)"
+
+
 def extra_persistent(spec, stream, steps: int, warmup: int) -> dict:
     """The headline chain on this GPU through the persistent dataflow executor (the executor
     of the row-sharded multi-GPU runs): its one-GPU time, for scaling comparisons."""
@@ -475,6 +502,7 @@ def run_anvil(args) -> None:
     spec = get_chain(args.workload)
     if args.gemvs:
         spec = spec.head(args.gemvs)
+    smithy = load_launch_table(args.smithy, args.workload)
     shard = args.multi == "rows"
     if args.executor == "auto":
         args.executor = "graph" if world == 1 or not shard else "persistent"
@@ -659,6 +687,7 @@ def run_anvil(args) -> None:
         "dtype": "int8 dp4a / fp32", "data": "synthetic",
         "config": {"workload": f"{args.workload} per-token GEMV chain",
                    "gemvs_per_step": len(spec.gemvs), "ncols": args.ncols,
+                   "launch_table": smithy or "built-in launch shapes",
                    "groups_per_step": n_groups if persistent else None,
                    "quantizations_per_step": n_groups if persistent else n_quantize,
                    "bytes_per_step": total_bytes, "weight_bytes": spec.weight_bytes(),

@@ -8,6 +8,7 @@ patches/smithy-config.h:268-317 and is exercised with HOME and env vars sandboxe
 """
 import ctypes
 import json
+from pathlib import Path
 import random
 import threading
 
@@ -194,12 +195,21 @@ def test_concurrent_lookups_and_resets(sandbox_home, tmp_path, monkeypatch):
     assert not bad
 
 
+TUNED = Path(__file__).resolve().parent.parent / "kernel-anvil_b200" / "kernel_anvil" / "tuned"
+
+
 @pytest.mark.parametrize("name,types", [("smithy_qwen3_8b_plus_draft.json", {8, 12, 14}),
-                                        ("smithy_qwen35_27b.json", {12, 13})])
+                                        ("smithy_qwen35_27b.json", {12, 13}),
+                                        ("tuned:llama3_70b_b200.json", {12})])
 def test_recorded_tuner_outputs_load_like_the_reference(golden_dir, tmp_path, name, types):
     """Configs the tuner wrote on a B200 (gguf-optimize with a draft model; autoforge on the
-    Qwen3.5-27B shapes) load with the same cells in this loader and in the reference's."""
-    doc = (golden_dir / name).read_text()
+    Qwen3.5-27B and Llama-3-70B shapes, the latter shipped for the bench) load with the same
+    cells in this loader and in the reference's."""
+    if name.startswith("tuned:"):
+        name = name[len("tuned:"):]
+        doc = (TUNED / name).read_text()
+    else:
+        doc = (golden_dir / name).read_text()
     n, cells = anvil_load_doc(tmp_path, doc, name)
     assert n > 0 and {c[0] for c in cells} == types
     ref = oracle.ref_smithy()
